@@ -1,0 +1,124 @@
+/*
+ * lfm2q — B200-native (sm_100a) INT8 matrix-multiply hot path of LFM2.5-VL-Optimization, C ABI.
+ *
+ * Plain pointers and sizes only: device pointers for all tensors, a cudaStream_t passed as `void *`
+ * (NULL = the legacy default stream). Every entry point validates its arguments on the host, enqueues
+ * the work on `stream` without synchronising, and returns an lfm2q_status; lfm2q_last_error() gives the
+ * message of the last failure on the calling thread. Callers allocate every output. No entry point
+ * allocates device memory.
+ *
+ * Element types: "bf16" tensors are uint16_t bit patterns of bfloat16; int8 tensors are int8_t; scales fp32.
+ * Layouts are row-major and dense. Every pointer must be 16-byte aligned.
+ *
+ * Each declaration names the reference interface it replaces (path:line in the reference project).
+ */
+#ifndef LFM2Q_H
+#define LFM2Q_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  LFM2Q_OK = 0,
+  LFM2Q_EINVAL = -22,   /* bad shape, size, alignment or null pointer; nothing was launched */
+  LFM2Q_ENOTSUP = -95,  /* no sm_100 device current, or the driver lacks the tensor-map entry point */
+  LFM2Q_ECUDA = -5,     /* the CUDA runtime reported an error while launching */
+  LFM2Q_ETIMEOUT = -62  /* a kernel's bounded pipeline wait gave up (see lfm2q_check_device) */
+} lfm2q_status;
+
+/* Message of the last non-OK status returned on this thread ("" if none). */
+const char *lfm2q_last_error(void);
+
+/* Library version string. */
+const char *lfm2q_version(void);
+
+/* 1 if the current device is an sm_100 part this library can launch on, else 0. */
+int lfm2q_device_supported(void);
+
+/* Reads (and with clear != 0 resets) the sticky device error word the GEMM kernels set when a bounded wait
+ * expires. Returns LFM2Q_OK or LFM2Q_ETIMEOUT. Synchronous (copies one int from the device). */
+int lfm2q_check_device(int clear);
+
+/* ------------------------------------------------------------------ activation quantizers
+ * Replaces launch_quant_rows / launch_quant_groups (kernels/int8_gemm.cu:822-825, :782-785) behind the
+ * quant_rows binding (kernels/int8_gemm.cpp:83-96).
+ * x bf16 [rows, K] -> q int8 [rows, K], s fp32 [rows] = max(|x_row|, 1e-8) / 127, q = clamp(rint(x / s), +-127).
+ * Needs K % 8 == 0 and K <= 16384 (the reference needs K % 128 == 0 and K <= 2048). */
+int lfm2q_quant_rows(const uint16_t *x, int8_t *q, float *s, int rows, int K, void *stream);
+/* Grouped: sT fp32 [K/64, rows], one scale per row and 64-wide group. Needs K % 64 == 0, K <= 16384. */
+int lfm2q_quant_groups(const uint16_t *x, int8_t *q, float *sT, int rows, int K, void *stream);
+
+/* ------------------------------------------------------------------ W8A8 GEMM (tcgen05)
+ * Replaces launch_gemm_i8 (kernels/int8_gemm.cu:741-748) behind gemm_i8 (kernels/int8_gemm.cpp:39-50).
+ * y bf16 [M, N] = bf16(act(((float)(xq . w^T)[m, n] * sx[m]) * sw[n] + bias[n])), act = GELU(tanh) if gelu.
+ * xq int8 [M, K], w int8 [N, K], sw fp32 [N], bias bf16 [N] or NULL.
+ * grouped == 0: sx fp32 [M] (one scale per token).
+ * grouped != 0: sx fp32 [K/64, M]; the int32 sum of every 64-wide K group is folded into fp32 with its scale.
+ * Needs K % 16 == 0, N % 8 == 0 (grouped: K % 64 == 0). */
+int lfm2q_gemm_i8(const int8_t *xq, const float *sx, int grouped, const int8_t *w, const float *sw,
+                  const uint16_t *bias, uint16_t *y, int M, int N, int K, int gelu, void *stream);
+
+/* Replaces launch_gemm_i8_q (kernels/int8_gemm.cu:751-763) behind gemm_i8_q (kernels/int8_gemm.cpp:53-69).
+ * Grouped W8A8 whose bf16-rounded output is requantized for the next W8A8 GEMM: yq int8 [M, N],
+ * ysT fp32 [N/64, M]. sxT fp32 [K/64, M]. Needs K % 64 == 0, N % 128 == 0. */
+int lfm2q_gemm_i8_q(const int8_t *xq, const float *sxT, const int8_t *w, const float *sw, const uint16_t *bias,
+                    int8_t *yq, float *ysT, int M, int N, int K, int gelu, void *stream);
+
+/* New fused epilogue with no single-kernel counterpart in the reference: it replaces the composition
+ * gemm_i8 (kernels/int8_gemm.cpp:39-50, bf16 out) -> silu_mul (kernels/lfm2_decode.cu:954-969).
+ * w = [w1 | w3] int8 [2I, K] with sw fp32 [2I], bias bf16 [2I] or NULL, per-token sx fp32 [M];
+ * y bf16 [M, I] = bf16(bf16(silu(g)) * u), g and u the bf16 per-token epilogue outputs of rows n and I + n.
+ * Needs K % 16 == 0, I % 8 == 0. */
+int lfm2q_gemm_i8_silu(const int8_t *xq, const float *sx, const int8_t *w, const float *sw, const uint16_t *bias,
+                       uint16_t *y, int M, int I, int K, void *stream);
+
+/* Replaces launch_gemm_w8 (kernels/int8_gemm.cu:765-780) behind gemm_w8 (kernels/int8_gemm.cpp:72-79).
+ * W8A16: y bf16 [M, N] = bf16(act((x . w^T) * sw[n] + bias[n])), x bf16 [M, K], w int8 [N, K].
+ * Needs K % 16 == 0, N % 8 == 0. */
+int lfm2q_gemm_w8(const uint16_t *x, const int8_t *w, const float *sw, const uint16_t *bias, uint16_t *y, int M,
+                  int N, int K, int gelu, void *stream);
+
+/* ------------------------------------------------------------------ fused producers
+ * Replace launch_add_layernorm_q / launch_add_rmsnorm_q / launch_silu_mul_q (kernels/int8_gemm.cu:787-820) behind
+ * the bindings of the same names (kernels/int8_gemm.cpp:107-141). grouped != 0 selects s [K/64, rows].
+ * h is updated in place (h += y) when y is non-NULL. */
+int lfm2q_add_layernorm_q(uint16_t *h, const uint16_t *y, const uint16_t *w, const uint16_t *b, int8_t *q, float *s,
+                          int rows, int D, float eps, int grouped, void *stream);
+int lfm2q_add_rmsnorm_q(uint16_t *h, const uint16_t *y, const uint16_t *w, int8_t *q, float *s, int rows, int H,
+                        float eps, int grouped, void *stream);
+/* g bf16 [rows, 2I] -> q int8 [rows, I] + scales of bf16(bf16(silu(g[:, :I])) * g[:, I:]). */
+int lfm2q_silu_mul_q(const uint16_t *g, int8_t *q, float *s, int rows, int I, int grouped, void *stream);
+
+/* ------------------------------------------------------------------ decode GEMV
+ * Replaces launch_gemv (kernels/lfm2_decode.cu:708-714) behind gemv (kernels/lfm2_decode.cpp:73-85).
+ * y bf16 [B, N] = bf16((x . W^T) * scale[n]), fp32 accumulation. w_is_int8 != 0: W int8 [N, K] with scale fp32
+ * [N] (required); else W bf16 [N, K] and scale optional (NULL = 1). x bf16 [B, K]. Needs K % 512 == 0 (int8) or
+ * K % 256 == 0 (bf16). `rows` is a tuning knob (0 = automatic; 1, 2, 4 or 8 = K-slices per 16-row group);
+ * results do not depend on it. */
+int lfm2q_gemv(const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int N, int K,
+               int rows, int B, void *stream);
+
+/* Replaces launch_gemv_epi (kernels/lfm2_decode.cu:818-827) behind gemv_epi (kernels/lfm2_decode.cpp:130-150).
+ * Batch 1. epi 0: W = w1|w3 [2S, K] -> y [S] = bf16(bf16(silu(g)) * u).
+ *          epi 1: W = in_proj [3S, K] (B|C|x) -> short-conv step, state bf16 [S, 3] updated in place,
+ *                 cw bf16 [S, 3], cbias bf16 [S] or NULL. */
+int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int S,
+                   int K, uint16_t *state, const uint16_t *cw, const uint16_t *cbias, void *stream);
+
+/* Replace set_pdl / set_gemv_impl (kernels/lfm2_decode.cpp:165-166). set_pdl toggles Programmatic Dependent
+ * Launch for the GEMV kernels (default on). set_gemv_impl is accepted for compatibility; this build has one
+ * GEMV implementation. */
+void lfm2q_set_pdl(int on);
+void lfm2q_set_gemv_impl(int impl);
+
+/* Forces the per-token GEMM tile width (128 or 256; 0 = automatic). Tuning and testing only. */
+void lfm2q_set_gemm_tile(int bn);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LFM2Q_H */

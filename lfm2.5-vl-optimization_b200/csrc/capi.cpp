@@ -1,0 +1,250 @@
+// C ABI of liblfm2q (include/lfm2q.h): host-side argument checks, device check, dispatch to the launchers.
+//
+// The checks restate the reference bindings' TORCH_CHECKs (kernels/int8_gemm.cpp:20-141,
+// kernels/lfm2_decode.cpp:73-150) with the limits of this build, and run before anything touches the device,
+// so a bad call returns LFM2Q_EINVAL (and a message) on any machine, with or without a GPU.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/lfm2q.h"
+#include "launch.h"
+
+namespace lfm2q {
+
+static thread_local std::string g_last_error;
+static std::atomic<bool> g_pdl{true};
+
+static int fail(int code, const std::string &msg) {
+  g_last_error = msg;
+  return code;
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DevInfo {
+  int sms = 0;
+  int supported = -1;  // -1 unknown
+};
+static DevInfo g_dev[64];
+static std::mutex g_dev_mu;
+
+static DevInfo &dev_info() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    static DevInfo none;
+    none.supported = 0;
+    return none;
+  }
+  DevInfo &d = g_dev[dev & 63];
+  if (d.supported < 0) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (d.supported < 0) {
+      int major = 0, minor = 0, sms = 0;
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      d.sms = sms;
+      d.supported = (major == 10 && minor == 0) ? 1 : 0;
+    }
+  }
+  return d;
+}
+
+int device_sm_count() {
+  const int s = dev_info().sms;
+  return s > 0 ? s : 148;
+}
+bool device_is_sm100() { return dev_info().supported == 1; }
+
+static int device_gate() {
+  if (!device_is_sm100())
+    return fail(LFM2Q_ENOTSUP, "lfm2q: the current CUDA device is not an sm_100 (B200) GPU, or no device is visible");
+  return LFM2Q_OK;
+}
+
+static int launched(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return LFM2Q_OK;
+  return fail(LFM2Q_ECUDA, std::string("lfm2q: ") + what + ": " + cudaGetErrorString(e));
+}
+
+#define REQUIRE(cond, msg) \
+  do {                     \
+    if (!(cond)) return fail(LFM2Q_EINVAL, std::string("lfm2q: ") + (msg)); \
+  } while (0)
+
+}  // namespace lfm2q
+
+using namespace lfm2q;
+
+extern "C" {
+
+const char *lfm2q_last_error(void) { return g_last_error.c_str(); }
+
+const char *lfm2q_version(void) { return "lfm2q 0.1.0 (sm_100a)"; }
+
+int lfm2q_device_supported(void) { return device_is_sm100() ? 1 : 0; }
+
+int lfm2q_check_device(int clear) {
+  if (int e = device_gate()) return e;
+  const int v = gemm_device_error(clear != 0);
+  if (v) return fail(LFM2Q_ETIMEOUT, "lfm2q: a GEMM pipeline wait timed out on the device");
+  return LFM2Q_OK;
+}
+
+void lfm2q_set_pdl(int on) { g_pdl.store(on != 0); }
+void lfm2q_set_gemv_impl(int) {}
+void lfm2q_set_gemm_tile(int bn) { gemm_set_tile_override(bn); }
+
+// ------------------------------------------------------------------ quantizers
+int lfm2q_quant_rows(const uint16_t *x, int8_t *q, float *s, int rows, int K, void *stream) {
+  REQUIRE(rows >= 0 && K > 0, "rows must be >= 0 and K > 0");
+  REQUIRE(K % 8 == 0 && K <= 16384, "K must be a multiple of 8, <= 16384");
+  REQUIRE(rows == 0 || (x && q && s), "x, q and s must be non-null");
+  REQUIRE(aligned16(x) && aligned16(q), "x and q must be 16-byte aligned");
+  if (rows == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_quant_rows(x, q, s, rows, K, (cudaStream_t)stream), "quant_rows");
+}
+
+int lfm2q_quant_groups(const uint16_t *x, int8_t *q, float *sT, int rows, int K, void *stream) {
+  REQUIRE(rows >= 0 && K > 0, "rows must be >= 0 and K > 0");
+  REQUIRE(K % 64 == 0 && K <= 16384, "grouped shapes: K must be a multiple of 64, <= 16384");
+  REQUIRE(rows == 0 || (x && q && sT), "x, q and s must be non-null");
+  REQUIRE(aligned16(x) && aligned16(q), "x and q must be 16-byte aligned");
+  if (rows == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_quant_groups(x, q, sT, rows, K, (cudaStream_t)stream), "quant_groups");
+}
+
+// ------------------------------------------------------------------ GEMMs
+static int check_gemm_common(const void *w, const float *sw, const uint16_t *bias, const void *y, int M, int N,
+                             int K) {
+  REQUIRE(M >= 0 && N > 0 && K > 0, "need M >= 0, N > 0, K > 0");
+  REQUIRE(K % 16 == 0 && N % 8 == 0, "need K % 16 == 0 and N % 8 == 0");
+  REQUIRE(w && sw && y, "w, sw and y must be non-null");
+  REQUIRE(aligned16(w) && aligned16(sw) && aligned16(y) && aligned16(bias), "w, sw, bias and y must be 16-byte aligned");
+  return LFM2Q_OK;
+}
+
+int lfm2q_gemm_i8(const int8_t *xq, const float *sx, int grouped, const int8_t *w, const float *sw,
+                  const uint16_t *bias, uint16_t *y, int M, int N, int K, int gelu, void *stream) {
+  if (int e = check_gemm_common(w, sw, bias, y, M, N, K)) return e;
+  REQUIRE(M == 0 || (xq && sx), "xq and sx must be non-null");
+  REQUIRE(aligned16(xq), "xq must be 16-byte aligned");
+  if (grouped) REQUIRE(K % 64 == 0, "sx shape: grouped scales need K % 64 == 0");
+  if (M == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_gemm_i8(xq, sx, w, sw, bias, y, M, N, K, gelu != 0, grouped != 0, (cudaStream_t)stream),
+                  "gemm_i8");
+}
+
+int lfm2q_gemm_i8_q(const int8_t *xq, const float *sxT, const int8_t *w, const float *sw, const uint16_t *bias,
+                    int8_t *yq, float *ysT, int M, int N, int K, int gelu, void *stream) {
+  REQUIRE(M >= 0 && N > 0 && K > 0, "need M >= 0, N > 0, K > 0");
+  REQUIRE(K % 64 == 0, "sxT shape: K must be a multiple of 64");
+  REQUIRE(N % 128 == 0, "w [N, K] with N % 128 == 0");
+  REQUIRE(w && sw && yq && ysT && (M == 0 || (xq && sxT)), "pointers must be non-null");
+  REQUIRE(aligned16(xq) && aligned16(w) && aligned16(sw) && aligned16(bias) && aligned16(yq),
+          "xq, w, sw, bias and yq must be 16-byte aligned");
+  if (M == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_gemm_i8_q(xq, sxT, w, sw, bias, yq, ysT, M, N, K, gelu != 0, (cudaStream_t)stream),
+                  "gemm_i8_q");
+}
+
+int lfm2q_gemm_i8_silu(const int8_t *xq, const float *sx, const int8_t *w, const float *sw, const uint16_t *bias,
+                       uint16_t *y, int M, int I, int K, void *stream) {
+  REQUIRE(M >= 0 && I > 0 && K > 0, "need M >= 0, I > 0, K > 0");
+  REQUIRE(K % 16 == 0 && I % 8 == 0, "need K % 16 == 0 and I % 8 == 0");
+  REQUIRE(w && sw && y && (M == 0 || (xq && sx)), "pointers must be non-null");
+  REQUIRE(aligned16(xq) && aligned16(w) && aligned16(sw) && aligned16(bias) && aligned16(y),
+          "xq, w, sw, bias and y must be 16-byte aligned");
+  REQUIRE(aligned16(sw + I) && aligned16(bias ? bias + I : nullptr), "I must keep the up-half scales 16-byte aligned");
+  if (M == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_gemm_i8_silu(xq, sx, w, sw, bias, y, M, I, K, (cudaStream_t)stream), "gemm_i8_silu");
+}
+
+int lfm2q_gemm_w8(const uint16_t *x, const int8_t *w, const float *sw, const uint16_t *bias, uint16_t *y, int M,
+                  int N, int K, int gelu, void *stream) {
+  if (int e = check_gemm_common(w, sw, bias, y, M, N, K)) return e;
+  REQUIRE(M == 0 || x, "x must be non-null");
+  REQUIRE(aligned16(x), "x must be 16-byte aligned");
+  if (M == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_gemm_w8(x, w, sw, bias, y, M, N, K, gelu != 0, (cudaStream_t)stream), "gemm_w8");
+}
+
+// ------------------------------------------------------------------ producers
+int lfm2q_add_layernorm_q(uint16_t *h, const uint16_t *y, const uint16_t *w, const uint16_t *b, int8_t *q, float *s,
+                          int rows, int D, float eps, int grouped, void *stream) {
+  REQUIRE(rows >= 0 && D > 0, "rows must be >= 0 and D > 0");
+  REQUIRE(D % 8 == 0 && D <= 16384, "D must be a multiple of 8, <= 16384");
+  if (grouped) REQUIRE(D % 64 == 0, "s shape: grouped scales need D % 64 == 0");
+  REQUIRE(h && w && b && q && s, "h, w, b, q and s must be non-null");
+  REQUIRE(aligned16(h) && aligned16(y), "h and y must be 16-byte aligned");
+  if (rows == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_add_layernorm_q(h, y, w, b, q, s, rows, D, eps, grouped != 0, (cudaStream_t)stream),
+                  "add_layernorm_q");
+}
+
+int lfm2q_add_rmsnorm_q(uint16_t *h, const uint16_t *y, const uint16_t *w, int8_t *q, float *s, int rows, int H,
+                        float eps, int grouped, void *stream) {
+  REQUIRE(rows >= 0 && H > 0, "rows must be >= 0 and H > 0");
+  REQUIRE(H % 8 == 0 && H <= 16384, "w shape: H must be a multiple of 8, <= 16384");
+  if (grouped) REQUIRE(H % 64 == 0, "s shape: grouped scales need H % 64 == 0");
+  REQUIRE(h && w && q && s, "h, w, q and s must be non-null");
+  REQUIRE(aligned16(h) && aligned16(y), "h and y must be 16-byte aligned");
+  if (rows == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_add_rmsnorm_q(h, y, w, q, s, rows, H, eps, grouped != 0, (cudaStream_t)stream),
+                  "add_rmsnorm_q");
+}
+
+int lfm2q_silu_mul_q(const uint16_t *g, int8_t *q, float *s, int rows, int I, int grouped, void *stream) {
+  REQUIRE(rows >= 0 && I > 0, "rows must be >= 0 and I > 0");
+  REQUIRE(I % 8 == 0 && I <= 16384, "I shape: I must be a multiple of 8, <= 16384");
+  if (grouped) REQUIRE(I % 64 == 0, "s shape: grouped scales need I % 64 == 0");
+  REQUIRE(g && q && s, "g, q and s must be non-null");
+  REQUIRE(aligned16(g), "g must be 16-byte aligned");
+  if (rows == 0) return LFM2Q_OK;
+  if (int e = device_gate()) return e;
+  return launched(launch_silu_mul_q(g, q, s, rows, I, grouped != 0, (cudaStream_t)stream), "silu_mul_q");
+}
+
+// ------------------------------------------------------------------ GEMV
+int lfm2q_gemv(const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int N, int K,
+               int rows, int B, void *stream) {
+  REQUIRE(N > 0 && K > 0 && B >= 1, "x [B, K], y [B, N]: need N > 0, K > 0, B >= 1");
+  REQUIRE(K % (w_is_int8 ? 512 : 256) == 0, "K must be a multiple of 256 (bf16) / 512 (int8)");
+  REQUIRE(W && x && y, "W, x and y must be non-null");
+  REQUIRE(!w_is_int8 || scale, "int8 W needs fp32 scale");
+  REQUIRE(aligned16(W) && aligned16(x), "W and x must be 16-byte aligned");
+  if (int e = device_gate()) return e;
+  return launched(launch_gemv(W, w_is_int8 != 0, scale, x, y, N, K, rows, B, g_pdl.load(), (cudaStream_t)stream),
+                  "gemv");
+}
+
+int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int S,
+                   int K, uint16_t *state, const uint16_t *cw, const uint16_t *cbias, void *stream) {
+  REQUIRE(epi == 0 || epi == 1, "epi 0 (swiglu) or 1 (shortconv)");
+  REQUIRE(S > 0 && K > 0, "batch 1: x [1, K], y [1, S]");
+  REQUIRE(K % (w_is_int8 ? 512 : 256) == 0, "K must be a multiple of 256 (bf16) / 512 (int8)");
+  REQUIRE(W && x && y, "W, x and y must be non-null");
+  REQUIRE(!w_is_int8 || scale, "int8 W needs fp32 scale");
+  REQUIRE(epi == 0 || (state && cw), "shortconv epilogue needs state and conv weight");
+  REQUIRE(aligned16(W) && aligned16(x), "W and x must be 16-byte aligned");
+  if (int e = device_gate()) return e;
+  return launched(launch_gemv_epi(epi, W, w_is_int8 != 0, scale, x, y, S, K, state, cw, cbias, g_pdl.load(),
+                                  (cudaStream_t)stream),
+                  "gemv_epi");
+}
+
+}  // extern "C"

@@ -1,0 +1,64 @@
+// Shared device helpers for the lfm2q kernels (sm_100a only).
+//
+// Every kernel in this library is written for B200 (compute capability 10.0a): 32-wide warps, 148 SMs,
+// tcgen05 tensor cores with TMEM accumulators, TMA bulk-tensor copies, HBM3e. Nothing here has a path
+// for another architecture; the host layer refuses to launch on anything but an sm_100 device.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lfm2q {
+
+typedef __nv_bfloat16 bf16;
+
+// ------------------------------------------------------------------ scalar conversions
+__device__ __forceinline__ float bf2f(bf16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ bf16 f2bf(float v) { return __float2bfloat16_rn(v); }
+// round an fp32 value to bf16 and back (the rounding point of every bf16 tensor op)
+__device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&p);
+}
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+
+// symmetric int8 code of v at scale sc: the IEEE quotient rounded half-to-even, clamped to +-127
+__device__ __forceinline__ int q8(float v, float sc) {
+  const int q = __float2int_rn(__fdiv_rn(v, sc));
+  return max(-127, min(127, q));
+}
+
+// ------------------------------------------------------------------ streaming loads
+// 16-byte read-only load that does not allocate in L1: weights are read exactly once per launch.
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// ------------------------------------------------------------------ warp reductions
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while its predecessor drains.
+// Before pdl_wait() it may only read immutable data (weights); pdl_wait() returns once the previous
+// grid's writes are visible. Both are no-ops for an ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+}  // namespace lfm2q

@@ -1,0 +1,665 @@
+// W8A8 GEMM on the B200 tensor cores: Y[M, N] = epilogue( Xq[M, K] . Wq[N, K]^T ), int8 x int8 -> exact int32.
+//
+// Reference: kernels/int8_gemm.cu:125-297 (gemm_i8_kernel, mma.sync m16n8k32 + cp.async), epilogue store_tile
+// :93-115, grouped fold :202-230, QOUT requantization :234-285, launchers :741-763; bindings
+// kernels/int8_gemm.cpp:39-69. The SiLU-gate epilogue has no counterpart in the reference GEMM: it fuses the
+// reference's gemm_i8 (bf16 out) -> silu_mul (kernels/lfm2_decode.cu:954-963) composition.
+//
+// Epilogues (fp32, no FMA contraction where the reference has none):
+//   EPI_TOKEN   y = bf16( act( ((float)acc * sx[m]) * sw[n] + b[n] ) ),          act = id | GELU(tanh)
+//   EPI_GROUP   f = fold_g fma((float)acc_g, sxT[g][m], f) over 64-wide K groups; y = bf16(act(f * sw[n] + b[n]))
+//   EPI_GROUP_Q as EPI_GROUP, then the bf16-rounded row segment of every 64 output columns is requantized:
+//               yq int8 [M, N], ysT[n / 64][m] = max(|.|, 1e-8) / 127
+//   EPI_SILU    weight rows [0, I) = gate, [I, 2I) = up; g, u = bf16 of the per-token epilogue;
+//               y[m, n] = bf16( bf16(silu(g)) * u ),  silu(g) = g / (1 + __expf(-g)),  y is [M, I]
+//
+// B200 structure (one persistent CTA per SM, 192 threads, warp-specialised):
+//   warp 0      TMA producer: 128 x 128-byte A tile and BN x 128-byte B tile per stage, 128-byte swizzle,
+//               OOB rows / K columns zero-filled by the copy engine (M, N and K tails need no code)
+//   warp 1      allocates TMEM and issues tcgen05.mma.cta_group::1.kind::i8 (M=128, N=BN, K=32) from one thread;
+//               tcgen05.commit releases a smem stage when its MMAs retire and hands a finished accumulator over
+//   warps 2-5   epilogue: tcgen05.ld (32 lanes x 32 columns per load) -> fp32 math -> global stores; each thread
+//               owns one output row, so per-row scales and the QOUT row-group maxima stay in registers
+//   TMEM        512 columns: 2 accumulators of 256 (TOKEN / SILU) or 4 of 128 (GROUP: one per 64-wide K group, so
+//               the int32 partial sums of group g are folded while the MMAs of groups g+1.. run)
+// Every mbarrier wait is bounded (~1 s of SM clocks). On expiry the kernel records an error code in a device word,
+// tells the other roles to stop through shared memory, frees its TMEM and returns; the host reads the code.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace lfm2q {
+
+__device__ int g_gemm_err = 0;  // sticky: 1 = a pipeline wait timed out
+
+namespace {
+
+constexpr int TM = 128;        // output rows per tile (UMMA M, one TMEM lane per row)
+constexpr int TK = 128;        // K bytes per pipeline stage: one 128-byte swizzle row
+constexpr int NTHREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr long long WAIT_LIMIT = 1ll << 31;
+
+struct GemmArgs {
+  const float *sa;    // sx [M] (per token) or sxT [K/64][M] (grouped)
+  const float *sb;    // sw [N] per weight row
+  const bf16 *bias;   // [N] or null
+  bf16 *Y;            // [M, Nout] bf16
+  int8_t *Yq;         // QOUT: [M, Nout] int8
+  float *YsT;         // QOUT: [Nout/64][M]
+  int M, N, K;        // N = weight rows (SILU: 2 * Nout)
+  int Nout;           // output columns
+  int tiles_m, tiles_n;
+  int m_fast;         // tile raster: 1 = consecutive tiles walk M (A stays in L2), 0 = walk N
+};
+
+// ------------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity. Returns false when this or another role gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*(volatile int *)abort_flag) return false;
+    if (clock64() - t0 > WAIT_LIMIT) {
+      atomicExch(abort_flag, 1);
+      atomicCAS(&g_gemm_err, 0, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// K-major operand in the 128-byte swizzle layout the TMA writes: rows of 128 bytes, 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address (16-byte units)
+  d |= (uint64_t)1 << 16;                    // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset: next 8-row atom
+  d |= (uint64_t)1 << 46;                    // descriptor version (tcgen05)
+  d |= (uint64_t)2 << 61;                    // 128-byte swizzle
+  return d;
+}
+// Instruction descriptor: s8 x s8 -> s32, both operands K-major, M = 128
+__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ float gelu_tanh(float v) {  // F.gelu(v, approximate="tanh")
+  return 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+}
+// exact (float)v for |v| < 2^22: add into the mantissa of 1.5 * 2^23 and subtract it again
+__device__ __forceinline__ float i2f_small(int v) { return __int_as_float(v + 0x4B400000) - 12582912.f; }
+
+__device__ __forceinline__ void tile_coord(int tile, const GemmArgs &a, int &mt, int &nt) {
+  if (a.m_fast) {
+    mt = tile % a.tiles_m;
+    nt = tile / a.tiles_m;
+  } else {
+    nt = tile % a.tiles_n;
+    mt = tile / a.tiles_n;
+  }
+}
+
+// one elected lane waits, the warp follows its verdict (keeps the .sync.aligned TMEM loads convergent)
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int *abort_flag) {
+  const int lane = threadIdx.x & 31;
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait(bar, parity, abort_flag);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  return ok;
+}
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = TM * TK;
+  static constexpr int B_BYTES = BN * TK;
+  static constexpr int A_OFF = 0;
+  static constexpr int B_OFF = STAGES * A_BYTES;
+  static constexpr int BAR_OFF = B_OFF + STAGES * B_BYTES;
+  static constexpr int NBARS = 2 * STAGES + 8;
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int BYTES = MISC_OFF + 16;
+  static constexpr int ALLOC = BYTES + 1024;  // room to align the base to 1024
+};
+
+// ------------------------------------------------------------------ epilogue helpers
+template <bool GELU>
+__device__ __forceinline__ float epi_token(int acc, float sxm, float sw, float b) {
+  float y = __fmul_rn((float)acc, sxm);  // cvt.rn: the int32 sum rounds to fp32 exactly as torch's .float()
+  y = __fadd_rn(__fmul_rn(y, sw), b);
+  if (GELU) y = gelu_tanh(y);
+  return y;
+}
+
+__device__ __forceinline__ void load8f(const float *p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8b(const bf16 *p, float (&v)[8]) {
+  if (p == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    return;
+  }
+  const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf_lo(w[i]);
+    v[2 * i + 1] = bf_hi(w[i]);
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int BN, int STAGES, int NACC, int EPI, bool GELU>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  using L = Smem<BN, STAGES>;
+  constexpr bool GROUPED = (EPI == EPI_GROUP || EPI == EPI_GROUP_Q);
+  constexpr int TMEM_COLS = NACC * BN;
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(!GROUPED || BN == 128, "grouped tiles are 128 columns wide");
+  constexpr uint32_t IDESC = idesc_i8(BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::MISC_OFF);
+  int *abort_flag = reinterpret_cast<int *>(smem + L::MISC_OFF + 4);
+  auto bar_full = [&](int s) { return smem_addr(bars + s); };
+  auto bar_empty = [&](int s) { return smem_addr(bars + STAGES + s); };
+  auto bar_tfull = [&](int a) { return smem_addr(bars + 2 * STAGES + a); };
+  auto bar_tempty = [&](int a) { return smem_addr(bars + 2 * STAGES + 4 + a); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = args.M, K = args.K;
+  const int KB = (K + TK - 1) / TK;      // pipeline stages per tile
+  const int G = K / 64;                  // grouped: 64-wide K groups (K % 64 == 0)
+  const int tiles = args.tiles_m * args.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int a = 0; a < 4; ++a) {
+      mbar_init(bar_tfull(a), 1);
+      mbar_init(bar_tempty(a), 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        int mt, nt;
+        tile_coord(tile, args, mt, nt);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(bar_empty(stage), phase ^ 1, abort_flag)) goto producer_done;
+          mbar_expect_tx(bar_full(stage), L::A_BYTES + L::B_BYTES);
+          const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
+          const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
+          tma_load_2d(sa, &tmA, bar_full(stage), kb * TK, mt * TM);
+          if (EPI == EPI_SILU) {
+            tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * (BN / 2));
+            tma_load_2d(sb + (BN / 2) * TK, &tmB, bar_full(stage), kb * TK, args.Nout + nt * (BN / 2));
+          } else {
+            tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * BN);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t aphase = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        if (!GROUPED) {
+          if (!mbar_wait(bar_tempty(acc), aphase ^ 1, abort_flag)) goto mma_done;
+          tc_fence_after();
+          const uint32_t d = tmem_base + acc * BN;
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!mbar_wait(bar_full(stage), phase, abort_flag)) goto mma_done;
+            tc_fence_after();
+            const uint64_t ad = sw128_desc(sbase + L::A_OFF + stage * L::A_BYTES);
+            const uint64_t bd = sw128_desc(sbase + L::B_OFF + stage * L::B_BYTES);
+#pragma unroll
+            for (int k = 0; k < TK / 32; ++k)  // +32 bytes of K per MMA = +2 in the 16-byte address field
+              umma_i8(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+            umma_commit(bar_empty(stage));
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          umma_commit(bar_tfull(acc));
+          if (++acc == NACC) {
+            acc = 0;
+            aphase ^= 1;
+          }
+        } else {
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!mbar_wait(bar_full(stage), phase, abort_flag)) goto mma_done;
+            tc_fence_after();
+            const uint64_t ad = sw128_desc(sbase + L::A_OFF + stage * L::A_BYTES);
+            const uint64_t bd = sw128_desc(sbase + L::B_OFF + stage * L::B_BYTES);
+#pragma unroll
+            for (int gi = 0; gi < 2; ++gi) {
+              if (2 * kb + gi >= G) break;
+              if (!mbar_wait(bar_tempty(acc), aphase ^ 1, abort_flag)) goto mma_done;
+              tc_fence_after();
+              const uint32_t d = tmem_base + acc * BN;
+              umma_i8(d, ad + 4 * gi, bd + 4 * gi, IDESC, 0u);
+              umma_i8(d, ad + 4 * gi + 2, bd + 4 * gi + 2, IDESC, 1u);
+              umma_commit(bar_tfull(acc));
+              if (++acc == NACC) {
+                acc = 0;
+                aphase ^= 1;
+              }
+            }
+            umma_commit(bar_empty(stage));
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+    mma_done:;
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue warps 2..5
+    const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;    // tile row == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      int mt, nt;
+      tile_coord(tile, args, mt, nt);
+      const int m = mt * TM + row;
+      const bool mrow = m < M;
+      if (!GROUPED) {
+        const int OUTW = (EPI == EPI_SILU) ? BN / 2 : BN;  // output columns per tile
+        const int n0 = nt * OUTW;
+        const float sxm = mrow ? __ldg(args.sa + m) : 0.f;
+        if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem_base + lane_addr + acc * BN;
+#pragma unroll 1
+        for (int c = 0; c < OUTW; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tb + c, r);
+          uint32_t ru[32];
+          if (EPI == EPI_SILU) tmem_ld32(tb + BN / 2 + c, ru);
+          tmem_wait_ld();
+          const int nb = n0 + c;
+          if (mrow) {
+#pragma unroll
+            for (int j8 = 0; j8 < 32; j8 += 8) {
+              const int n = nb + j8;
+              if (n >= args.Nout) break;
+              float sw[8], bb[8];
+              load8f(args.sb + n, sw);
+              load8b(args.bias ? args.bias + n : nullptr, bb);
+              uint32_t o[4];
+              if (EPI == EPI_SILU) {
+                float swu[8], bu[8];
+                load8f(args.sb + args.Nout + n, swu);
+                load8b(args.bias ? args.bias + args.Nout + n : nullptr, bu);
+#pragma unroll
+                for (int j = 0; j < 8; j += 2) {
+                  float out[2];
+#pragma unroll
+                  for (int h = 0; h < 2; ++h) {
+                    const float g = rbf(epi_token<false>((int)r[j8 + j + h], sxm, sw[j + h], bb[j + h]));
+                    const float u = rbf(epi_token<false>((int)ru[j8 + j + h], sxm, swu[j + h], bu[j + h]));
+                    out[h] = rbf(g / (1.f + __expf(-g))) * u;
+                  }
+                  o[j / 2] = pack_bf16x2(out[0], out[1]);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; j += 2)
+                  o[j / 2] = pack_bf16x2(epi_token<GELU>((int)r[j8 + j], sxm, sw[j], bb[j]),
+                                         epi_token<GELU>((int)r[j8 + j + 1], sxm, sw[j + 1], bb[j + 1]));
+              }
+              *reinterpret_cast<uint4 *>(args.Y + (size_t)m * args.Nout + n) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_tempty(acc));
+        if (++acc == NACC) {
+          acc = 0;
+          aphase ^= 1;
+        }
+      } else {
+        // grouped: fold every 64-wide K group into fp32 running sums held in registers (128 columns per row)
+        const int n0 = nt * BN;
+        float f[BN];
+#pragma unroll
+        for (int j = 0; j < BN; ++j) f[j] = 0.f;
+        float s_next = (mrow && G > 0) ? __ldg(args.sa + m) : 0.f;
+        bool ok = true;
+        for (int g = 0; g < G; ++g) {
+          const float s = s_next;
+          if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tb = tmem_base + lane_addr + acc * BN;
+#pragma unroll
+          for (int c = 0; c < BN; c += 64) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tb + c, r0);
+            tmem_ld32(tb + c + 32, r1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[c + j] = __fmaf_rn(i2f_small((int)r0[j]), s, f[c + j]);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[c + 32 + j] = __fmaf_rn(i2f_small((int)r1[j]), s, f[c + 32 + j]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty(acc));
+          if (++acc == NACC) {
+            acc = 0;
+            aphase ^= 1;
+          }
+          if (g + 1 < G) s_next = mrow ? __ldg(args.sa + (size_t)(g + 1) * M + m) : 0.f;
+        }
+        if (!ok) break;
+        if (!mrow) continue;
+        if (EPI == EPI_GROUP) {
+#pragma unroll
+          for (int j8 = 0; j8 < BN; j8 += 8) {
+            const int n = n0 + j8;
+            if (n >= args.Nout) break;
+            float sw[8], bb[8];
+            load8f(args.sb + n, sw);
+            load8b(args.bias ? args.bias + n : nullptr, bb);
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              float y0 = __fadd_rn(__fmul_rn(f[j8 + j], sw[j]), bb[j]);
+              float y1 = __fadd_rn(__fmul_rn(f[j8 + j + 1], sw[j + 1]), bb[j + 1]);
+              if (GELU) {
+                y0 = gelu_tanh(y0);
+                y1 = gelu_tanh(y1);
+              }
+              o[j / 2] = pack_bf16x2(y0, y1);
+            }
+            *reinterpret_cast<uint4 *>(args.Y + (size_t)m * args.Nout + n) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        } else {
+          // QOUT: bf16-round the outputs, then one scale per (row, 64 columns); N % 128 == 0 (whole tiles)
+#pragma unroll
+          for (int h = 0; h < BN / 64; ++h) {
+            float amax = 0.f;
+#pragma unroll
+            for (int j8 = 0; j8 < 64; j8 += 8) {
+              const int n = n0 + h * 64 + j8;
+              float sw[8], bb[8];
+              load8f(args.sb + n, sw);
+              load8b(args.bias ? args.bias + n : nullptr, bb);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float y = __fadd_rn(__fmul_rn(f[h * 64 + j8 + j], sw[j]), bb[j]);
+                if (GELU) y = gelu_tanh(y);
+                y = rbf(y);
+                f[h * 64 + j8 + j] = y;
+                amax = fmaxf(amax, fabsf(y));
+              }
+            }
+            const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
+            args.YsT[(size_t)((n0 >> 6) + h) * M + m] = sc;
+#pragma unroll
+            for (int j16 = 0; j16 < 64; j16 += 16) {
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int b0 = q8(f[h * 64 + j16 + 4 * i + 0], sc), b1 = q8(f[h * 64 + j16 + 4 * i + 1], sc);
+                const int b2 = q8(f[h * 64 + j16 + 4 * i + 2], sc), b3 = q8(f[h * 64 + j16 + 4 * i + 3], sc);
+                w[i] = (uint32_t)(b0 & 0xFF) | ((uint32_t)(b1 & 0xFF) << 8) | ((uint32_t)(b2 & 0xFF) << 16) |
+                       ((uint32_t)(b3 & 0xFF) << 24);
+              }
+              *reinterpret_cast<uint4 *>(args.Yq + (size_t)m * args.Nout + n0 + h * 64 + j16) =
+                  make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D int8 matrix [rows, inner] row-major, box = 128 bytes x box_rows, 128-byte swizzle, OOB reads as zero
+bool make_map(CUtensorMap *map, const void *ptr, int inner, int rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner};
+  cuuint32_t box[2] = {(cuuint32_t)TK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int g_tile_override = 0;
+
+template <int BN, int STAGES, int NACC, int EPI, bool GELU>
+cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) {
+  using L = Smem<BN, STAGES>;
+  auto kern = gemm_tc_kernel<BN, STAGES, NACC, EPI, GELU>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  CUtensorMap ta, tb;
+  const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN;
+  if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, box_b)) return cudaErrorInvalidValue;
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
+  kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
+GemmArgs base_args(const float *sa, const float *sb, const void *bias, int M, int N, int K, int nout, int tile_n) {
+  GemmArgs a = {};
+  a.sa = sa;
+  a.sb = sb;
+  a.bias = (const bf16 *)bias;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.Nout = nout;
+  a.tiles_m = (M + TM - 1) / TM;
+  a.tiles_n = (nout + tile_n - 1) / tile_n;
+  a.m_fast = M <= nout ? 1 : 0;  // walk the dimension whose operand is smaller, so it stays in L2
+  return a;
+}
+
+}  // namespace
+
+int gemm_device_error(bool clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_err, sizeof(int));
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_gemm_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+void gemm_set_tile_override(int bn) { g_tile_override = (bn == 128 || bn == 256) ? bn : 0; }
+
+cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias, void *Y,
+                           int M, int N, int K, bool gelu, bool grouped, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (grouped) {
+    GemmArgs a = base_args(sa, sb, bias, M, N, K, N, 128);
+    a.Y = (bf16 *)Y;
+    return gelu ? run_tc<128, 6, 4, EPI_GROUP, true>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false>(A, B, a, st);
+  }
+  int bn = g_tile_override;
+  if (!bn) {
+    const long tiles256 = (long)((M + TM - 1) / TM) * ((N + 255) / 256);
+    bn = tiles256 >= device_sm_count() ? 256 : 128;
+  }
+  GemmArgs a = base_args(sa, sb, bias, M, N, K, N, bn);
+  a.Y = (bf16 *)Y;
+  if (bn == 256)
+    return gelu ? run_tc<256, 4, 2, EPI_TOKEN, true>(A, B, a, st) : run_tc<256, 4, 2, EPI_TOKEN, false>(A, B, a, st);
+  return gelu ? run_tc<128, 6, 2, EPI_TOKEN, true>(A, B, a, st) : run_tc<128, 6, 2, EPI_TOKEN, false>(A, B, a, st);
+}
+
+cudaError_t launch_gemm_i8_q(const int8_t *A, const float *saT, const int8_t *B, const float *sb, const void *bias,
+                             int8_t *Yq, float *YsT, int M, int N, int K, bool gelu, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  GemmArgs a = base_args(saT, sb, bias, M, N, K, N, 128);
+  a.Yq = Yq;
+  a.YsT = YsT;
+  return gelu ? run_tc<128, 6, 4, EPI_GROUP_Q, true>(A, B, a, st)
+              : run_tc<128, 6, 4, EPI_GROUP_Q, false>(A, B, a, st);
+}
+
+cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias,
+                                void *Y, int M, int I, int K, cudaStream_t st) {
+  if (M <= 0 || I <= 0) return cudaSuccess;
+  GemmArgs a = base_args(sa, sb, bias, M, 2 * I, K, I, 128);
+  a.Y = (bf16 *)Y;
+  return run_tc<256, 4, 2, EPI_SILU, false>(A, B, a, st);
+}
+
+}  // namespace lfm2q
+
+namespace lfm2q {
+// W8A16 is built in a later step; until then the entry point reports that it is unavailable.
+cudaError_t launch_gemm_w8(const void *, const int8_t *, const float *, const void *, void *, int, int, int, bool,
+                           cudaStream_t) {
+  return cudaErrorNotSupported;
+}
+}  // namespace lfm2q

@@ -1,0 +1,343 @@
+// Weight-only decode GEMV: y[b, n] = bf16( (sum_k W[n, k] * x[b, k]) * scale[n] ), W int8 (or bf16) [N, K]
+// row-major, x / y bf16, fp32 accumulation, for 1..16 tokens per launch (more in chunks of 16).
+//
+// Reference: kernels/lfm2_decode.cu:576-661 (gemv_direct_kernel), :666-714 (gemv_dispatch / launch_gemv),
+// binding kernels/lfm2_decode.cpp:73-85; fused epilogues kernels/lfm2_decode.cu:724-827 (gemv_epi_kernel).
+//
+// B200 design. The op is HBM-bound: every weight byte is read once, so the kernel must keep ~40 KB of loads in
+// flight per SM and spend few ALU instructions per byte (at 85 % of 6.5 TB/s there are ~6 lane-instructions per
+// weight). A warp owns a 16-row group of W and a K-slice; each lane streams two 16-byte chunks per 64-wide K step
+// (rows g and g + 8 of the group), converts the int8 codes exactly to bf16 in registers (exponent-bias trick:
+// byte + 128 placed in the mantissa of 2^23, one FADD removes the bias; the small integers are exact in bf16),
+// and feeds warp-level bf16 MMAs (m16n8k16, fp32 accumulation) with the tokens on the N side. The MMA makes the
+// cost per weight independent of the batch (8 tokens per MMA). The K order inside a 64-wide step is permuted
+// identically for W and x (lane t, step s take physical k 16t+4s..16t+4s+3), which leaves the dot product
+// unchanged. Small N is split over K-slices (KS warps per row group) whose fp32 partials meet in shared memory
+// and are summed in a fixed order, so results are deterministic.
+#include "common.cuh"
+#include "launch.h"
+
+namespace lfm2q {
+namespace {
+
+constexpr int GV_THREADS = 256;  // 8 warps
+constexpr int GV_BATCH = 4;      // 64-wide K steps loaded per batch (double-buffered)
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 4 int8 codes (bytes of w) -> two bf16x2 words (lo: bytes 0,1; hi: bytes 2,3), exact
+__device__ __forceinline__ void i8x4_to_bf16x2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  const uint32_t u = w ^ 0x80808080u;  // q + 128 in 0..255
+  const float bias = 8388736.f;        // 2^23 + 128
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - bias;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - bias;
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - bias;
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - bias;
+  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+}
+
+template <typename WT>
+struct WFmt;
+// int8: one 16-byte chunk = 16 codes = 4 MMA k-steps of one row; a 64-wide K step is one chunk per lane-row
+template <>
+struct WFmt<int8_t> {
+  static constexpr int KSTEP = 64;  // K covered per lane chunk pair
+  static constexpr int STEPS = 4;   // MMA k16 steps per chunk
+  __device__ static void frag(const uint4 &r0, const uint4 &r1, int s, uint32_t (&a)[4]) {
+    const uint32_t w0 = (&r0.x)[s], w1 = (&r1.x)[s];
+    i8x4_to_bf16x2x2(w0, a[0], a[2]);  // row g: k slots 2t,2t+1 | 2t+8,2t+9
+    i8x4_to_bf16x2x2(w1, a[1], a[3]);  // row g + 8
+  }
+};
+// bf16: one 16-byte chunk = 8 weights = 2 MMA k-steps of one row
+template <>
+struct WFmt<bf16> {
+  static constexpr int KSTEP = 32;
+  static constexpr int STEPS = 2;
+  __device__ static void frag(const uint4 &r0, const uint4 &r1, int s, uint32_t (&a)[4]) {
+    a[0] = (&r0.x)[2 * s];
+    a[2] = (&r0.x)[2 * s + 1];
+    a[1] = (&r1.x)[2 * s];
+    a[3] = (&r1.x)[2 * s + 1];
+  }
+};
+
+// x fragment words for lane (g, t) at K position k0 of token `tok`: the lane's chunk of x covers the same
+// physical k as its weight chunk: int8 -> 16 bf16 (two 16-byte loads), bf16 -> 8 bf16 (one load)
+template <typename WT>
+__device__ __forceinline__ void load_x(const bf16 *__restrict__ x, int K, int tok, int B, int kphys, uint32_t (&xw)[8]) {
+  constexpr int NW = WFmt<WT>::KSTEP / 8;  // 32-bit words per lane chunk: 8 (int8) or 4 (bf16)
+  if (tok < B) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(x + (size_t)tok * K + kphys);
+    const uint4 v0 = __ldg(p);
+    xw[0] = v0.x; xw[1] = v0.y; xw[2] = v0.z; xw[3] = v0.w;
+    if (NW == 8) {
+      const uint4 v1 = __ldg(p + 1);
+      xw[4] = v1.x; xw[5] = v1.y; xw[6] = v1.z; xw[7] = v1.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xw[i] = 0u;
+  }
+}
+
+// Core: one warp accumulates rows [r0, r0 + 16) x K-slice [kb, ke) for tokens 0..8*NT-1 into acc[NT][4].
+template <typename WT, int NT>
+__device__ __forceinline__ void warp_gemv(const WT *__restrict__ W, const bf16 *__restrict__ x, int N, int K, int B,
+                                          int r0, int kb, int ke, float (&acc)[NT][4], bool pdl) {
+  constexpr int KSTEP = WFmt<WT>::KSTEP, STEPS = WFmt<WT>::STEPS;
+  constexpr int CH = 16 / sizeof(WT);  // elements per 16-byte chunk
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const WT *row0 = W + (size_t)min(r0 + g, N - 1) * K;
+  const WT *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K;
+  // lane t's chunk inside a KSTEP-wide step starts at element t * CH
+  const int nsteps = (ke - kb) / KSTEP;
+  uint4 wb[2][GV_BATCH][2];
+
+  auto load_batch = [&](int buf, int st0) {
+#pragma unroll
+    for (int u = 0; u < GV_BATCH; ++u) {
+      const int st = st0 + u;
+      if (st < nsteps) {
+        const int k = kb + st * KSTEP + t * CH;
+        wb[buf][u][0] = ld_stream16(row0 + k);
+        wb[buf][u][1] = ld_stream16(row1 + k);
+      }
+    }
+  };
+  auto compute_batch = [&](int buf, int st0) {
+#pragma unroll
+    for (int u = 0; u < GV_BATCH; ++u) {
+      const int st = st0 + u;
+      if (st < nsteps) {
+        const int kphys = kb + st * KSTEP + t * CH;
+        uint32_t xw[NT][8];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kphys, xw[j]);
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+          uint32_t a[4];
+          WFmt<WT>::frag(wb[buf][u][0], wb[buf][u][1], s, a);
+#pragma unroll
+          for (int j = 0; j < NT; ++j) mma_bf16_16816(acc[j], a, xw[j][2 * s], xw[j][2 * s + 1]);
+        }
+      }
+    }
+  };
+
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+
+  load_batch(0, 0);  // weights are immutable: stream them before the dependency wait
+  if (pdl) pdl_wait();
+  for (int st0 = 0; st0 < nsteps; st0 += 2 * GV_BATCH) {
+    load_batch(1, st0 + GV_BATCH);
+    compute_batch(0, st0);
+    load_batch(0, st0 + 2 * GV_BATCH);
+    compute_batch(1, st0 + GV_BATCH);
+  }
+}
+
+// Fragment accumulator element e of token group j -> (row in group, token)
+__device__ __forceinline__ int frag_row(int lane, int e) { return (lane >> 2) + ((e & 2) ? 8 : 0); }
+__device__ __forceinline__ int frag_tok(int lane, int j, int e) { return 8 * j + 2 * (lane & 3) + (e & 1); }
+
+// Plain GEMV. Block = RG row groups x KS K-slices (RG * KS == 8 warps).
+template <typename WT, int NT, int KS>
+__global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__ W, const float *__restrict__ scale,
+                                                          const bf16 *__restrict__ x, bf16 *__restrict__ y, int N, int K,
+                                                          int B, int pdl) {
+  constexpr int RG = 8 / KS;
+  __shared__ float red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
+  if (pdl) pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rg = warp / KS, ks = warp % KS;
+  const int r0 = (blockIdx.x * RG + rg) * 16;
+  const int kslice = K / KS;
+  float acc[NT][4];
+  warp_gemv<WT, NT>(W, x, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, pdl != 0);
+  if (KS == 1) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int n = r0 + frag_row(lane, e), b = frag_tok(lane, j, e);
+        if (n < N && b < B) y[(size_t)b * N + n] = f2bf(scale ? acc[j][e] * scale[n] : acc[j][e]);
+      }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
+  __syncthreads();
+  for (int i = threadIdx.x; i < RG * 16 * 8 * NT; i += GV_THREADS) {
+    const int b = i % (8 * NT), rr = (i / (8 * NT)) % 16, g2 = i / (16 * 8 * NT);
+    const int n = (blockIdx.x * RG + g2) * 16 + rr;
+    if (n >= N || b >= B) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int s = 0; s < KS; ++s) v += red[((g2 * KS + s) * 16 + rr) * 8 * NT + b];
+    y[(size_t)b * N + n] = f2bf(scale ? v * scale[n] : v);
+  }
+}
+
+// Batch-1 GEMV over NR stacked [S, K] blocks of W followed by an elementwise epilogue on the NR values of one
+// output index (kernels/lfm2_decode.cu:718-805):
+//   EPI 0, NR 2 (w1 | w3):         y[n] = bf16( bf16(silu(g)) * u ),  g, u = the bf16 the plain GEMV would store
+//   EPI 1, NR 3 (in_proj B|C|x):   bx = bf16(B * x); conv state shift; y = bf16(C * bf16(w . window + bias))
+// Block = NR parts x 8/NR... laid out as 2 row groups x 4 K-slices (NR=2) or 2 row groups x ... see host dispatch:
+// the block covers 16 output indices; warp w handles part w / KSE and K-slice w % KSE.
+template <typename WT, int NR, int EPI>
+__global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restrict__ W, const float *__restrict__ scale,
+                                                              const bf16 *__restrict__ x, bf16 *__restrict__ y, int S,
+                                                              int K, bf16 *__restrict__ state,
+                                                              const bf16 *__restrict__ cw,
+                                                              const bf16 *__restrict__ cbias, int pdl) {
+  constexpr int KSE = (NR == 2) ? 4 : 2;  // K-slices per part (NR * KSE <= 8 warps)
+  __shared__ float red[NR][KSE][16];
+  __shared__ float part[NR][16];
+  if (pdl) pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = warp / KSE, ks = warp % KSE;
+  const int n0 = blockIdx.x * 16;
+  if (p < NR) {
+    const int kslice = K / KSE;
+    float acc[1][4];
+    // rows of part p: p * S + n0 .. ; clamp inside the part so the loads stay in W
+    const WT *Wp = W + (size_t)p * S * K;
+    warp_gemv<WT, 1>(Wp, x, S, K, 1, n0, ks * kslice, (ks + 1) * kslice, acc, pdl != 0);
+    // token 0 lives in lanes with t == 0, element e & 1 == 0
+    if ((lane & 3) == 0) {
+      red[p][ks][frag_row(lane, 0)] = acc[0][0];
+      red[p][ks][frag_row(lane, 2)] = acc[0][2];
+    }
+  } else if (pdl) {
+    pdl_wait();
+  }
+  __syncthreads();
+  if (threadIdx.x < NR * 16) {
+    const int pp = threadIdx.x / 16, r = threadIdx.x % 16, n = n0 + r;
+    float v = 0.f;
+#pragma unroll
+    for (int s = 0; s < KSE; ++s) v += red[pp][s][r];
+    part[pp][r] = (n < S) ? rbf(scale ? v * scale[pp * S + n] : v) : 0.f;
+  }
+  __syncthreads();
+  if (threadIdx.x >= 16) return;
+  const int m = n0 + threadIdx.x;
+  if (m >= S) return;
+  if (EPI == 0) {
+    const float g = part[0][threadIdx.x], u = part[1][threadIdx.x];
+    y[m] = f2bf(rbf(g / (1.f + __expf(-g))) * u);
+  } else {
+    const float bx = rbf(part[0][threadIdx.x] * part[2][threadIdx.x]);
+    bf16 *st = state + (size_t)m * 3;
+    const float s1 = bf2f(st[1]), s2 = bf2f(st[2]);
+    st[0] = st[1];
+    st[1] = st[2];
+    st[2] = f2bf(bx);
+    // conv = w0 * s1 + w1 * s2 + w2 * bx (+ bias), evaluated left to right with explicit fp32 roundings
+    float acc2 = __fmul_rn(bf2f(cw[m * 3 + 0]), s1);
+    acc2 = __fadd_rn(acc2, __fmul_rn(bf2f(cw[m * 3 + 1]), s2));
+    acc2 = __fadd_rn(acc2, __fmul_rn(bf2f(cw[m * 3 + 2]), bx));
+    if (cbias) acc2 = __fadd_rn(acc2, bf2f(cbias[m]));
+    y[m] = f2bf(part[1][threadIdx.x] * rbf(acc2));
+  }
+}
+
+template <typename KernelT, typename... Args>
+cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <typename WT, int NT>
+cudaError_t gemv_ks(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
+                    cudaStream_t st) {
+  const int groups = (N + 15) / 16, rg = 8 / ks;
+  const dim3 grid((groups + rg - 1) / rg);
+  const int p = pdl ? 1 : 0;
+  switch (ks) {
+    case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
+    case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
+    case 4: return launch_ex(gemv_kernel<WT, NT, 4>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
+    default: return launch_ex(gemv_kernel<WT, NT, 8>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
+  }
+}
+
+// K-slices: the fewest that give ~8 warps per SM, keeping each slice a whole number of 64-wide steps
+int pick_ks(int N, int K, int kstep, int rows_override) {
+  if (rows_override == 1 || rows_override == 2 || rows_override == 4 || rows_override == 8) return rows_override;
+  const long groups = (N + 15) / 16;
+  const long target = 8L * device_sm_count();
+  int ks = 1;
+  while (ks < 8 && groups * ks < target && (K / (2 * ks)) % kstep == 0 && K / (2 * ks) >= kstep) ks *= 2;
+  return ks;
+}
+
+template <typename WT>
+cudaError_t gemv_dispatch(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int rows, int B,
+                          bool pdl, cudaStream_t st) {
+  const int ks = pick_ks(N, K, WFmt<WT>::KSTEP, rows);
+  for (int b0 = 0; b0 < B; b0 += 16) {
+    const int bs = min(16, B - b0);
+    const bf16 *xb = x + (size_t)b0 * K;
+    bf16 *yb = y + (size_t)b0 * N;
+    const cudaError_t e = bs > 8 ? gemv_ks<WT, 2>(W, scale, xb, yb, N, K, bs, ks, pdl, st)
+                                 : gemv_ks<WT, 1>(W, scale, xb, yb, N, K, bs, ks, pdl, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+template <typename WT>
+cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf16 *x, bf16 *y, int S, int K,
+                              bf16 *state, const bf16 *cw, const bf16 *cbias, bool pdl, cudaStream_t st) {
+  const dim3 grid((S + 15) / 16);
+  const int p = pdl ? 1 : 0;
+  if (epi == 0)
+    return launch_ex(gemv_epi_kernel<WT, 2, 0>, grid, GV_THREADS, pdl, st, W, scale, x, y, S, K, state, cw, cbias, p);
+  return launch_ex(gemv_epi_kernel<WT, 3, 1>, grid, GV_THREADS, pdl, st, W, scale, x, y, S, K, state, cw, cbias, p);
+}
+
+}  // namespace
+
+cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
+                        int B, bool pdl, cudaStream_t st) {
+  if (N <= 0 || B <= 0) return cudaSuccess;
+  if (int8)
+    return gemv_dispatch<int8_t>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
+  return gemv_dispatch<bf16>((const bf16 *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
+}
+
+cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,
+                            void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st) {
+  if (S <= 0) return cudaSuccess;
+  if (int8)
+    return gemv_epi_dispatch<int8_t>(epi, (const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, S, K, (bf16 *)state,
+                                     (const bf16 *)cw, (const bf16 *)cbias, pdl, st);
+  return gemv_epi_dispatch<bf16>(epi, (const bf16 *)W, scale, (const bf16 *)x, (bf16 *)y, S, K, (bf16 *)state,
+                                 (const bf16 *)cw, (const bf16 *)cbias, pdl, st);
+}
+
+}  // namespace lfm2q

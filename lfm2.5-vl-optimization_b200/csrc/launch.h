@@ -1,0 +1,47 @@
+// Internal launcher interface between the CUDA translation units and the C ABI (capi.cpp).
+// Launchers assume validated arguments (capi.cpp checks shapes, alignment and the device) and only
+// enqueue work on `st`; they return the launch status.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lfm2q {
+
+// quant.cu
+cudaError_t launch_quant_rows(const void *x, int8_t *q, float *s, int rows, int K, cudaStream_t st);
+cudaError_t launch_quant_groups(const void *x, int8_t *q, float *sT, int rows, int K, cudaStream_t st);
+
+// producers.cu
+cudaError_t launch_add_layernorm_q(void *h, const void *y, const void *w, const void *b, int8_t *q, float *s, int rows,
+                                   int D, float eps, bool grouped, cudaStream_t st);
+cudaError_t launch_add_rmsnorm_q(void *h, const void *y, const void *w, int8_t *q, float *s, int rows, int H, float eps,
+                                 bool grouped, cudaStream_t st);
+cudaError_t launch_silu_mul_q(const void *g, int8_t *q, float *s, int rows, int I, bool grouped, cudaStream_t st);
+
+// gemv.cu
+cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
+                        int B, bool pdl, cudaStream_t st);
+cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,
+                            void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st);
+
+// gemm_tc.cu: tcgen05 W8A8 GEMMs
+enum GemmEpi { EPI_TOKEN = 0, EPI_GROUP = 1, EPI_GROUP_Q = 2, EPI_SILU = 3 };
+cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias, void *Y,
+                           int M, int N, int K, bool gelu, bool grouped, cudaStream_t st);
+cudaError_t launch_gemm_i8_q(const int8_t *A, const float *saT, const int8_t *B, const float *sb, const void *bias,
+                             int8_t *Yq, float *YsT, int M, int N, int K, bool gelu, cudaStream_t st);
+cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias,
+                                void *Y, int M, int I, int K, cudaStream_t st);
+int gemm_device_error(bool clear);  // sticky code written by a bounded wait that gave up (0 = none)
+void gemm_set_tile_override(int bn);  // 0 = heuristic, 128 / 256 = force the per-token tile width
+
+// gemm_w8.cu: tcgen05 W8A16 GEMM
+cudaError_t launch_gemm_w8(const void *A, const int8_t *B, const float *sb, const void *bias, void *Y, int M, int N,
+                           int K, bool gelu, cudaStream_t st);
+
+// device facts cached per device
+int device_sm_count();
+bool device_is_sm100();
+
+}  // namespace lfm2q

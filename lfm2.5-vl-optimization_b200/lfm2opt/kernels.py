@@ -1,0 +1,297 @@
+"""The two extension objects the reference loads (src/lfm2opt/kernels.py:178-230 of the reference), backed by the
+prebuilt sm_100a library liblfm2q.so instead of a JIT build.
+
+    int8_ext()  ops of the reference's lfm2_int8_gemm extension (kernels/int8_gemm.cpp:143-151):
+                gemm_i8, gemm_i8_q, gemm_w8, quant_rows, add_layernorm_q, add_rmsnorm_q, silu_mul_q,
+                plus gemm_i8_silu (W8A8 GEMM with the SiLU(w1) * w3 gate fused into its epilogue)
+    ext()       the GEMV part of the reference's lfm2_decode extension (kernels/lfm2_decode.cpp:152-168):
+                gemv, gemv_epi, set_pdl, set_gemv_impl
+
+Argument names, meaning, in-place outputs and the RuntimeError messages of the shape checks follow the reference
+bindings (kernels/int8_gemm.cpp:20-141, kernels/lfm2_decode.cpp:30-150). Every op enqueues on PyTorch's current
+stream of the tensors' device and returns None. The decode extension's non-GEMV kernels (attention, RoPE, conv,
+norms) are not part of this library; reaching for them raises AttributeError.
+"""
+
+import os
+
+import torch
+
+from . import _capi
+
+_I8, _BF, _F32 = torch.int8, torch.bfloat16, torch.float32
+
+
+def _check(t, dtype, name):
+    if not (t.is_cuda and t.dtype == dtype and t.is_contiguous()):
+        raise RuntimeError(f"{name} must be contiguous CUDA {_DT_NAME[dtype]}")
+
+
+_DT_NAME = {_I8: "at::kChar", _BF: "at::kBFloat16", _F32: "at::kFloat"}
+
+
+def _req(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+class _DeviceOf:
+    """Make t's device current for the duration of a call (ops launch on the current device)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, t):
+        self.idx = t.device.index
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.prev)
+
+
+class Int8GemmExt:
+    """Ops of the reference's lfm2_int8_gemm extension."""
+
+    @staticmethod
+    def _common(w, sw, bias, y, M, K):
+        _check(w, _I8, "w")
+        _check(sw, _F32, "sw")
+        _check(y, _BF, "y")
+        _req(w.dim() == 2 and w.size(1) == K, "w must be [N, K]")
+        N = w.size(0)
+        _req(K % 16 == 0 and N % 8 == 0, "need K % 16 == 0 and N % 8 == 0")
+        _req(sw.numel() == N and y.numel() == M * N, "sw / y shape")
+        if bias is not None:
+            _check(bias, _BF, "(*bias)")
+            _req(bias.numel() == N, "bias shape")
+        return N
+
+    def gemm_i8(self, xq, sx, w, sw, bias, y, gelu):
+        """W8A8: y[M, N] = (xq[M, K] . w[N, K]^T) * sx[m] * sw[n] (+ bias) (GELU), bf16 out. sx [M]: one scale per
+        row; sx [K/64, M]: one scale per row and group of 64 input channels."""
+        _check(xq, _I8, "xq")
+        _check(sx, _F32, "sx")
+        K = xq.size(-1)
+        M = xq.numel() // K
+        grouped = sx.dim() == 2
+        _req((K % 64 == 0 and sx.size(0) == K // 64 and sx.size(1) == M) if grouped else sx.numel() == M, "sx shape")
+        N = self._common(w, sw, bias, y, M, K)
+        with _DeviceOf(xq):
+            _capi.call("lfm2q_gemm_i8", xq.data_ptr(), sx.data_ptr(), int(grouped), w.data_ptr(), sw.data_ptr(),
+                       _ptr(bias), y.data_ptr(), M, N, K, int(bool(gelu)), _stream(xq))
+
+    def gemm_i8_q(self, xq, sxT, w, sw, bias, yq, ysT, gelu):
+        """Grouped W8A8 with an INT8 output for the next W8A8 GEMM: (yq [M, N], ysT [N/64, M])."""
+        for t, n, d in ((xq, "xq", _I8), (sxT, "sxT", _F32), (w, "w", _I8), (sw, "sw", _F32), (yq, "yq", _I8),
+                        (ysT, "ysT", _F32)):
+            _check(t, d, n)
+        K = xq.size(-1)
+        M, N = xq.numel() // K, w.size(0)
+        _req(sxT.dim() == 2 and K % 64 == 0 and sxT.size(0) == K // 64 and sxT.size(1) == M, "sxT shape")
+        _req(w.dim() == 2 and w.size(1) == K and N % 128 == 0 and sw.numel() == N, "w [N, K] with N % 128 == 0")
+        _req(yq.numel() == M * N and ysT.dim() == 2 and ysT.size(0) == N // 64 and ysT.size(1) == M, "yq / ysT shape")
+        if bias is not None:
+            _check(bias, _BF, "(*bias)")
+            _req(bias.numel() == N, "bias shape")
+        with _DeviceOf(xq):
+            _capi.call("lfm2q_gemm_i8_q", xq.data_ptr(), sxT.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias),
+                       yq.data_ptr(), ysT.data_ptr(), M, N, K, int(bool(gelu)), _stream(xq))
+
+    def gemm_i8_silu(self, xq, sx, w, sw, bias, y):
+        """W8A8 over w = [w1 | w3] [2I, K] with the SwiGLU gate in the epilogue: y [M, I] = bf16(bf16(silu(g)) * u),
+        g / u = the bf16 per-token outputs of rows n / I + n (gemm_i8 followed by silu_mul, in one kernel)."""
+        _check(xq, _I8, "xq")
+        _check(sx, _F32, "sx")
+        K = xq.size(-1)
+        M = xq.numel() // K
+        _req(sx.dim() == 1 and sx.numel() == M, "sx shape: the SiLU-gate epilogue takes per-token scales [M]")
+        _check(w, _I8, "w")
+        _check(sw, _F32, "sw")
+        _check(y, _BF, "y")
+        _req(w.dim() == 2 and w.size(1) == K and w.size(0) % 2 == 0, "w must be [2I, K]")
+        I = w.size(0) // 2
+        _req(K % 16 == 0 and I % 8 == 0, "need K % 16 == 0 and I % 8 == 0")
+        _req(sw.numel() == 2 * I and y.numel() == M * I, "sw / y shape")
+        if bias is not None:
+            _check(bias, _BF, "(*bias)")
+            _req(bias.numel() == 2 * I, "bias shape")
+        with _DeviceOf(xq):
+            _capi.call("lfm2q_gemm_i8_silu", xq.data_ptr(), sx.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias),
+                       y.data_ptr(), M, I, K, _stream(xq))
+
+    def gemm_w8(self, x, w, sw, bias, y, gelu):
+        """W8A16: y[M, N] = (x[M, K] . w[N, K]^T) * sw[n] (+ bias) (GELU), bf16 in / out."""
+        _check(x, _BF, "x")
+        K = x.size(-1)
+        M = x.numel() // K
+        N = self._common(w, sw, bias, y, M, K)
+        with _DeviceOf(x):
+            _capi.call("lfm2q_gemm_w8", x.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias), y.data_ptr(), M, N, K,
+                       int(bool(gelu)), _stream(x))
+
+    def quant_rows(self, x, q, s):
+        """Per-row (token) symmetric quantization: s = max(|x|) / 127, q = round(x / s); with s of shape [K/64, rows]:
+        one scale per row and group of 64 channels (transposed, as gemm_i8 reads it)."""
+        _check(x, _BF, "x")
+        _check(q, _I8, "q")
+        _check(s, _F32, "s")
+        K = x.size(-1)
+        rows = x.numel() // K
+        if s.dim() == 2:
+            _req(K % 64 == 0 and K <= 16384 and s.size(0) == K // 64 and s.size(1) == rows and q.numel() == x.numel(),
+                 "grouped shapes")
+            with _DeviceOf(x):
+                _capi.call("lfm2q_quant_groups", x.data_ptr(), q.data_ptr(), s.data_ptr(), rows, K, _stream(x))
+            return
+        _req(K % 8 == 0 and K <= 16384, "K must be a multiple of 8, <= 16384")
+        _req(q.numel() == x.numel() and s.numel() == rows, "q / s shape")
+        with _DeviceOf(x):
+            _capi.call("lfm2q_quant_rows", x.data_ptr(), q.data_ptr(), s.data_ptr(), rows, K, _stream(x))
+
+    @staticmethod
+    def _check_qs(q, s, rows, K):
+        _check(q, _I8, "q")
+        _check(s, _F32, "s")
+        grouped = s.dim() == 2
+        _req(q.numel() == rows * K, "q shape")
+        _req((K % 64 == 0 and s.size(0) == K // 64 and s.size(1) == rows) if grouped else s.numel() == rows,
+             "s shape")
+        return grouped
+
+    def add_layernorm_q(self, h, y, w, b, q, s, eps):
+        """Vision: h += y (optional, in place); (q, s) = quant(LayerNorm(h) * w + b)."""
+        _check(h, _BF, "h")
+        _check(w, _BF, "w")
+        _check(b, _BF, "b")
+        if y is not None:
+            _check(y, _BF, "(*y)")
+            _req(y.numel() == h.numel(), "y shape")
+        D = h.size(-1)
+        rows = h.numel() // D
+        _req(D % 8 == 0 and D <= 16384 and w.numel() == D and b.numel() == D, "D must be a multiple of 8, <= 16384")
+        grouped = self._check_qs(q, s, rows, D)
+        with _DeviceOf(h):
+            _capi.call("lfm2q_add_layernorm_q", h.data_ptr(), _ptr(y), w.data_ptr(), b.data_ptr(), q.data_ptr(),
+                       s.data_ptr(), rows, D, float(eps), int(grouped), _stream(h))
+
+    def add_rmsnorm_q(self, h, y, w, q, s, eps):
+        """LM prefill: h += y (optional, in place); (q, s) = quant(w * rmsnorm(h))."""
+        _check(h, _BF, "h")
+        _check(w, _BF, "w")
+        if y is not None:
+            _check(y, _BF, "(*y)")
+            _req(y.numel() == h.numel(), "y shape")
+        H = h.size(-1)
+        rows = h.numel() // H
+        _req(w.numel() == H and H % 8 == 0 and H <= 16384, "w shape")
+        grouped = self._check_qs(q, s, rows, H)
+        with _DeviceOf(h):
+            _capi.call("lfm2q_add_rmsnorm_q", h.data_ptr(), _ptr(y), w.data_ptr(), q.data_ptr(), s.data_ptr(), rows,
+                       H, float(eps), int(grouped), _stream(h))
+
+    def silu_mul_q(self, g, q, s):
+        """LM prefill: g [rows, 2I] = w1 | w3 outputs -> (q, s) = quant(silu(g1) * g3)."""
+        _check(g, _BF, "g")
+        I = g.size(-1) // 2
+        rows = g.numel() // (2 * I)
+        _req(I % 8 == 0 and I <= 16384, "I shape")
+        grouped = self._check_qs(q, s, rows, I)
+        with _DeviceOf(g):
+            _capi.call("lfm2q_silu_mul_q", g.data_ptr(), q.data_ptr(), s.data_ptr(), rows, I, int(grouped),
+                       _stream(g))
+
+
+class DecodeGemvExt:
+    """The GEMV ops of the reference's lfm2_decode extension."""
+
+    def gemv(self, W, scale, x, y, rows=0):
+        """y [B, N] = x [B, K] @ W^T, W [N, K] BF16 or INT8 (then scale [N] fp32 is required); B >= 1."""
+        if not (x.is_cuda and x.dtype == _BF and x.is_contiguous()):
+            raise RuntimeError("x must be contiguous CUDA bf16")
+        if not (y.is_cuda and y.dtype == _BF and y.is_contiguous()):
+            raise RuntimeError("y must be contiguous CUDA bf16")
+        _req(W.is_cuda and W.is_contiguous() and W.dim() == 2, "W must be a contiguous CUDA matrix")
+        int8 = W.dtype == _I8
+        _req(int8 or W.dtype == _BF, "W must be bf16 or int8")
+        _req(not int8 or (scale is not None and scale.dtype == _F32), "int8 W needs fp32 scale")
+        N, K = W.shape
+        B = x.numel() // K
+        _req(x.numel() == B * K and y.numel() == B * N and B >= 1, "x [B, K], y [B, N]")
+        _req(K % (32 * (16 if int8 else 8)) == 0, "K must be a multiple of 256 (bf16) / 512 (int8)")
+        if scale is not None:
+            _req(scale.is_cuda and scale.is_contiguous() and scale.numel() == N, "scale must be contiguous CUDA [N]")
+        with _DeviceOf(x):
+            _capi.call("lfm2q_gemv", W.data_ptr(), int(int8), _ptr(scale), x.data_ptr(), y.data_ptr(), N, K,
+                       int(rows), B, _stream(x))
+
+    def gemv_epi(self, epi, W, scale, x, y, state=None, cw=None, cbias=None):
+        """Batch-1 GEMV + fused epilogue. epi 0: W = w1|w3 [2S, K] -> y [1, S] = silu(w1 x) * (w3 x);
+        epi 1: W = in_proj [3S, K] -> y [1, S] = shortconv_step(in_proj x), conv state updated in place."""
+        for t, n in ((x, "x"), (y, "y")):
+            if not (t.is_cuda and t.dtype == _BF and t.is_contiguous()):
+                raise RuntimeError(f"{n} must be contiguous CUDA bf16")
+        _req(W.is_cuda and W.is_contiguous() and W.dim() == 2, "W must be a contiguous CUDA matrix")
+        int8 = W.dtype == _I8
+        _req(int8 or W.dtype == _BF, "W must be bf16 or int8")
+        _req(not int8 or (scale is not None and scale.dtype == _F32), "int8 W needs fp32 scale")
+        _req(epi in (0, 1), "epi 0 (swiglu) or 1 (shortconv)")
+        NR = 2 if epi == 0 else 3
+        K = W.size(1)
+        S = W.size(0) // NR
+        _req(W.size(0) == NR * S and x.numel() == K and y.numel() == S, "batch 1: x [1, K], y [1, S]")
+        _req(K % (32 * (16 if int8 else 8)) == 0, "K must be a multiple of 256 (bf16) / 512 (int8)")
+        if epi == 1:
+            _req(state is not None and cw is not None, "shortconv epilogue needs state and conv weight")
+            for t, n in ((state, "(*state)"), (cw, "(*cw)")):
+                if not (t.is_cuda and t.dtype == _BF and t.is_contiguous()):
+                    raise RuntimeError(f"{n} must be contiguous CUDA bf16")
+            _req(state.numel() == S * 3 and cw.numel() == S * 3, "state [1, S, 3], cw [S, 3]")
+            if cbias is not None and not (cbias.is_cuda and cbias.dtype == _BF and cbias.is_contiguous()):
+                raise RuntimeError("(*cbias) must be contiguous CUDA bf16")
+        with _DeviceOf(x):
+            _capi.call("lfm2q_gemv_epi", int(epi), W.data_ptr(), int(int8), _ptr(scale), x.data_ptr(), y.data_ptr(),
+                       S, K, _ptr(state) if epi == 1 else None, _ptr(cw) if epi == 1 else None,
+                       _ptr(cbias) if epi == 1 else None, _stream(x))
+
+    def set_pdl(self, on):
+        """Enable/disable Programmatic Dependent Launch for the GEMV kernels (default on)."""
+        _capi.lib().lfm2q_set_pdl(int(bool(on)))
+
+    def set_gemv_impl(self, impl):
+        """Accepted for compatibility with the reference (0 = staged x, 1 = direct x); this build has one GEMV."""
+        _capi.lib().lfm2q_set_gemv_impl(int(impl))
+
+
+_INT8 = None
+_DEC = None
+
+
+def int8_ext():
+    """INT8 tensor-core GEMMs for prefill and the vision encoder (replaces the reference's JIT-built extension)."""
+    global _INT8
+    if _INT8 is None:
+        _capi.lib()  # fail here, loudly, if the library is missing
+        _INT8 = Int8GemmExt()
+    return _INT8
+
+
+def ext():
+    """Decode GEMV kernels. Programmatic Dependent Launch is on unless LFM2_PDL=0, as in the reference."""
+    global _DEC
+    if _DEC is None:
+        _capi.lib()
+        _DEC = DecodeGemvExt()
+        _DEC.set_pdl(os.environ.get("LFM2_PDL", "1") != "0")
+    return _DEC

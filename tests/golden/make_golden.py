@@ -1,0 +1,186 @@
+"""Generate the golden vectors in tests/golden/ from the reference's own Python code, run on CPU in the build
+container (the reference tree is not present on the GPU box; the vectors travel as committed .npz files).
+
+What is executed from the reference (jainilbavishi24/LFM2.5-VL-Optimization, checked out read-only):
+  * src/lfm2opt/quant.py            quantize_int8 (imported as a module)
+  * tests/test_int8_gemm.py         ref_quant, ref_quant_groups, bf16_ulps, test_quant_rows, test_quant_groups,
+                                    test_i8, test_i8_grouped (function definitions taken from the file's AST)
+  * tests/test_kernels.py           test_gemv (function definition from the AST; its shape list is swapped for
+                                    small shapes so the CPU run stays quick)
+The test functions are executed with dev = "cpu" and with stand-ins for the CUDA extension calls; a `check`
+stand-in captures the reference tensors the test computes (its locals), which become the golden outputs.
+
+    python tests/golden/make_golden.py [--reference /path/to/reference]
+"""
+
+import argparse
+import ast
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+
+
+def load_functions(path: Path, names, replace_lists=None):
+    """Compile the named top-level functions of `path` (optionally with the first list literal of a function
+    replaced) into a code object per function."""
+    tree = ast.parse(path.read_text())
+    out = {}
+    for node in tree.body:
+        if isinstance(node, ast.FunctionDef) and node.name in names:
+            if replace_lists and node.name in replace_lists:
+                new = ast.parse(replace_lists[node.name], mode="eval").body
+
+                class Swap(ast.NodeTransformer):
+                    done = False
+
+                    def visit_List(self, n):
+                        if not Swap.done:
+                            Swap.done = True
+                            return ast.copy_location(new, n)
+                        return n
+
+                node = Swap().visit(node)
+                ast.fix_missing_locations(node)
+            out[node.name] = ast.Module(body=[node], type_ignores=[])
+    missing = set(names) - set(out)
+    if missing:
+        raise RuntimeError(f"functions {missing} not found in {path}")
+    return out
+
+
+def run_in(ns, mod):
+    exec(compile(mod, "<reference>", "exec"), ns)
+
+
+class Capture:
+    """Stand-in for the reference's `check`/`report`: keeps the caller's local tensors."""
+
+    def __init__(self):
+        self.cases = []
+
+    def __call__(self, *args, **kwargs):
+        frame = sys._getframe(1)
+        case = {k: v.clone() if isinstance(v, torch.Tensor) else v for k, v in frame.f_locals.items()}
+        case["_args"] = tuple(v.clone() if isinstance(v, torch.Tensor) else v for v in args)
+        self.cases.append(case)
+
+
+class Stub:
+    """Stand-in for a CUDA extension object: every op is a no-op (the reference values come from the test's own
+    torch expressions, not from the kernel)."""
+
+    def __getattr__(self, name):
+        return lambda *a, **k: None
+
+
+def t2np(t):
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().copy()
+    return t.numpy().copy()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    a = ap.parse_args()
+    ref = Path(a.reference)
+    sys.path.insert(0, str(ref / "src"))
+    import lfm2opt.quant as rq  # the reference's own module
+
+    # ---------------------------------------------------------------- weight quantizer (imported)
+    out = {}
+    g = torch.Generator().manual_seed(0)
+    for i, (N, K) in enumerate([(8, 64), (64, 128), (33, 2048), (16, 1152)]):
+        w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+        if i == 2:
+            w[3] = 0  # an all-zero row: scale clamps to 1e-12
+            w[5, 7] = 0.5  # an outlier
+        q, s = rq.quantize_int8(w)
+        out[f"w{i}"], out[f"q{i}"], out[f"s{i}"] = t2np(w), t2np(q), t2np(s)
+    np.savez_compressed(HERE / "quantize_int8.npz", **out)
+
+    # ---------------------------------------------------------------- activation quantizers + W8A8 (test functions)
+    tests = load_functions(ref / "tests/test_int8_gemm.py",
+                           ["ref_quant", "ref_quant_groups", "bf16_ulps", "test_quant_rows", "test_quant_groups",
+                            "test_i8", "test_i8_grouped"])
+    cap = Capture()
+    ns = {"torch": torch, "F": F, "dev": "cpu", "bf": torch.bfloat16, "E": Stub(), "check": cap,
+          "quantize_int8": rq.quantize_int8}
+    for name, mod in tests.items():
+        run_in(ns, mod)
+    ns["quantize_rows"] = lambda x, group=0: ns["ref_quant_groups"](x) if group else ns["ref_quant"](x)
+
+    torch.manual_seed(0)
+    qr = {}
+    for i, (M, K) in enumerate([(1, 2048), (37, 1152), (5, 128)]):
+        ns["test_quant_rows"](M, K)
+        c = cap.cases[-1]
+        qr[f"x{i}"], qr[f"q{i}"], qr[f"s{i}"] = t2np(c["x"]), t2np(c["rq"]), t2np(c["rs"])
+    for i, (M, K) in enumerate([(1, 2048), (37, 1152), (3, 256)]):
+        ns["test_quant_groups"](M, K)
+        c = cap.cases[-1]
+        qr[f"gx{i}"], qr[f"gq{i}"], qr[f"gs{i}"] = t2np(c["x"]), t2np(c["rq"]), t2np(c["rs"])
+    np.savez_compressed(HERE / "quant_rows.npz", **qr)
+
+    torch.manual_seed(1)
+    gm = {}
+    cases = [(17, 256, 64, False, False), (9, 1152, 128, True, False), (33, 512, 96, True, True),
+             (1, 2048, 64, False, False)]
+    for i, (M, K, N, bias, gelu) in enumerate(cases):
+        ns["test_i8"](M, K, N, bias, gelu)
+        c = cap.cases[-1]
+        gm[f"xq{i}"], gm[f"sx{i}"], gm[f"wq{i}"], gm[f"sw{i}"] = (t2np(c["xq"]), t2np(c["sx"]), t2np(c["wq"]),
+                                                                 t2np(c["sw"]))
+        gm[f"b{i}"] = t2np(c["b"]) if c["b"] is not None else np.zeros(0, np.int16)
+        gm[f"y{i}"] = t2np(c["r"])
+        gm[f"meta{i}"] = np.array([M, K, N, int(bias), int(gelu)])
+    np.savez_compressed(HERE / "gemm_i8.npz", **gm)
+
+    torch.manual_seed(2)
+    gg = {}
+    cases = [(17, 256, 64, False, False), (9, 1152, 128, True, False), (5, 512, 64, True, True)]
+    for i, (M, K, N, bias, gelu) in enumerate(cases):
+        ns["test_i8_grouped"](M, K, N, bias, gelu)
+        c = cap.cases[-1]
+        gg[f"xq{i}"], gg[f"sx{i}"], gg[f"wq{i}"], gg[f"sw{i}"] = (t2np(c["xq"]), t2np(c["sxT"]), t2np(c["wq"]),
+                                                                 t2np(c["sw"]))
+        gg[f"b{i}"] = t2np(c["b"]) if c["b"] is not None else np.zeros(0, np.int16)
+        gg[f"r{i}"] = t2np(c["r"])  # the fp64 reference the test compares against
+        gg[f"meta{i}"] = np.array([M, K, N, int(bias), int(gelu)])
+    np.savez_compressed(HERE / "gemm_i8_grouped.npz", **gg)
+
+    # ---------------------------------------------------------------- decode GEMV (test_kernels.test_gemv)
+    tk = load_functions(ref / "tests/test_kernels.py", ["test_gemv"],
+                        replace_lists={"test_gemv": "[(64, 512), (40, 1024)]"})
+    cap2 = Capture()
+    ns2 = {"torch": torch, "F": F, "dev": "cpu", "bf": torch.bfloat16, "K": Stub(), "report": cap2}
+    run_in(ns2, tk["test_gemv"])
+    torch.manual_seed(3)
+    ns2["test_gemv"]()
+    gv = {}
+    n = 0
+    for c in cap2.cases:
+        name, _, ref_y = c["_args"]
+        if "int4" in name:
+            continue
+        batched = "B=" in name
+        xin = c["xb"] if batched else c["x"]
+        if "int8" in name:
+            W, sc = c["Wq"], c["scale"]
+        else:
+            W, sc = c["W"], None
+        gv[f"name{n}"] = np.array(name)
+        gv[f"W{n}"], gv[f"x{n}"], gv[f"y{n}"] = t2np(W), t2np(xin), t2np(ref_y)
+        gv[f"s{n}"] = t2np(sc) if sc is not None else np.zeros(0, np.float32)
+        n += 1
+    np.savez_compressed(HERE / "gemv.npz", **gv)
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,165 @@
+"""W8A8 tcgen05 GEMMs on the B200 against the oracle.
+
+Per-token: the int32 accumulator is exact and the fp32 epilogue has the reference's operation order, so the bf16
+output must equal the oracle bit for bit (0 ulp); with GELU (tanhf on the GPU, torch's tanh on the CPU) within
+1 bf16 ulp, the reference's own bound (tests/test_int8_gemm.py:174). Grouped: the fp32 fold is restated exactly
+(fmaf per group, in order), so again 0 ulp, and the reference's 1.05x-of-bf16-rounding bound against fp64 holds.
+"""
+
+import pytest
+import torch
+
+import oracle
+from conftest import golden, to_t
+from lfm2opt import _capi
+from lfm2opt.int8 import quantize_rows
+from lfm2opt.kernels import int8_ext
+from lfm2opt.quant import quantize_int8
+
+pytestmark = pytest.mark.gpu
+
+BF = torch.bfloat16
+
+
+def make(M, K, N, bias, seed, outlier_ch=False):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).to(BF)
+    if outlier_ch:
+        x[:, 5 % K] *= 30
+    w = (torch.randn(N, K, generator=g) * 0.02).to(BF)
+    b = torch.randn(N, generator=g).to(BF) if bias else None
+    return x, w, b
+
+
+@pytest.fixture(params=[0, 128, 256], ids=["auto", "bn128", "bn256"])
+def tile(request):
+    _capi.lib().lfm2q_set_gemm_tile(request.param)
+    yield request.param
+    _capi.lib().lfm2q_set_gemm_tile(0)
+
+
+TOKEN_CASES = [(9216, 1152, 3456, True, False), (9216, 1152, 4304, True, True), (2327, 2048, 16384, False, False),
+               (272, 2048, 3072, False, False), (17, 2048, 2048, False, False), (1, 1152, 1152, True, False),
+               (300, 1152, 1152, True, True), (16, 2048, 8192, False, False), (130, 4304, 1152, False, False),
+               (129, 144, 264, True, False), (5, 16, 8, False, False), (4096, 8192, 2048, False, False)]
+
+
+@pytest.mark.parametrize("M,K,N,bias,gelu", TOKEN_CASES)
+def test_gemm_i8_per_token(cuda_dev, tile, M, K, N, bias, gelu):
+    if tile and M * N > 40_000_000:
+        pytest.skip("forced tiles: the automatic run covers the big shapes")
+    x, w, b = make(M, K, N, bias, M + K + N)
+    xq, sx = quantize_rows(x.to(cuda_dev))
+    wq, sw = quantize_int8(w)
+    y = torch.empty(M, N, device=cuda_dev, dtype=BF)
+    int8_ext().gemm_i8(xq, sx, wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y, gelu)
+    r = oracle.gemm_i8_ref(xq.cpu(), sx.cpu(), wq, sw, b, gelu)
+    u = oracle.bf16_ulps(y.cpu(), r)
+    assert u <= (1 if gelu else 0), u
+    assert _capi.lib().lfm2q_check_device(0) == 0
+
+
+def test_gemm_i8_int32_accumulator_exact(cuda_dev):
+    """With unit scales and no bias the output is bf16(float(acc)): the int32 accumulator is checked through it on
+    magnitudes where bf16 is exact (|acc| <= 256) and on the full range through the fp32 rounding."""
+    g = torch.Generator().manual_seed(9)
+    M, K, N = 257, 512, 384
+    xq = torch.randint(-2, 3, (M, K), generator=g, dtype=torch.int8)
+    wq = torch.randint(-1, 2, (N, K), generator=g, dtype=torch.int8)
+    ones_m, ones_n = torch.ones(M), torch.ones(N)
+    y = torch.empty(M, N, device=cuda_dev, dtype=BF)
+    int8_ext().gemm_i8(xq.to(cuda_dev), ones_m.to(cuda_dev), wq.to(cuda_dev), ones_n.to(cuda_dev), None, y, False)
+    acc = oracle.int_mm_exact(xq, wq)
+    small = acc.abs() <= 256
+    assert torch.equal(y.cpu().float()[small], acc.float()[small])
+    assert torch.equal(y.cpu(), acc.float().to(BF))
+
+
+def test_gemm_i8_golden(cuda_dev):
+    d = golden("gemm_i8")
+    for i in range(4):
+        M, K, N, bias, gelu = (int(v) for v in d[f"meta{i}"])
+        b = to_t(d[f"b{i}"], bf16=True).to(cuda_dev) if bias else None
+        y = torch.empty(M, N, device=cuda_dev, dtype=BF)
+        int8_ext().gemm_i8(to_t(d[f"xq{i}"]).to(cuda_dev), to_t(d[f"sx{i}"]).to(cuda_dev),
+                           to_t(d[f"wq{i}"]).to(cuda_dev), to_t(d[f"sw{i}"]).to(cuda_dev), b, y, bool(gelu))
+        u = oracle.bf16_ulps(y.cpu(), to_t(d[f"y{i}"], bf16=True))
+        assert u <= (1 if gelu else 0), (i, u)
+
+
+GROUP_CASES = [(9216, 1152, 3456, True, False), (9216, 4352, 1152, True, False), (2327, 8192, 2048, False, False),
+               (1024, 1152, 4352, True, True), (17, 2048, 2048, False, False), (1, 1152, 1152, True, False),
+               (33, 192, 136, True, False)]
+
+
+@pytest.mark.parametrize("M,K,N,bias,gelu", GROUP_CASES)
+def test_gemm_i8_grouped(cuda_dev, M, K, N, bias, gelu):
+    x, w, b = make(M, K, N, bias, 3 * M + K + N, outlier_ch=True)
+    xq, sxT = quantize_rows(x.to(cuda_dev), 64)
+    wq, sw = quantize_int8(w)
+    y = torch.empty(M, N, device=cuda_dev, dtype=BF)
+    int8_ext().gemm_i8(xq, sxT, wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y, gelu)
+    xq, sxT = xq.cpu(), sxT.cpu()
+    r = oracle.gemm_i8_grouped_ref(xq, sxT, wq, sw, b, gelu)
+    u = oracle.bf16_ulps(y.cpu(), r)
+    assert u <= (1 if gelu else 0), u
+    if M * N <= 4_000_000:  # the reference's own acceptance bound against fp64
+        r64 = oracle.gemm_i8_grouped_f64(xq, sxT, wq, sw, b, gelu)
+        e_ours = ((y.cpu().double() - r64).norm() / r64.norm()).item()
+        e_round = ((r64.to(BF).double() - r64).norm() / r64.norm()).item()
+        assert e_ours <= 1.05 * e_round + 1e-6
+
+
+def test_gemm_i8_grouped_golden(cuda_dev):
+    d = golden("gemm_i8_grouped")
+    for i in range(3):
+        M, K, N, bias, gelu = (int(v) for v in d[f"meta{i}"])
+        b = to_t(d[f"b{i}"], bf16=True) if bias else None
+        y = torch.empty(M, N, device=cuda_dev, dtype=BF)
+        int8_ext().gemm_i8(to_t(d[f"xq{i}"]).to(cuda_dev), to_t(d[f"sx{i}"]).to(cuda_dev),
+                           to_t(d[f"wq{i}"]).to(cuda_dev), to_t(d[f"sw{i}"]).to(cuda_dev),
+                           None if b is None else b.to(cuda_dev), y, bool(gelu))
+        r = to_t(d[f"r{i}"])
+        e_ours = ((y.cpu().double() - r).norm() / r.norm()).item()
+        e_round = ((r.to(BF).double() - r).norm() / r.norm()).item()
+        assert e_ours <= 1.05 * e_round + 1e-6, (i, e_ours, e_round)
+
+
+@pytest.mark.parametrize("M,K,N,bias,gelu", [(9216, 1152, 4352, True, True), (1024, 1152, 4352, True, True),
+                                             (37, 2048, 2048, False, False), (300, 4352, 1152, True, False)])
+def test_gemm_i8_q(cuda_dev, M, K, N, bias, gelu):
+    g = torch.Generator().manual_seed(M + N)
+    x = torch.randn(M, K, generator=g).to(BF)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(BF)
+    b = torch.randn(N, generator=g).to(BF).to(cuda_dev) if bias else None
+    xq, sxT = quantize_rows(x.to(cuda_dev), 64)
+    wq, sw = quantize_int8(w.to(cuda_dev))
+    E = int8_ext()
+    y = torch.empty(M, N, device=cuda_dev, dtype=BF)
+    E.gemm_i8(xq, sxT, wq, sw, b, y, gelu)
+    rq, rs = quantize_rows(y, 64)  # the reference's definition: gemm_i8 -> grouped quant_rows, exactly
+    q, s = torch.empty_like(rq), torch.empty_like(rs)
+    E.gemm_i8_q(xq, sxT, wq, sw, b, q, s, gelu)
+    assert torch.equal(q, rq) and torch.equal(s, rs)
+    if not gelu:
+        oq, os_ = oracle.gemm_i8_q_ref(xq.cpu(), sxT.cpu(), wq.cpu(), sw.cpu(), None if b is None else b.cpu())
+        assert torch.equal(q.cpu(), oq) and torch.equal(s.cpu(), os_)
+
+
+@pytest.mark.parametrize("M,K,I", [(4096, 2048, 8192), (1024, 2048, 8192), (17, 2048, 8192), (300, 1152, 264),
+                                   (1, 64, 8)])
+def test_gemm_i8_silu(cuda_dev, M, K, I):
+    x, w, _ = make(M, K, 2 * I, False, M * 3 + I)
+    xq, sx = quantize_rows(x.to(cuda_dev))
+    wq, sw = quantize_int8(w)
+    y = torch.empty(M, I, device=cuda_dev, dtype=BF)
+    int8_ext().gemm_i8_silu(xq, sx, wq.to(cuda_dev), sw.to(cuda_dev), None, y)
+    r = oracle.gemm_i8_silu_ref(xq.cpu(), sx.cpu(), wq, sw)
+    assert oracle.bf16_ulps(y.cpu(), r) <= 1
+    frac = (y.cpu() != r).float().mean().item()
+    assert frac < 1e-3, frac
+
+
+def test_device_error_word_clear(cuda_dev):
+    torch.cuda.synchronize()
+    assert _capi.lib().lfm2q_check_device(1) == 0

@@ -1,0 +1,141 @@
+"""Decode GEMV on the B200 against the oracle.
+
+The reference's own bound (tests/test_kernels.py:32): max|err| <= 2e-2 * max(max|ref|, 1) against
+F.linear(x.float(), Wq.float() * scale).to(bf16). Tighter here: against the fp64 value, the relative Frobenius error
+stays within 1.05x of the bf16 rounding error of the exact result (fp32 accumulation adds ~1e-6 relative).
+"""
+
+import pytest
+import torch
+
+import oracle
+from conftest import golden, to_t
+from lfm2opt.kernels import ext
+from lfm2opt.quant import quantize_int8
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def check(y, W, s, x):
+    ref = oracle.gemv_ref(W, s, x)
+    err = (y.float() - ref.float()).abs().max().item()
+    assert err <= 2e-2 * max(ref.float().abs().max().item(), 1.0), err
+    r64 = oracle.gemv_f64(W, s, x)
+    e = ((y.double() - r64).norm() / r64.norm()).item()
+    e_round = ((r64.to(BF).double() - r64).norm() / r64.norm()).item()
+    assert e <= 1.05 * e_round + 1e-6, (e, e_round)
+
+
+SHAPES = [(3072, 2048), (6144, 2048), (2048, 2048), (16384, 2048), (2048, 8192), (65536, 2048), (40, 512),
+          (1000, 1536)]
+
+
+@pytest.mark.parametrize("N,K", SHAPES)
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 7, 8, 13, 16, 19])
+def test_gemv_int8(cuda_dev, N, K, B):
+    if N * K > 40_000_000 and B not in (1, 8, 16):
+        pytest.skip("large shape: a few batch sizes suffice")
+    g = torch.Generator().manual_seed(N + K + B)
+    W = (torch.randn(N, K, generator=g) * 0.02).to(BF)
+    Wq, s = quantize_int8(W)
+    x = torch.randn(B, K, generator=g).to(BF)
+    y = torch.empty(B, N, device=cuda_dev, dtype=BF)
+    ext().gemv(Wq.to(cuda_dev), s.to(cuda_dev), x.to(cuda_dev), y)
+    check(y.cpu(), Wq, s, x)
+
+
+@pytest.mark.parametrize("rows", [1, 2, 4, 8])
+def test_gemv_kslices_agree(cuda_dev, rows):
+    """The K-split tuning knob changes only the fp32 summation order."""
+    g = torch.Generator().manual_seed(rows)
+    Wq = torch.randint(-127, 128, (3072, 2048), generator=g, dtype=torch.int8)
+    s = torch.rand(3072, generator=g) * 1e-3
+    x = torch.randn(4, 2048, generator=g).to(BF)
+    y = torch.empty(4, 3072, device=cuda_dev, dtype=BF)
+    ext().gemv(Wq.to(cuda_dev), s.to(cuda_dev), x.to(cuda_dev), y, rows)
+    check(y.cpu(), Wq, s, x)
+
+
+@pytest.mark.parametrize("B", [1, 5])
+def test_gemv_bf16_weights(cuda_dev, B):
+    g = torch.Generator().manual_seed(B)
+    W = (torch.randn(2048, 1024, generator=g) * 0.02).to(BF)
+    x = torch.randn(B, 1024, generator=g).to(BF)
+    y = torch.empty(B, 2048, device=cuda_dev, dtype=BF)
+    ext().gemv(W.to(cuda_dev), None, x.to(cuda_dev), y)
+    check(y.cpu(), W, None, x)
+
+
+def test_gemv_golden(cuda_dev):
+    d = golden("gemv")
+    n = len([k for k in d.files if k.startswith("name")])
+    for i in range(n):
+        name = str(d[f"name{i}"])
+        W = to_t(d[f"W{i}"], bf16="bf16" in name)
+        s = to_t(d[f"s{i}"]) if d[f"s{i}"].size else None
+        x = to_t(d[f"x{i}"], bf16=True)
+        y = torch.empty(x.shape[0], W.shape[0], device=cuda_dev, dtype=BF)
+        ext().gemv(W.to(cuda_dev), None if s is None else s.to(cuda_dev), x.to(cuda_dev), y)
+        ref = to_t(d[f"y{i}"], bf16=True)
+        err = (y.cpu().float() - ref.float()).abs().max().item()
+        assert err <= 2e-2 * max(ref.float().abs().max().item(), 1.0), name
+
+
+@pytest.mark.parametrize("int8", [True, False])
+def test_gemv_epi_swiglu(cuda_dev, int8):
+    """Epilogue 0 equals the plain GEMV's bf16 outputs (same K-slicing) followed by silu_mul (<= 1 bf16 ulp: the
+    GPU uses __expf)."""
+    g = torch.Generator().manual_seed(5)
+    H, I = 2048, 8192
+    x = torch.randn(1, H, generator=g).to(BF).to(cuda_dev)
+    W = (torch.randn(2 * I, H, generator=g) * 0.02).to(BF)
+    s = None
+    if int8:
+        W, s = quantize_int8(W)
+        s = s.to(cuda_dev)
+    W = W.to(cuda_dev)
+    gout = torch.empty(1, 2 * I, device=cuda_dev, dtype=BF)
+    ext().gemv(W, s, x, gout, 4)
+    out = torch.empty(1, I, device=cuda_dev, dtype=BF)
+    ext().gemv_epi(0, W, s, x, out)
+    ref = oracle.gemm.silu_mul_ref(gout.cpu())
+    assert oracle.bf16_ulps(out.cpu(), ref) <= 1
+    assert (out.cpu() != ref).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("int8", [True, False])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_gemv_epi_shortconv(cuda_dev, int8, with_bias):
+    """Epilogue 1 equals the plain GEMV's bf16 outputs followed by the short-conv step, bit for bit, state too."""
+    g = torch.Generator().manual_seed(6)
+    H = 2048
+    x = torch.randn(1, H, generator=g).to(BF).to(cuda_dev)
+    W = (torch.randn(3 * H, H, generator=g) * 0.02).to(BF)
+    s = None
+    if int8:
+        W, s = quantize_int8(W)
+        s = s.to(cuda_dev)
+    W = W.to(cuda_dev)
+    cw = (torch.randn(H, 3, generator=g) * 0.5).to(BF)
+    cb = (torch.randn(H, generator=g) * 0.1).to(BF) if with_bias else None
+    st0 = torch.randn(1, H, 3, generator=g).to(BF)
+    parts = torch.empty(1, 3 * H, device=cuda_dev, dtype=BF)
+    ext().gemv(W, s, x, parts, 2)
+    st = st0.clone().to(cuda_dev)
+    out = torch.empty(1, H, device=cuda_dev, dtype=BF)
+    ext().gemv_epi(1, W, s, x, out, st, cw.to(cuda_dev), None if cb is None else cb.to(cuda_dev))
+    p = parts.cpu().reshape(-1)
+    b_, c_, x_ = p[:H].float(), p[H:2 * H].float(), p[2 * H:].float()
+    bx = (b_ * x_).to(BF).float()
+    s0 = st0.reshape(H, 3).float()
+    wf = cw.float()
+    acc = wf[:, 0] * s0[:, 1]
+    acc = acc + wf[:, 1] * s0[:, 2]
+    acc = acc + wf[:, 2] * bx
+    if cb is not None:
+        acc = acc + cb.float()
+    ref = (c_ * acc.to(BF).float()).to(BF)
+    assert torch.equal(out.cpu().reshape(-1), ref)
+    new_state = torch.stack([s0[:, 1], s0[:, 2], bx], 1).to(BF)
+    assert torch.equal(st.cpu().reshape(H, 3), new_state)
