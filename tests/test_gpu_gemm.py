@@ -21,6 +21,20 @@ pytestmark = pytest.mark.gpu
 BF = torch.bfloat16
 
 
+def assert_close_bf16(y, r, gelu):
+    """0 ulp without GELU. With GELU <= 1 ulp, except in the fp32 cancellation region of 0.5 v (1 + tanh(u)) near
+    tanh = -1 (v < ~ -4.5): there the fp32 value of 1 + tanh is a few units of 2^-24, CUDA's tanhf and the CPU's
+    vectorised tanh may round it differently, and the outputs (|y| < 2e-7) may differ by up to 4e-7 absolute."""
+    if not gelu:
+        assert oracle.bf16_ulps(y, r) == 0
+        return
+    ia, ib = y.view(torch.int16).int(), r.view(torch.int16).int()
+    ia = torch.where(ia < 0, -32768 - ia, ia)
+    ib = torch.where(ib < 0, -32768 - ib, ib)
+    bad = ((ia - ib).abs() > 1) & ((y.float() - r.float()).abs() > 4e-7)
+    assert not bad.any(), (bad.sum().item(), y[bad][:4], r[bad][:4])
+
+
 def make(M, K, N, bias, seed, outlier_ch=False):
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(M, K, generator=g).to(BF)
@@ -54,8 +68,7 @@ def test_gemm_i8_per_token(cuda_dev, tile, M, K, N, bias, gelu):
     y = torch.empty(M, N, device=cuda_dev, dtype=BF)
     int8_ext().gemm_i8(xq, sx, wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y, gelu)
     r = oracle.gemm_i8_ref(xq.cpu(), sx.cpu(), wq, sw, b, gelu)
-    u = oracle.bf16_ulps(y.cpu(), r)
-    assert u <= (1 if gelu else 0), u
+    assert_close_bf16(y.cpu(), r, gelu)
     assert _capi.lib().lfm2q_check_device(0) == 0
 
 
@@ -83,8 +96,7 @@ def test_gemm_i8_golden(cuda_dev):
         y = torch.empty(M, N, device=cuda_dev, dtype=BF)
         int8_ext().gemm_i8(to_t(d[f"xq{i}"]).to(cuda_dev), to_t(d[f"sx{i}"]).to(cuda_dev),
                            to_t(d[f"wq{i}"]).to(cuda_dev), to_t(d[f"sw{i}"]).to(cuda_dev), b, y, bool(gelu))
-        u = oracle.bf16_ulps(y.cpu(), to_t(d[f"y{i}"], bf16=True))
-        assert u <= (1 if gelu else 0), (i, u)
+        assert_close_bf16(y.cpu(), to_t(d[f"y{i}"], bf16=True), gelu)
 
 
 GROUP_CASES = [(9216, 1152, 3456, True, False), (9216, 4352, 1152, True, False), (2327, 8192, 2048, False, False),
@@ -101,8 +113,7 @@ def test_gemm_i8_grouped(cuda_dev, M, K, N, bias, gelu):
     int8_ext().gemm_i8(xq, sxT, wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y, gelu)
     xq, sxT = xq.cpu(), sxT.cpu()
     r = oracle.gemm_i8_grouped_ref(xq, sxT, wq, sw, b, gelu)
-    u = oracle.bf16_ulps(y.cpu(), r)
-    assert u <= (1 if gelu else 0), u
+    assert_close_bf16(y.cpu(), r, gelu)
     if M * N <= 4_000_000:  # the reference's own acceptance bound against fp64
         r64 = oracle.gemm_i8_grouped_f64(xq, sxT, wq, sw, b, gelu)
         e_ours = ((y.cpu().double() - r64).norm() / r64.norm()).item()

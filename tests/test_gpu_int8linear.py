@@ -27,7 +27,8 @@ def test_int8linear_a8(cuda_dev, group, gelu):
     else:
         xq, sx = oracle.quant_rows_ref(x2)
         r = oracle.gemm_i8_ref(xq, sx, lin.q.cpu(), lin.s.cpu(), b, gelu)
-    assert oracle.bf16_ulps(y.reshape(-1, 4304).cpu(), r) <= (1 if gelu else 0)
+    from test_gpu_gemm import assert_close_bf16
+    assert_close_bf16(y.reshape(-1, 4304).cpu(), r, gelu)
 
 
 def test_int8linear_quant_out_chain(cuda_dev):
