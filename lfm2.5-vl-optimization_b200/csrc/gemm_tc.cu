@@ -27,6 +27,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -135,6 +136,28 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Wait for this thread's TMEM loads with the destination registers tied to the wait, so no use of them can be
+// scheduled before it.
+__device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]),
+        "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]),
+        "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+        "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -149,8 +172,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
-__device__ __forceinline__ float gelu_tanh(float v) {  // F.gelu(v, approximate="tanh")
-  return 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+// F.gelu(v, approximate="tanh") = 0.5 v (1 + tanh(u)), u = sqrt(2/pi) (v + 0.044715 v^3), evaluated as the equal
+// v / (1 + exp(-2u)): no cancellation near tanh = -1, one exponential and one reciprocal per element.
+__device__ __forceinline__ float gelu_tanh(float v) {
+  const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  return __fdividef(v, 1.f + __expf(-2.f * u));
 }
 // exact (float)v for |v| < 2^22: add into the mantissa of 1.5 * 2^23 and subtract it again
 __device__ __forceinline__ float i2f_small(int v) { return __int_as_float(v + 0x4B400000) - 12582912.f; }
@@ -183,8 +209,15 @@ struct Smem {
   static constexpr int BAR_OFF = B_OFF + STAGES * B_BYTES;
   static constexpr int NBARS = 2 * STAGES + 8;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
-  static constexpr int BYTES = MISC_OFF + 16;
+  // epilogue: per-warp staging of the tile's weight scales and bias (2 x 256 fp32 per warp)
+  static constexpr int PAR_OFF = ((MISC_OFF + 16 + 1023) / 1024) * 1024;
+  static constexpr int PAR_FLOATS = 512;
+  // epilogue: per-warp double-buffered 32 x 32 bf16 output blocks (64-byte rows, 64-byte swizzle) for TMA stores
+  static constexpr int OUT_OFF = PAR_OFF + 4 * PAR_FLOATS * 4;
+  static constexpr int OUT_BLOCK = 32 * 64;
+  static constexpr int BYTES = OUT_OFF + 4 * 2 * OUT_BLOCK;
   static constexpr int ALLOC = BYTES + 1024;  // room to align the base to 1024
+  static_assert(ALLOC <= 232448, "shared memory per block");
 };
 
 // ------------------------------------------------------------------ epilogue helpers
@@ -220,7 +253,7 @@ __device__ __forceinline__ void load8b(const bf16 *p, float (&v)[8]) {
 template <int BN, int STAGES, int NACC, int EPI, bool GELU>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmY, const GemmArgs args) {
   using L = Smem<BN, STAGES>;
   constexpr bool GROUPED = (EPI == EPI_GROUP || EPI == EPI_GROUP_Q);
   constexpr int TMEM_COLS = NACC * BN;
@@ -361,68 +394,110 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue warps 2..5
+    const int ew = warp - 2;          // epilogue warp 0..3
     const int q = warp & 3;           // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;    // tile row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * L::PAR_FLOATS;  // [256] weight scales
+    float *par_b = par_sw + 256;                                                           // [256] bias
+    const uint32_t out_base = sbase + L::OUT_OFF + ew * 2 * L::OUT_BLOCK;
+    uint32_t out_count = 0;  // 32 x 32 blocks this warp has handed to the TMA engine
     int acc = 0;
     uint32_t aphase = 0;
+
+    // Stage this tile's per-column epilogue parameters in the warp's shared memory (issued before the accumulator
+    // wait, so the loads overlap the MMAs). Entry i is output column n0 + i (SILU: i < 128 gate, i >= 128 up).
+    auto stage_params = [&](int n0, int width, bool silu) {
+      __syncwarp();
+      for (int i = lane; i < (silu ? 256 : width); i += 32) {
+        const int oc = silu ? (i & 127) : i;
+        const int col = silu ? (i < 128 ? n0 + oc : args.Nout + n0 + oc) : n0 + i;
+        const bool ok = n0 + oc < args.Nout;
+        par_sw[i] = ok ? __ldg(args.sb + col) : 0.f;
+        par_b[i] = (ok && args.bias) ? bf2f(args.bias[col]) : 0.f;
+      }
+      __syncwarp();
+    };
+    // Hand a 32 x 32 bf16 block (this lane's row: 16 packed words) to the TMA engine at (column x, row y).
+    auto store_block = [&](const uint32_t (&o)[16], int x, int y) {
+      const uint32_t buf = out_base + (out_count & 1) * L::OUT_BLOCK;
+      if (lane == 0) bulk_wait_read1();  // the buffer's previous store has finished reading it
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t addr = buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(o[4 * j]), "r"(o[4 * j + 1]),
+                     "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tmY, buf, x, y);
+        bulk_commit();
+      }
+      ++out_count;
+    };
+
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int mt, nt;
       tile_coord(tile, args, mt, nt);
       const int m = mt * TM + row;
       const bool mrow = m < M;
+      const int yrow = mt * TM + q * 32;  // first output row of this warp's blocks
       if (!GROUPED) {
-        const int OUTW = (EPI == EPI_SILU) ? BN / 2 : BN;  // output columns per tile
+        constexpr int OUTW = (EPI == EPI_SILU) ? BN / 2 : BN;  // output columns per tile
+        constexpr int NCH = OUTW / 32;
         const int n0 = nt * OUTW;
         const float sxm = mrow ? __ldg(args.sa + m) : 0.f;
+        stage_params(n0, OUTW, EPI == EPI_SILU);
         if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
         tc_fence_after();
         const uint32_t tb = tmem_base + lane_addr + acc * BN;
-#pragma unroll 1
-        for (int c = 0; c < OUTW; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tb + c, r);
-          uint32_t ru[32];
-          if (EPI == EPI_SILU) tmem_ld32(tb + BN / 2 + c, ru);
-          tmem_wait_ld();
-          const int nb = n0 + c;
-          if (mrow) {
+        uint32_t r[2][32], ru[2][32];
+        tmem_ld32(tb, r[0]);
+        if (EPI == EPI_SILU) tmem_ld32(tb + BN / 2, ru[0]);
+        tmem_wait_tie(r[0]);
+        if (EPI == EPI_SILU) tmem_wait_tie(ru[0]);
 #pragma unroll
-            for (int j8 = 0; j8 < 32; j8 += 8) {
-              const int n = nb + j8;
-              if (n >= args.Nout) break;
-              float sw[8], bb[8];
-              load8f(args.sb + n, sw);
-              load8b(args.bias ? args.bias + n : nullptr, bb);
-              uint32_t o[4];
-              if (EPI == EPI_SILU) {
-                float swu[8], bu[8];
-                load8f(args.sb + args.Nout + n, swu);
-                load8b(args.bias ? args.bias + args.Nout + n : nullptr, bu);
+        for (int c = 0; c < NCH; ++c) {
+          const int cur = c & 1, nxt = cur ^ 1;
+          if (c + 1 < NCH) {
+            tmem_ld32(tb + (c + 1) * 32, r[nxt]);
+            if (EPI == EPI_SILU) tmem_ld32(tb + BN / 2 + (c + 1) * 32, ru[nxt]);
+          } else {
+            // every column of this accumulator is in registers: let the MMA warp reuse it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty(acc));
+          }
+          uint32_t o[16];
 #pragma unroll
-                for (int j = 0; j < 8; j += 2) {
-                  float out[2];
+          for (int j = 0; j < 32; j += 2) {
+            const int i = c * 32 + j;
+            float v0, v1;
+            if (EPI == EPI_SILU) {
+              float out[2];
 #pragma unroll
-                  for (int h = 0; h < 2; ++h) {
-                    const float g = rbf(epi_token<false>((int)r[j8 + j + h], sxm, sw[j + h], bb[j + h]));
-                    const float u = rbf(epi_token<false>((int)ru[j8 + j + h], sxm, swu[j + h], bu[j + h]));
-                    out[h] = rbf(g / (1.f + __expf(-g))) * u;
-                  }
-                  o[j / 2] = pack_bf16x2(out[0], out[1]);
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 8; j += 2)
-                  o[j / 2] = pack_bf16x2(epi_token<GELU>((int)r[j8 + j], sxm, sw[j], bb[j]),
-                                         epi_token<GELU>((int)r[j8 + j + 1], sxm, sw[j + 1], bb[j + 1]));
+              for (int h = 0; h < 2; ++h) {
+                const float g = rbf(epi_token<false>((int)r[cur][j + h], sxm, par_sw[i + h], par_b[i + h]));
+                const float u = rbf(epi_token<false>((int)ru[cur][j + h], sxm, par_sw[128 + i + h], par_b[128 + i + h]));
+                out[h] = rbf(g / (1.f + __expf(-g))) * u;
               }
-              *reinterpret_cast<uint4 *>(args.Y + (size_t)m * args.Nout + n) = make_uint4(o[0], o[1], o[2], o[3]);
+              v0 = out[0];
+              v1 = out[1];
+            } else {
+              v0 = epi_token<GELU>((int)r[cur][j], sxm, par_sw[i], par_b[i]);
+              v1 = epi_token<GELU>((int)r[cur][j + 1], sxm, par_sw[i + 1], par_b[i + 1]);
             }
+            o[j / 2] = pack_bf16x2(v0, v1);
+          }
+          store_block(o, n0 + c * 32, yrow);
+          if (c + 1 < NCH) {
+            tmem_wait_tie(r[nxt]);
+            if (EPI == EPI_SILU) tmem_wait_tie(ru[nxt]);
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_tempty(acc));
         if (++acc == NACC) {
           acc = 0;
           aphase ^= 1;
@@ -430,6 +505,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       } else {
         // grouped: fold every 64-wide K group into fp32 running sums held in registers (128 columns per row)
         const int n0 = nt * BN;
+        stage_params(n0, BN, false);
         float f[BN];
 #pragma unroll
         for (int j = 0; j < BN; ++j) f[j] = 0.f;
@@ -448,7 +524,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t r0[32], r1[32];
             tmem_ld32(tb + c, r0);
             tmem_ld32(tb + c + 32, r1);
-            tmem_wait_ld();
+            tmem_wait_tie(r0);
+            tmem_wait_tie(r1);
 #pragma unroll
             for (int j = 0; j < 32; ++j) f[c + j] = __fmaf_rn(i2f_small((int)r0[j]), s, f[c + j]);
 #pragma unroll
@@ -464,47 +541,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (g + 1 < G) s_next = mrow ? __ldg(args.sa + (size_t)(g + 1) * M + m) : 0.f;
         }
         if (!ok) break;
-        if (!mrow) continue;
         if (EPI == EPI_GROUP) {
 #pragma unroll
-          for (int j8 = 0; j8 < BN; j8 += 8) {
-            const int n = n0 + j8;
-            if (n >= args.Nout) break;
-            float sw[8], bb[8];
-            load8f(args.sb + n, sw);
-            load8b(args.bias ? args.bias + n : nullptr, bb);
-            uint32_t o[4];
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t o[16];
 #pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-              float y0 = __fadd_rn(__fmul_rn(f[j8 + j], sw[j]), bb[j]);
-              float y1 = __fadd_rn(__fmul_rn(f[j8 + j + 1], sw[j + 1]), bb[j + 1]);
+            for (int j = 0; j < 32; j += 2) {
+              float y0 = __fadd_rn(__fmul_rn(f[c + j], par_sw[c + j]), par_b[c + j]);
+              float y1 = __fadd_rn(__fmul_rn(f[c + j + 1], par_sw[c + j + 1]), par_b[c + j + 1]);
               if (GELU) {
                 y0 = gelu_tanh(y0);
                 y1 = gelu_tanh(y1);
               }
               o[j / 2] = pack_bf16x2(y0, y1);
             }
-            *reinterpret_cast<uint4 *>(args.Y + (size_t)m * args.Nout + n) = make_uint4(o[0], o[1], o[2], o[3]);
+            store_block(o, n0 + c, yrow);
           }
-        } else {
+        } else if (mrow) {
           // QOUT: bf16-round the outputs, then one scale per (row, 64 columns); N % 128 == 0 (whole tiles)
 #pragma unroll
           for (int h = 0; h < BN / 64; ++h) {
             float amax = 0.f;
 #pragma unroll
-            for (int j8 = 0; j8 < 64; j8 += 8) {
-              const int n = n0 + h * 64 + j8;
-              float sw[8], bb[8];
-              load8f(args.sb + n, sw);
-              load8b(args.bias ? args.bias + n : nullptr, bb);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float y = __fadd_rn(__fmul_rn(f[h * 64 + j8 + j], sw[j]), bb[j]);
-                if (GELU) y = gelu_tanh(y);
-                y = rbf(y);
-                f[h * 64 + j8 + j] = y;
-                amax = fmaxf(amax, fabsf(y));
-              }
+            for (int j = 0; j < 64; ++j) {
+              float y = __fadd_rn(__fmul_rn(f[h * 64 + j], par_sw[h * 64 + j]), par_b[h * 64 + j]);
+              if (GELU) y = gelu_tanh(y);
+              y = rbf(y);
+              f[h * 64 + j] = y;
+              amax = fmaxf(amax, fabsf(y));
             }
             const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
             args.YsT[(size_t)((n0 >> 6) + h) * M + m] = sc;
@@ -525,6 +589,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_all();  // every TMA store of this warp has completed
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -548,6 +614,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   });
   return fn;
+}
+
+// bf16 output [rows, cols] row-major, stored in 32 x 32 blocks from 64-byte-swizzled shared memory; rows / columns
+// beyond the matrix are clipped by the copy engine
+bool make_out_map(CUtensorMap *map, const void *ptr, int cols, int rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 // 2-D int8 matrix [rows, inner] row-major, box = 128 bytes x box_rows, 128-byte swizzle, OOB reads as zero
@@ -578,12 +659,17 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ty;
   const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN;
   if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, box_b)) return cudaErrorInvalidValue;
+  if (EPI == EPI_GROUP_Q) {
+    memset(&ty, 0, sizeof(ty));  // int8 output: written with plain stores, the map is unused
+  } else if (!make_out_map(&ty, a.Y, a.Nout, a.M)) {
+    return cudaErrorInvalidValue;
+  }
   const int tiles = a.tiles_m * a.tiles_n;
   const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
-  kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, a);
+  kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, ty, a);
   return cudaGetLastError();
 }
 
