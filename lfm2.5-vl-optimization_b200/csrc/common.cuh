@@ -32,6 +32,23 @@ __device__ __forceinline__ int q8(float v, float sc) {
   return max(-127, min(127, q));
 }
 
+// The same code without a division per element (rinv = 1 / sc, IEEE). For |v / sc| <= 127.5 the estimate
+// t = v * rinv lies within 2.3e-5 of the IEEE quotient, so both round to the same integer unless t is within that
+// distance of a half-integer; only then (a few elements in 10^4) is the quotient divided out exactly. Rounding to
+// an integer is an add of 1.5 * 2^23 (ties to even), and the integer is read from the sum's bits.
+__device__ __forceinline__ int q8r(float v, float sc, float rinv) {
+  const float big = 12582912.f;
+  const float t = __fmul_rn(v, rinv);
+  float tb = __fadd_rn(t, big);
+  if (fabsf(__fsub_rn(t, __fsub_rn(tb, big))) > 0.49996f) tb = __fadd_rn(rintf(__fdiv_rn(v, sc)), big);
+  return max(-127, min(127, __float_as_int(tb) - 0x4B400000));
+}
+
+// four int8 codes -> one word (byte 0 = a)
+__device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 // ------------------------------------------------------------------ streaming loads
 // 16-byte read-only load that does not allocate in L1: weights are read exactly once per launch.
 __device__ __forceinline__ uint4 ld_stream16(const void *p) {

@@ -41,7 +41,8 @@ namespace {
 
 constexpr int TM = 128;        // output rows per tile (UMMA M, one TMEM lane per row)
 constexpr int TK = 128;        // K bytes per pipeline stage: one 128-byte swizzle row
-constexpr int NTHREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (2 per TMEM lane quarter)
+constexpr int EPI_WARPS = 8;
 constexpr long long WAIT_LIMIT = 1ll << 31;
 
 struct GemmArgs {
@@ -209,13 +210,13 @@ struct Smem {
   static constexpr int BAR_OFF = B_OFF + STAGES * B_BYTES;
   static constexpr int NBARS = 2 * STAGES + 8;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
-  // epilogue: per-warp staging of the tile's weight scales and bias (2 x 256 fp32 per warp)
+  // epilogue: per-warp staging of its columns' weight scales and bias (2 x 128 fp32 per warp)
   static constexpr int PAR_OFF = ((MISC_OFF + 16 + 1023) / 1024) * 1024;
-  static constexpr int PAR_FLOATS = 512;
-  // epilogue: per-warp double-buffered 32 x 32 bf16 output blocks (64-byte rows, 64-byte swizzle) for TMA stores
-  static constexpr int OUT_OFF = PAR_OFF + 4 * PAR_FLOATS * 4;
-  static constexpr int OUT_BLOCK = 32 * 64;
-  static constexpr int BYTES = OUT_OFF + 4 * 2 * OUT_BLOCK;
+  static constexpr int PAR_FLOATS = 256;
+  // epilogue: per-warp double-buffered 32 x 16 bf16 output blocks (32-byte rows, 32-byte swizzle) for TMA stores
+  static constexpr int OUT_OFF = PAR_OFF + EPI_WARPS * PAR_FLOATS * 4;
+  static constexpr int OUT_BLOCK = 32 * 32;
+  static constexpr int BYTES = OUT_OFF + EPI_WARPS * 2 * OUT_BLOCK;
   static constexpr int ALLOC = BYTES + 1024;  // room to align the base to 1024
   static_assert(ALLOC <= 232448, "shared memory per block");
 };
@@ -285,7 +286,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int a = 0; a < 4; ++a) {
       mbar_init(bar_tfull(a), 1);
-      mbar_init(bar_tempty(a), 4);  // one arrival per epilogue warp
+      mbar_init(bar_tempty(a), EPI_WARPS);  // one arrival per epilogue warp
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -393,39 +394,41 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mma_done:;
     }
   } else {
-    // ---------------------------------------------------------------- epilogue warps 2..5
-    const int ew = warp - 2;          // epilogue warp 0..3
+    // ---------------------------------------------------------------- epilogue warps 2..9
+    // Warp w reads TMEM lane quarter w % 4 (tile rows 32q..32q+31) and owns one half of the tile's output columns.
+    const int ew = warp - 2;          // epilogue warp 0..7
     const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const int half = ew >> 2;         // which half of the columns
     const int row = q * 32 + lane;    // tile row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * L::PAR_FLOATS;  // [256] weight scales
-    float *par_b = par_sw + 256;                                                           // [256] bias
+    float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * L::PAR_FLOATS;  // [128] weight scales
+    float *par_b = par_sw + 128;                                                           // [128] bias
     const uint32_t out_base = sbase + L::OUT_OFF + ew * 2 * L::OUT_BLOCK;
-    uint32_t out_count = 0;  // 32 x 32 blocks this warp has handed to the TMA engine
+    uint32_t out_count = 0;  // 32 x 16 blocks this warp has handed to the TMA engine
     int acc = 0;
     uint32_t aphase = 0;
 
-    // Stage this tile's per-column epilogue parameters in the warp's shared memory (issued before the accumulator
-    // wait, so the loads overlap the MMAs). Entry i is output column n0 + i (SILU: i < 128 gate, i >= 128 up).
-    auto stage_params = [&](int n0, int width, bool silu) {
+    // Stage the per-column epilogue parameters of this warp's columns (issued before the accumulator wait, so the
+    // loads overlap the MMAs). Entry i: output column c0 + i; with `silu`, entries 64.. hold the up rows.
+    auto stage_params = [&](int c0, int width, bool silu) {
       __syncwarp();
-      for (int i = lane; i < (silu ? 256 : width); i += 32) {
-        const int oc = silu ? (i & 127) : i;
-        const int col = silu ? (i < 128 ? n0 + oc : args.Nout + n0 + oc) : n0 + i;
-        const bool ok = n0 + oc < args.Nout;
+      for (int i = lane; i < (silu ? 2 * width : width); i += 32) {
+        const int oc = c0 + (silu ? (i % width) : i);
+        const int col = (silu && i >= width) ? args.Nout + oc : oc;
+        const bool ok = oc < args.Nout;
         par_sw[i] = ok ? __ldg(args.sb + col) : 0.f;
         par_b[i] = (ok && args.bias) ? bf2f(args.bias[col]) : 0.f;
       }
       __syncwarp();
     };
-    // Hand a 32 x 32 bf16 block (this lane's row: 16 packed words) to the TMA engine at (column x, row y).
-    auto store_block = [&](const uint32_t (&o)[16], int x, int y) {
+    // Hand a 32-row x 16-column bf16 block (this lane's row: 8 packed words) to the TMA engine at (column x, row y).
+    auto store_block = [&](const uint32_t *o, int x, int y) {
       const uint32_t buf = out_base + (out_count & 1) * L::OUT_BLOCK;
       if (lane == 0) bulk_wait_read1();  // the buffer's previous store has finished reading it
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t addr = buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t addr = buf + lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(o[4 * j]), "r"(o[4 * j + 1]),
                      "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
                      : "memory");
@@ -438,6 +441,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       ++out_count;
     };
+    auto release_acc = [&]() {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_tempty(acc));
+      if (++acc == NACC) {
+        acc = 0;
+        aphase ^= 1;
+      }
+    };
 
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int mt, nt;
@@ -445,70 +457,76 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int m = mt * TM + row;
       const bool mrow = m < M;
       const int yrow = mt * TM + q * 32;  // first output row of this warp's blocks
-      if (!GROUPED) {
-        constexpr int OUTW = (EPI == EPI_SILU) ? BN / 2 : BN;  // output columns per tile
-        constexpr int NCH = OUTW / 32;
-        const int n0 = nt * OUTW;
+      if (EPI == EPI_TOKEN) {
+        constexpr int CW = BN / 2, NCH = CW / 32;  // this warp's columns
+        const int c0 = nt * BN + half * CW;
         const float sxm = mrow ? __ldg(args.sa + m) : 0.f;
-        stage_params(n0, OUTW, EPI == EPI_SILU);
+        stage_params(c0, CW, false);
         if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
         tc_fence_after();
-        const uint32_t tb = tmem_base + lane_addr + acc * BN;
-        uint32_t r[2][32], ru[2][32];
+        const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
+        uint32_t r[2][32];
         tmem_ld32(tb, r[0]);
-        if (EPI == EPI_SILU) tmem_ld32(tb + BN / 2, ru[0]);
         tmem_wait_tie(r[0]);
-        if (EPI == EPI_SILU) tmem_wait_tie(ru[0]);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           const int cur = c & 1, nxt = cur ^ 1;
-          if (c + 1 < NCH) {
-            tmem_ld32(tb + (c + 1) * 32, r[nxt]);
-            if (EPI == EPI_SILU) tmem_ld32(tb + BN / 2 + (c + 1) * 32, ru[nxt]);
-          } else {
-            // every column of this accumulator is in registers: let the MMA warp reuse it
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty(acc));
-          }
+          if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, r[nxt]);
+          else release_acc();  // every column of this warp is in registers
+          uint32_t o[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2)
+            o[j / 2] = pack_bf16x2(epi_token<GELU>((int)r[cur][j], sxm, par_sw[c * 32 + j], par_b[c * 32 + j]),
+                                   epi_token<GELU>((int)r[cur][j + 1], sxm, par_sw[c * 32 + j + 1],
+                                                   par_b[c * 32 + j + 1]));
+          store_block(o, c0 + c * 32, yrow);
+          store_block(o + 8, c0 + c * 32 + 16, yrow);
+          if (c + 1 < NCH) tmem_wait_tie(r[nxt]);
+        }
+      } else if (EPI == EPI_SILU) {
+        constexpr int CW = BN / 4;  // 64 output columns per warp: gate TMEM columns [CW*half..), up [BN/2 + ..)
+        const int c0 = nt * (BN / 2) + half * CW;
+        const float sxm = mrow ? __ldg(args.sa + m) : 0.f;
+        stage_params(c0, CW, true);
+        if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
+        uint32_t rg[2][32], ru[2][32];
+        tmem_ld32(tb, rg[0]);
+        tmem_ld32(tb + 32, rg[1]);
+        tmem_ld32(tb + BN / 2, ru[0]);
+        tmem_ld32(tb + BN / 2 + 32, ru[1]);
+        tmem_wait_tie(rg[0]);
+        tmem_wait_tie(rg[1]);
+        tmem_wait_tie(ru[0]);
+        tmem_wait_tie(ru[1]);
+        release_acc();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const int i = c * 32 + j;
-            float v0, v1;
-            if (EPI == EPI_SILU) {
-              float out[2];
+            float out[2];
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float g = rbf(epi_token<false>((int)r[cur][j + h], sxm, par_sw[i + h], par_b[i + h]));
-                const float u = rbf(epi_token<false>((int)ru[cur][j + h], sxm, par_sw[128 + i + h], par_b[128 + i + h]));
-                out[h] = rbf(g / (1.f + __expf(-g))) * u;
-              }
-              v0 = out[0];
-              v1 = out[1];
-            } else {
-              v0 = epi_token<GELU>((int)r[cur][j], sxm, par_sw[i], par_b[i]);
-              v1 = epi_token<GELU>((int)r[cur][j + 1], sxm, par_sw[i + 1], par_b[i + 1]);
+            for (int h = 0; h < 2; ++h) {
+              const int i = c * 32 + j + h;
+              const float g = rbf(epi_token<false>((int)rg[c][j + h], sxm, par_sw[i], par_b[i]));
+              const float u = rbf(epi_token<false>((int)ru[c][j + h], sxm, par_sw[CW + i], par_b[CW + i]));
+              out[h] = rbf(__fdividef(g, 1.f + __expf(-g))) * u;
             }
-            o[j / 2] = pack_bf16x2(v0, v1);
+            o[j / 2] = pack_bf16x2(out[0], out[1]);
           }
-          store_block(o, n0 + c * 32, yrow);
-          if (c + 1 < NCH) {
-            tmem_wait_tie(r[nxt]);
-            if (EPI == EPI_SILU) tmem_wait_tie(ru[nxt]);
-          }
-        }
-        if (++acc == NACC) {
-          acc = 0;
-          aphase ^= 1;
+          store_block(o, c0 + c * 32, yrow);
+          store_block(o + 8, c0 + c * 32 + 16, yrow);
         }
       } else {
-        // grouped: fold every 64-wide K group into fp32 running sums held in registers (128 columns per row)
-        const int n0 = nt * BN;
-        stage_params(n0, BN, false);
-        float f[BN];
+        // grouped: fold every 64-wide K group into fp32 running sums held in registers (64 columns per warp)
+        constexpr int CW = BN / 2;
+        const int c0 = nt * BN + half * CW;
+        stage_params(c0, CW, false);
+        float f[CW];
 #pragma unroll
-        for (int j = 0; j < BN; ++j) f[j] = 0.f;
+        for (int j = 0; j < CW; ++j) f[j] = 0.f;
         float s_next = (mrow && G > 0) ? __ldg(args.sa + m) : 0.f;
         bool ok = true;
         for (int g = 0; g < G; ++g) {
@@ -518,35 +536,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t tb = tmem_base + lane_addr + acc * BN;
-#pragma unroll
-          for (int c = 0; c < BN; c += 64) {
-            uint32_t r0[32], r1[32];
-            tmem_ld32(tb + c, r0);
-            tmem_ld32(tb + c + 32, r1);
-            tmem_wait_tie(r0);
-            tmem_wait_tie(r1);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[c + j] = __fmaf_rn(i2f_small((int)r0[j]), s, f[c + j]);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[c + 32 + j] = __fmaf_rn(i2f_small((int)r1[j]), s, f[c + 32 + j]);
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty(acc));
-          if (++acc == NACC) {
-            acc = 0;
-            aphase ^= 1;
-          }
+          const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tb, r0);
+          tmem_ld32(tb + 32, r1);
+          tmem_wait_tie(r0);
+          tmem_wait_tie(r1);
+          release_acc();
           if (g + 1 < G) s_next = mrow ? __ldg(args.sa + (size_t)(g + 1) * M + m) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __fmaf_rn(i2f_small((int)r0[j]), s, f[j]);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[32 + j] = __fmaf_rn(i2f_small((int)r1[j]), s, f[32 + j]);
         }
         if (!ok) break;
         if (EPI == EPI_GROUP) {
 #pragma unroll
-          for (int c = 0; c < BN; c += 32) {
-            uint32_t o[16];
+          for (int c = 0; c < CW; c += 16) {
+            uint32_t o[8];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
+            for (int j = 0; j < 16; j += 2) {
               float y0 = __fadd_rn(__fmul_rn(f[c + j], par_sw[c + j]), par_b[c + j]);
               float y1 = __fadd_rn(__fmul_rn(f[c + j + 1], par_sw[c + j + 1]), par_b[c + j + 1]);
               if (GELU) {
@@ -555,36 +564,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               }
               o[j / 2] = pack_bf16x2(y0, y1);
             }
-            store_block(o, n0 + c, yrow);
+            store_block(o, c0 + c, yrow);
           }
         } else if (mrow) {
-          // QOUT: bf16-round the outputs, then one scale per (row, 64 columns); N % 128 == 0 (whole tiles)
+          // QOUT: bf16-round the outputs, then one scale per (row, 64 columns): this warp's 64 columns are one
+          // group (N % 128 == 0, whole tiles)
+          float amax = 0.f;
 #pragma unroll
-          for (int h = 0; h < BN / 64; ++h) {
-            float amax = 0.f;
+          for (int j = 0; j < CW; ++j) {
+            float y = __fadd_rn(__fmul_rn(f[j], par_sw[j]), par_b[j]);
+            if (GELU) y = gelu_tanh(y);
+            y = rbf(y);
+            f[j] = y;
+            amax = fmaxf(amax, fabsf(y));
+          }
+          const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
+          const float rinv = __frcp_rn(sc);
+          args.YsT[(size_t)(c0 >> 6) * M + m] = sc;
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-              float y = __fadd_rn(__fmul_rn(f[h * 64 + j], par_sw[h * 64 + j]), par_b[h * 64 + j]);
-              if (GELU) y = gelu_tanh(y);
-              y = rbf(y);
-              f[h * 64 + j] = y;
-              amax = fmaxf(amax, fabsf(y));
-            }
-            const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
-            args.YsT[(size_t)((n0 >> 6) + h) * M + m] = sc;
+          for (int j16 = 0; j16 < CW; j16 += 16) {
+            uint32_t w[4];
 #pragma unroll
-            for (int j16 = 0; j16 < 64; j16 += 16) {
-              uint32_t w[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int b0 = q8(f[h * 64 + j16 + 4 * i + 0], sc), b1 = q8(f[h * 64 + j16 + 4 * i + 1], sc);
-                const int b2 = q8(f[h * 64 + j16 + 4 * i + 2], sc), b3 = q8(f[h * 64 + j16 + 4 * i + 3], sc);
-                w[i] = (uint32_t)(b0 & 0xFF) | ((uint32_t)(b1 & 0xFF) << 8) | ((uint32_t)(b2 & 0xFF) << 16) |
-                       ((uint32_t)(b3 & 0xFF) << 24);
-              }
-              *reinterpret_cast<uint4 *>(args.Yq + (size_t)m * args.Nout + n0 + h * 64 + j16) =
-                  make_uint4(w[0], w[1], w[2], w[3]);
-            }
+            for (int i = 0; i < 4; ++i)
+              w[i] = pack_i8x4(q8r(f[j16 + 4 * i + 0], sc, rinv), q8r(f[j16 + 4 * i + 1], sc, rinv),
+                               q8r(f[j16 + 4 * i + 2], sc, rinv), q8r(f[j16 + 4 * i + 3], sc, rinv));
+            *reinterpret_cast<uint4 *>(args.Yq + (size_t)m * args.Nout + c0 + j16) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
@@ -616,17 +620,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 output [rows, cols] row-major, stored in 32 x 32 blocks from 64-byte-swizzled shared memory; rows / columns
+// bf16 output [rows, cols] row-major, stored in 32-row x 16-column blocks from 32-byte-swizzled shared memory; rows / columns
 // beyond the matrix are clipped by the copy engine
 bool make_out_map(CUtensorMap *map, const void *ptr, int cols, int rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {16, 32};
   cuuint32_t es[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }

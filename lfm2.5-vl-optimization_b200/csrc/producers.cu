@@ -52,16 +52,18 @@ __device__ __forceinline__ void quant_row_smem(const float *xs, int K, int8_t *_
     float m = 0.f;
     for (int i = threadIdx.x; i < K; i += PT) m = fmaxf(m, fabsf(xs[i]));
     const float sc = __fdiv_rn(fmaxf(block_max(m, red), 1e-8f), 127.f);
+    const float rinv = __frcp_rn(sc);
     if (threadIdx.x == 0) s[row] = sc;
-    for (int i = threadIdx.x; i < K; i += PT) qr[i] = (int8_t)q8(xs[i], sc);
+    for (int i = threadIdx.x; i < K; i += PT) qr[i] = (int8_t)q8r(xs[i], sc, rinv);
   } else {
     // one warp per 64-wide group: lane holds elements lane and lane + 32
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int g = warp; g < K / 64; g += PT / 32) {
       const float a = xs[g * 64 + lane], b = xs[g * 64 + 32 + lane];
       const float sc = __fdiv_rn(fmaxf(warp_max(fmaxf(fabsf(a), fabsf(b))), 1e-8f), 127.f);
-      qr[g * 64 + lane] = (int8_t)q8(a, sc);
-      qr[g * 64 + 32 + lane] = (int8_t)q8(b, sc);
+      const float rinv = __frcp_rn(sc);
+      qr[g * 64 + lane] = (int8_t)q8r(a, sc, rinv);
+      qr[g * 64 + 32 + lane] = (int8_t)q8r(b, sc, rinv);
       if (lane == 0) s[(size_t)g * rows + row] = sc;
     }
   }

@@ -2,7 +2,8 @@
 //
 //   quant_rows:   one scale per row (token):            s[row]        = max(|x[row, :]|, 1e-8) / 127
 //   quant_groups: one scale per row and 64-wide group:  sT[g][row]    = max(|x[row, 64g:64g+64]|, 1e-8) / 127
-//   codes:        q = clamp(rint(x / s), -127, 127), the quotient an IEEE fp32 division, ties to even.
+//   codes:        q = clamp(rint(x / s), -127, 127), the quotient an IEEE fp32 division, ties to even (computed
+//                 as x * (1 / s) with an exact fallback near rounding boundaries: q8r in common.cuh).
 //
 // Semantics follow kernels/int8_gemm.cu:393-432 (quant_rows_kernel) and :435-474 (quant_groups_kernel) of the
 // reference; the reference's per-row limit K <= 2048 (kernels/int8_gemm.cpp:93) is lifted here (K <= 16384,
@@ -60,6 +61,7 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
     }
     if (!live) return;
     const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
+    const float rinv = __frcp_rn(sc);
     if (sub == 0 && lane == 0) s[row] = sc;
     uint2 *qr = reinterpret_cast<uint2 *>(q + (size_t)row * K);
 #pragma unroll
@@ -69,12 +71,9 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
         const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
         uint32_t o[2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int a = q8(bf_lo(w[2 * h]), sc), b = q8(bf_hi(w[2 * h]), sc);
-          const int c2 = q8(bf_lo(w[2 * h + 1]), sc), d = q8(bf_hi(w[2 * h + 1]), sc);
-          o[h] = (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c2 & 0xFF) << 16) |
-                 ((uint32_t)(d & 0xFF) << 24);
-        }
+        for (int h = 0; h < 2; ++h)
+          o[h] = pack_i8x4(q8r(bf_lo(w[2 * h]), sc, rinv), q8r(bf_hi(w[2 * h]), sc, rinv),
+                           q8r(bf_lo(w[2 * h + 1]), sc, rinv), q8r(bf_hi(w[2 * h + 1]), sc, rinv));
         qr[c] = make_uint2(o[0], o[1]);
       }
     }
@@ -94,15 +93,13 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
       m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
       if (c < K8) {
         const float sc = __fdiv_rn(fmaxf(m, 1e-8f), 127.f);
+        const float rinv = __frcp_rn(sc);
         if ((lane & 7) == 0) s[(size_t)(c >> 3) * rows + row] = sc;
         uint32_t o[2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int a = q8(bf_lo(w[2 * h]), sc), b = q8(bf_hi(w[2 * h]), sc);
-          const int c2 = q8(bf_lo(w[2 * h + 1]), sc), d = q8(bf_hi(w[2 * h + 1]), sc);
-          o[h] = (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c2 & 0xFF) << 16) |
-                 ((uint32_t)(d & 0xFF) << 24);
-        }
+        for (int h = 0; h < 2; ++h)
+          o[h] = pack_i8x4(q8r(bf_lo(w[2 * h]), sc, rinv), q8r(bf_hi(w[2 * h]), sc, rinv),
+                           q8r(bf_lo(w[2 * h + 1]), sc, rinv), q8r(bf_hi(w[2 * h + 1]), sc, rinv));
         qr[c] = make_uint2(o[0], o[1]);
       }
     }
