@@ -538,6 +538,35 @@ def run_case(a):
                       "frac_nominal": round(tops / INT8_PEAK_NOMINAL, 4)}), flush=True)
 
 
+def run_gemv_case(a):
+    """One decode GEMV shape, back to back over enough distinct weight copies to exceed L2 (>= 256 MB)."""
+    from lfm2opt.kernels import ext
+
+    parts = [int(v) for v in a.gemv_case.split(",")]
+    N, K, B = parts[:3]
+    rows = parts[3] if len(parts) > 3 else 0
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    copies = max(1, -(-256 * 2 ** 20 // (N * K)))
+    Ws = [torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8) for _ in range(copies)]
+    s = torch.rand(N, generator=g, device=dev) * 1e-3
+    x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty(B, N, device=dev, dtype=torch.bfloat16)
+    E = ext()
+    it = [0]
+
+    def fn():
+        E.gemv(Ws[it[0] % copies], s, x, y, rows)
+        it[0] += 1
+
+    ms = time_steps(fn, a.steps, max(3, a.warmup), 1) / a.steps
+    nbytes = N * K + 4 * N + 2 * B * K + 2 * B * N
+    peak = load_peaks().get("hbm_gbs")
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({"gemv_case": a.gemv_case, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+                      "frac_hbm": round(gbs / peak, 4) if peak else None, "copies": copies}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -550,10 +579,13 @@ def main():
     ap.add_argument("--case", default=None,
                     help="M,K,N[,epi] — time one GEMM shape (epi: none|gelu|silu|group|groupq); tuning and ncu target")
     ap.add_argument("--tile", type=int, default=0, help="force the per-token GEMM tile width (128 or 256)")
+    ap.add_argument("--gemv-case", default=None, help="N,K,B[,rows] — time one decode GEMV shape (tuning, ncu target)")
     a = ap.parse_args()
     warmup = max(3, a.warmup)
     if a.case:
         return run_case(a)
+    if a.gemv_case:
+        return run_gemv_case(a)
 
     if a.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

@@ -44,6 +44,52 @@ __device__ __forceinline__ int q8r(float v, float sc, float rinv) {
   return max(-127, min(127, __float_as_int(tb) - 0x4B400000));
 }
 
+// ------------------------------------------------------------------ packed fp32 pairs (sm_100 f32x2 arithmetic)
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// Two int8 codes at once, as q8r, returned as the rounding sums 1.5 * 2^23 + code: the code is the low byte of
+// the sum's bits. No clamp is needed: with sc = RN(max(amax, 1e-8) / 127) and |v| <= amax, |v / sc| <= 127 *
+// (1 + 2^-23), so both the estimate and the IEEE quotient round to an integer of magnitude <= 127.
+__device__ __forceinline__ float2 q8r2(float2 v, float sc, float rinv) {
+  const float2 big = make_float2(12582912.f, 12582912.f);
+  const float2 t = fmul2(v, make_float2(rinv, rinv));
+  float2 tb = fadd2(t, big);
+  const float2 d = fsub2(t, fsub2(tb, big));
+  if (fmaxf(fabsf(d.x), fabsf(d.y)) > 0.49996f) {
+    tb.x = __fadd_rn(rintf(__fdiv_rn(v.x, sc)), 12582912.f);
+    tb.y = __fadd_rn(rintf(__fdiv_rn(v.y, sc)), 12582912.f);
+  }
+  return tb;
+}
+// low bytes of four rounding sums (see q8r2) -> one word of int8 codes
+__device__ __forceinline__ uint32_t pack_sums4(float2 a, float2 b) {
+  return __byte_perm(__byte_perm(__float_as_uint(a.x), __float_as_uint(a.y), 0x0040),
+                     __byte_perm(__float_as_uint(b.x), __float_as_uint(b.y), 0x0040), 0x5410);
+}
+
 // four int8 codes -> one word (byte 0 = a)
 __device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);

@@ -45,11 +45,16 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
     }
   }
   if (!GROUPED) {
+    {
+      // |x| of bf16 pairs is the word with both sign bits cleared; the max of two non-negative bf16 values is their
+      // larger 16-bit pattern, so the row maximum is a packed unsigned max over the words
+      uint32_t m2 = 0;
 #pragma unroll
-    for (int i = 0; i < QC; ++i) {
-      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) amax = fmaxf(amax, fmaxf(fabsf(bf_lo(w[j])), fabsf(bf_hi(w[j]))));
+      for (int i = 0; i < QC; ++i) {
+        m2 = __vmaxu2(m2, __vmaxu2(v[i].x & 0x7FFF7FFFu, v[i].y & 0x7FFF7FFFu));
+        m2 = __vmaxu2(m2, __vmaxu2(v[i].z & 0x7FFF7FFFu, v[i].w & 0x7FFF7FFFu));
+      }
+      amax = fmaxf(bf_lo(m2), bf_hi(m2));
     }
     amax = warp_max(amax);
     if (RW > 1) {
@@ -72,8 +77,8 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
         uint32_t o[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          o[h] = pack_i8x4(q8r(bf_lo(w[2 * h]), sc, rinv), q8r(bf_hi(w[2 * h]), sc, rinv),
-                           q8r(bf_lo(w[2 * h + 1]), sc, rinv), q8r(bf_hi(w[2 * h + 1]), sc, rinv));
+          o[h] = pack_sums4(q8r2(make_float2(bf_lo(w[2 * h]), bf_hi(w[2 * h])), sc, rinv),
+                            q8r2(make_float2(bf_lo(w[2 * h + 1]), bf_hi(w[2 * h + 1])), sc, rinv));
         qr[c] = make_uint2(o[0], o[1]);
       }
     }
@@ -98,8 +103,8 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
         uint32_t o[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          o[h] = pack_i8x4(q8r(bf_lo(w[2 * h]), sc, rinv), q8r(bf_hi(w[2 * h]), sc, rinv),
-                           q8r(bf_lo(w[2 * h + 1]), sc, rinv), q8r(bf_hi(w[2 * h + 1]), sc, rinv));
+          o[h] = pack_sums4(q8r2(make_float2(bf_lo(w[2 * h]), bf_hi(w[2 * h])), sc, rinv),
+                            q8r2(make_float2(bf_lo(w[2 * h + 1]), bf_hi(w[2 * h + 1])), sc, rinv));
         qr[c] = make_uint2(o[0], o[1]);
       }
     }
