@@ -93,7 +93,9 @@ int lfm2q_device_supported(void) { return device_is_sm100() ? 1 : 0; }
 int lfm2q_check_device(int clear) {
   if (int e = device_gate()) return e;
   const int v = gemm_device_error(clear != 0);
+  const int u = gemv_device_error(clear != 0);
   if (v) return fail(LFM2Q_ETIMEOUT, "lfm2q: a GEMM pipeline wait timed out on the device");
+  if (u) return fail(LFM2Q_ETIMEOUT, "lfm2q: a GEMV pipeline wait timed out on the device");
   return LFM2Q_OK;
 }
 

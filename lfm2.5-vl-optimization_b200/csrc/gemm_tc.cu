@@ -157,7 +157,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t sr
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read2() { asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -216,7 +216,8 @@ struct Smem {
   // epilogue: per-warp double-buffered 32 x 16 bf16 output blocks (32-byte rows, 32-byte swizzle) for TMA stores
   static constexpr int OUT_OFF = PAR_OFF + EPI_WARPS * PAR_FLOATS * 4;
   static constexpr int OUT_BLOCK = 32 * 32;
-  static constexpr int BYTES = OUT_OFF + EPI_WARPS * 2 * OUT_BLOCK;
+  static constexpr int OUT_BUFS = 3;
+  static constexpr int BYTES = OUT_OFF + EPI_WARPS * OUT_BUFS * OUT_BLOCK;
   static constexpr int ALLOC = BYTES + 1024;  // room to align the base to 1024
   static_assert(ALLOC <= 232448, "shared memory per block");
 };
@@ -403,28 +404,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * L::PAR_FLOATS;  // [128] weight scales
     float *par_b = par_sw + 128;                                                           // [128] bias
-    const uint32_t out_base = sbase + L::OUT_OFF + ew * 2 * L::OUT_BLOCK;
+    const uint32_t out_base = sbase + L::OUT_OFF + ew * L::OUT_BUFS * L::OUT_BLOCK;
     uint32_t out_count = 0;  // 32 x 16 blocks this warp has handed to the TMA engine
     int acc = 0;
     uint32_t aphase = 0;
 
-    // Stage the per-column epilogue parameters of this warp's columns (issued before the accumulator wait, so the
-    // loads overlap the MMAs). Entry i: output column c0 + i; with `silu`, entries 64.. hold the up rows.
-    auto stage_params = [&](int c0, int width, bool silu) {
+    // Per-column epilogue parameters of this warp's columns: lane l holds entries l, l + 32, l + 64, l + 96 of the
+    // next tile in registers (loaded one tile ahead, so their latency hides behind a whole tile of work) and writes
+    // them to the warp's shared memory when that tile starts. Entry i: output column c0 + i; with `silu`, entries
+    // CW.. hold the up rows (weight rows Nout + column).
+    float pf_sw[4], pf_b[4], pf_sx = 0.f;
+    auto prefetch = [&](int tile_i) {
+      if (tile_i >= tiles) return;
+      int pmt, pnt;
+      tile_coord(tile_i, args, pmt, pnt);
+      const int pm = pmt * TM + row;
+      pf_sx = (pm < M && !GROUPED) ? __ldg(args.sa + pm) : 0.f;
+      const int width = (EPI == EPI_SILU) ? BN / 4 : BN / 2;
+      const int c0 = (EPI == EPI_SILU) ? pnt * (BN / 2) + half * width : pnt * BN + half * width;
+      const int count = (EPI == EPI_SILU) ? 2 * width : width;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = lane + 32 * k;
+        const int oc = c0 + ((EPI == EPI_SILU) ? (i % width) : i);
+        const int col = (EPI == EPI_SILU && i >= width) ? args.Nout + oc : oc;
+        const bool ok = i < count && oc < args.Nout;
+        pf_sw[k] = ok ? __ldg(args.sb + col) : 0.f;
+        pf_b[k] = (ok && args.bias) ? bf2f(args.bias[col]) : 0.f;
+      }
+    };
+    auto stage_params = [&]() {
       __syncwarp();
-      for (int i = lane; i < (silu ? 2 * width : width); i += 32) {
-        const int oc = c0 + (silu ? (i % width) : i);
-        const int col = (silu && i >= width) ? args.Nout + oc : oc;
-        const bool ok = oc < args.Nout;
-        par_sw[i] = ok ? __ldg(args.sb + col) : 0.f;
-        par_b[i] = (ok && args.bias) ? bf2f(args.bias[col]) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        par_sw[lane + 32 * k] = pf_sw[k];
+        par_b[lane + 32 * k] = pf_b[k];
       }
       __syncwarp();
     };
     // Hand a 32-row x 16-column bf16 block (this lane's row: 8 packed words) to the TMA engine at (column x, row y).
     auto store_block = [&](const uint32_t *o, int x, int y) {
-      const uint32_t buf = out_base + (out_count & 1) * L::OUT_BLOCK;
-      if (lane == 0) bulk_wait_read1();  // the buffer's previous store has finished reading it
+      const uint32_t buf = out_base + (out_count % L::OUT_BUFS) * L::OUT_BLOCK;
+      if (lane == 0) bulk_wait_read2();  // the buffer's previous store (3 blocks ago) has finished reading it
       __syncwarp();
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -451,17 +472,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     };
 
+    prefetch(blockIdx.x);
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int mt, nt;
       tile_coord(tile, args, mt, nt);
       const int m = mt * TM + row;
       const bool mrow = m < M;
       const int yrow = mt * TM + q * 32;  // first output row of this warp's blocks
+      const float sxm = pf_sx;
+      stage_params();
+      prefetch(tile + gridDim.x);
       if (EPI == EPI_TOKEN) {
         constexpr int CW = BN / 2, NCH = CW / 32;  // this warp's columns
         const int c0 = nt * BN + half * CW;
-        const float sxm = mrow ? __ldg(args.sa + m) : 0.f;
-        stage_params(c0, CW, false);
         if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
         tc_fence_after();
         const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
@@ -486,8 +509,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       } else if (EPI == EPI_SILU) {
         constexpr int CW = BN / 4;  // 64 output columns per warp: gate TMEM columns [CW*half..), up [BN/2 + ..)
         const int c0 = nt * (BN / 2) + half * CW;
-        const float sxm = mrow ? __ldg(args.sa + m) : 0.f;
-        stage_params(c0, CW, true);
         if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
         tc_fence_after();
         const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
@@ -523,7 +544,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // grouped: fold every 64-wide K group into fp32 running sums held in registers (64 columns per warp)
         constexpr int CW = BN / 2;
         const int c0 = nt * BN + half * CW;
-        stage_params(c0, CW, false);
         float f[CW];
 #pragma unroll
         for (int j = 0; j < CW; ++j) f[j] = 0.f;

@@ -256,6 +256,155 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restri
   }
 }
 
+// ------------------------------------------------------------------ int8 GEMV streamed with bulk copies
+// Persistent, one block per SM (grid = min(16-row groups, SMs)): block b owns a contiguous range of 16-row groups,
+// i.e. a contiguous slab of W. Warp 8 (one thread) streams it into a ring of GB_STAGES shared-memory stages of
+// 16 rows x SK bytes with cp.async.bulk (one copy per row, rows padded by 64 bytes so the consumers' 16-byte
+// loads are bank-conflict-free), completing on mbarriers; it never waits for data, so up to GB_STAGES x 16 KB
+// are in flight per SM with no registers tied up. Warps 0-7 consume: warp w converts and multiplies K bytes
+// [w SK/8, (w+1) SK/8) of every stage (same MMA fragment scheme as warp_gemv), keeping fp32 partials across the
+// K/SK stages of a row group; at the group's end the 8 partials meet in shared memory and are summed in warp order.
+// Every mbarrier wait is bounded; on expiry the block stops loading, the consumers run out their fixed number of
+// steps without computing, and the device error word is set.
+constexpr int GB_STAGES = 5;
+constexpr int GB_THREADS = 288;  // 8 consumer warps + 1 producer warp
+constexpr long long GB_WAIT = 1ll << 31;
+__device__ int g_gemv_err = 0;
+
+__device__ __forceinline__ uint32_t gb_smem(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool gb_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool gb_wait(uint32_t bar, uint32_t parity, int *abort_flag) {
+  if (gb_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!gb_try(bar, parity)) {
+    if (*(volatile int *)abort_flag) return false;
+    if (clock64() - t0 > GB_WAIT) {
+      atomicExch(abort_flag, 1);
+      atomicCAS(&g_gemv_err, 0, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(GB_THREADS, 1)
+    gemv_bulk_kernel(const int8_t *__restrict__ W, const float *__restrict__ scale, const bf16 *__restrict__ x,
+                     bf16 *__restrict__ y, int N, int K, int B, int SK, int pdl) {
+  extern __shared__ __align__(128) uint8_t gsm[];
+  const int pitch = SK + 64;
+  const int stage_bytes = 16 * pitch;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(gsm + GB_STAGES * stage_bytes);
+  float *red = reinterpret_cast<float *>(bars + 2 * GB_STAGES);
+  int *abort_flag = reinterpret_cast<int *>(red + 8 * 16 * 8 * NT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = (N + 15) / 16;
+  const int g0 = (int)((long long)groups * blockIdx.x / gridDim.x);
+  const int g1 = (int)((long long)groups * (blockIdx.x + 1) / gridDim.x);
+  const int spg = K / SK;  // stages per row group
+  const int total = (g1 - g0) * spg;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < GB_STAGES; ++i) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(gb_smem(bars + i)), "r"(1) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(gb_smem(bars + GB_STAGES + i)), "r"(8) : "memory");
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (pdl) pdl_trigger();
+  if (warp == 8) {
+    // producer: weights are immutable, so streaming starts before the dependency wait
+    if (lane == 0) {
+      for (int i = 0; i < total; ++i) {
+        const int st = i % GB_STAGES;
+        const uint32_t ph = (uint32_t)(i / GB_STAGES) & 1u;
+        if (!gb_wait(gb_smem(bars + GB_STAGES + st), ph ^ 1u, abort_flag)) break;
+        const int gi = g0 + i / spg, kc = i % spg;
+        const uint32_t full = gb_smem(bars + st);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full), "r"(16 * SK) : "memory");
+        const uint32_t dst0 = gb_smem(gsm + st * stage_bytes);
+        for (int r = 0; r < 16; ++r) {
+          const int row = min(gi * 16 + r, N - 1);
+          const int8_t *src = W + (size_t)row * K + (size_t)kc * SK;
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                  dst0 + r * pitch),
+              "l"(src), "r"(SK), "r"(full)
+              : "memory");
+        }
+      }
+    }
+    return;
+  }
+  // consumers
+  if (pdl) pdl_wait();
+  const int g = lane >> 2, t = lane & 3;
+  const int kw = SK / 8;  // K bytes per warp per stage (a multiple of 64)
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+  for (int i = 0; i < total; ++i) {
+    const int st = i % GB_STAGES;
+    const uint32_t ph = (uint32_t)(i / GB_STAGES) & 1u;
+    const int gi = g0 + i / spg, kc = i % spg;
+    bool ok = true;
+    if (lane == 0) ok = gb_wait(gb_smem(bars + st), ph, abort_flag);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (ok) {
+      const uint8_t *base = gsm + st * stage_bytes + warp * kw + t * 16;
+      for (int ks = 0; ks < kw; ks += 64) {
+        const uint4 r0 = *reinterpret_cast<const uint4 *>(base + g * pitch + ks);
+        const uint4 r1 = *reinterpret_cast<const uint4 *>(base + (g + 8) * pitch + ks);
+        const int kphys = kc * SK + warp * kw + ks + t * 16;
+        uint32_t xw[NT][8];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) load_x<int8_t>(x, K, g + 8 * j, B, kphys, xw[j]);
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4) {
+          uint32_t a[4];
+          WFmt<int8_t>::frag(r0, r1, s4, a);
+#pragma unroll
+          for (int j = 0; j < NT; ++j) mma_bf16_16816(acc[j], a, xw[j][2 * s4], xw[j][2 * s4 + 1]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(gb_smem(bars + GB_STAGES + st)) : "memory");
+    if (kc == spg - 1) {
+      // row group done: the 8 warps' partials meet in shared memory and are summed in warp order
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          red[(warp * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
+          acc[j][e] = 0.f;
+        }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      for (int o = threadIdx.x; o < 16 * 8 * NT; o += 256) {
+        const int rr = o / (8 * NT), b = o % (8 * NT), n = gi * 16 + rr;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) v += red[(w * 16 + rr) * 8 * NT + b];
+        if (n < N && b < B) y[(size_t)b * N + n] = f2bf(scale[n] * v);
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+    }
+  }
+}
+
+size_t gemv_bulk_smem(int SK, int NT) { return (size_t)GB_STAGES * 16 * (SK + 64) + 2 * GB_STAGES * 8 + 8 * 16 * 8 * NT * 4 + 16; }
+
 template <typename KernelT, typename... Args>
 cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -295,9 +444,49 @@ int pick_ks(int N, int K, int kstep, int rows_override) {
   return ks;
 }
 
+template <int NT>
+cudaError_t gemv_bulk_launch(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
+                             cudaStream_t st) {
+  const int SK = (K % 1024 == 0) ? 1024 : 512;
+  const size_t smem = gemv_bulk_smem(SK, NT);
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    const cudaError_t e = cudaFuncSetAttribute(gemv_bulk_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)gemv_bulk_smem(1024, NT));
+    if (e != cudaSuccess) return e;
+    attr_done[dev & 63] = true;
+  }
+  const int groups = (N + 15) / 16;
+  const int grid = groups < device_sm_count() ? groups : device_sm_count();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GB_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<NT>, W, scale, x, y, N, K, B, SK, pdl ? 1 : 0);
+}
+
 template <typename WT>
 cudaError_t gemv_dispatch(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int rows, int B,
                           bool pdl, cudaStream_t st) {
+  if constexpr (sizeof(WT) == 1) {
+    if (rows == 0) {  // the bulk-copy kernel; rows = 1, 2, 4, 8 selects the register-streaming kernel
+      for (int b0 = 0; b0 < B; b0 += 16) {
+        const int bs = min(16, B - b0);
+        const cudaError_t e = bs > 8 ? gemv_bulk_launch<2>(W, scale, x + (size_t)b0 * K, y + (size_t)b0 * N, N, K, bs, pdl, st)
+                                     : gemv_bulk_launch<1>(W, scale, x + (size_t)b0 * K, y + (size_t)b0 * N, N, K, bs, pdl, st);
+        if (e != cudaSuccess) return e;
+      }
+      return cudaSuccess;
+    }
+  }
   const int ks = pick_ks(N, K, WFmt<WT>::KSTEP, rows);
   for (int b0 = 0; b0 < B; b0 += 16) {
     const int bs = min(16, B - b0);
@@ -321,6 +510,16 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
 }
 
 }  // namespace
+
+int gemv_device_error(bool clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemv_err, sizeof(int));
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_gemv_err, &z, sizeof(int));
+  }
+  return v;
+}
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st) {

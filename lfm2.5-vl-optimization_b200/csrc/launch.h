@@ -22,6 +22,7 @@ cudaError_t launch_silu_mul_q(const void *g, int8_t *q, float *s, int rows, int 
 // gemv.cu
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st);
+int gemv_device_error(bool clear);  // sticky code written by a bounded wait of the bulk-copy GEMV (0 = none)
 cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,
                             void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st);
 
