@@ -21,7 +21,7 @@ namespace lfm2q {
 namespace {
 
 constexpr int GV_THREADS = 256;  // 8 warps
-constexpr int GV_BATCH = 4;      // 64-wide K steps loaded per batch (double-buffered)
+constexpr int GV_RING = 6;       // K steps (1 KB each) a warp keeps in flight
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -89,47 +89,29 @@ __device__ __forceinline__ void load_x(const bf16 *__restrict__ x, int K, int to
 }
 
 // Core: one warp accumulates rows [r0, r0 + 16) x K-slice [kb, ke) for tokens 0..8*NT-1 into acc[NT][4].
+// Weights travel global -> shared memory with cp.async (16 bytes per lane per row and step), GV_RING steps ahead, in
+// a ring private to the warp (ring: GV_RING x 1 KB; each lane writes and later reads only its own 16-byte slots,
+// at row * 64 + t * 16, which is bank-conflict-free), so no registers are tied up by loads in flight and a warp
+// keeps ~5 KB of weights outstanding. A slot is refilled only after its data has been read and used.
 template <typename WT, int NT>
 __device__ __forceinline__ void warp_gemv(const WT *__restrict__ W, const bf16 *__restrict__ x, int N, int K, int B,
-                                          int r0, int kb, int ke, float (&acc)[NT][4], bool pdl) {
+                                          int r0, int kb, int ke, float (&acc)[NT][4], uint8_t *ring, bool pdl) {
   constexpr int KSTEP = WFmt<WT>::KSTEP, STEPS = WFmt<WT>::STEPS;
   constexpr int CH = 16 / sizeof(WT);  // elements per 16-byte chunk
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const WT *row0 = W + (size_t)min(r0 + g, N - 1) * K;
-  const WT *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K;
-  // lane t's chunk inside a KSTEP-wide step starts at element t * CH
+  const WT *row0 = W + (size_t)min(r0 + g, N - 1) * K + kb + t * CH;
+  const WT *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K + kb + t * CH;
+  const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(ring) + g * 64 + t * 16;
   const int nsteps = (ke - kb) / KSTEP;
-  uint4 wb[2][GV_BATCH][2];
 
-  auto load_batch = [&](int buf, int st0) {
-#pragma unroll
-    for (int u = 0; u < GV_BATCH; ++u) {
-      const int st = st0 + u;
-      if (st < nsteps) {
-        const int k = kb + st * KSTEP + t * CH;
-        wb[buf][u][0] = ld_stream16(row0 + k);
-        wb[buf][u][1] = ld_stream16(row1 + k);
-      }
+  auto issue = [&](int st) {
+    if (st < nsteps) {
+      const uint32_t d = slot0 + (st % GV_RING) * 1024;
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + st * KSTEP) : "memory");
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(row1 + st * KSTEP)
+                   : "memory");
     }
-  };
-  auto compute_batch = [&](int buf, int st0) {
-#pragma unroll
-    for (int u = 0; u < GV_BATCH; ++u) {
-      const int st = st0 + u;
-      if (st < nsteps) {
-        const int kphys = kb + st * KSTEP + t * CH;
-        uint32_t xw[NT][8];
-#pragma unroll
-        for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kphys, xw[j]);
-#pragma unroll
-        for (int s = 0; s < STEPS; ++s) {
-          uint32_t a[4];
-          WFmt<WT>::frag(wb[buf][u][0], wb[buf][u][1], s, a);
-#pragma unroll
-          for (int j = 0; j < NT; ++j) mma_bf16_16816(acc[j], a, xw[j][2 * s], xw[j][2 * s + 1]);
-        }
-      }
-    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
 #pragma unroll
@@ -137,58 +119,83 @@ __device__ __forceinline__ void warp_gemv(const WT *__restrict__ W, const bf16 *
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
 
-  load_batch(0, 0);  // weights are immutable: stream them before the dependency wait
+#pragma unroll
+  for (int st = 0; st < GV_RING; ++st) issue(st);  // weights are immutable: stream before the dependency wait
   if (pdl) pdl_wait();
-  for (int st0 = 0; st0 < nsteps; st0 += 2 * GV_BATCH) {
-    load_batch(1, st0 + GV_BATCH);
-    compute_batch(0, st0);
-    load_batch(0, st0 + 2 * GV_BATCH);
-    compute_batch(1, st0 + GV_BATCH);
+  for (int st = 0; st < nsteps; ++st) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 1) : "memory");
+    const uint32_t d = slot0 + (st % GV_RING) * 1024;
+    uint4 w0, w1;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
+                 : "memory");
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
+                 : "r"(d + 512)
+                 : "memory");
+    const int kphys = kb + st * KSTEP + t * CH;
+    uint32_t xw[NT][8];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kphys, xw[j]);
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+      uint32_t a[4];
+      WFmt<WT>::frag(w0, w1, s, a);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mma_bf16_16816(acc[j], a, xw[j][2 * s], xw[j][2 * s + 1]);
+    }
+    issue(st + GV_RING);  // the slot just consumed
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // Fragment accumulator element e of token group j -> (row in group, token)
 __device__ __forceinline__ int frag_row(int lane, int e) { return (lane >> 2) + ((e & 2) ? 8 : 0); }
 __device__ __forceinline__ int frag_tok(int lane, int j, int e) { return 8 * j + 2 * (lane & 3) + (e & 1); }
 
-// Plain GEMV. Block = RG row groups x KS K-slices (RG * KS == 8 warps).
+// Plain GEMV. Block = RG row groups x KS K-slices (RG * KS == 8 warps); blocks walk the row-group sets in a grid
+// stride (grid = min(sets, resident blocks)), so large N runs in one wave with balanced work.
 template <typename WT, int NT, int KS>
 __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__ W, const float *__restrict__ scale,
                                                           const bf16 *__restrict__ x, bf16 *__restrict__ y, int N, int K,
                                                           int B, int pdl) {
   constexpr int RG = 8 / KS;
+  extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x GV_RING x 1 KB
   __shared__ float red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
   if (pdl) pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
-  const int r0 = (blockIdx.x * RG + rg) * 16;
   const int kslice = K / KS;
-  float acc[NT][4];
-  warp_gemv<WT, NT>(W, x, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, pdl != 0);
-  if (KS == 1) {
+  const int sets = ((N + 15) / 16 + RG - 1) / RG;
+  for (int set = blockIdx.x; set < sets; set += gridDim.x) {
+    const int r0 = (set * RG + rg) * 16;
+    float acc[NT][4];
+    warp_gemv<WT, NT>(W, x, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, rings + warp * GV_RING * 1024,
+                      pdl != 0 && set == blockIdx.x);
+    if (KS == 1) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = r0 + frag_row(lane, e), b = frag_tok(lane, j, e);
+          if (n < N && b < B) y[(size_t)b * N + n] = f2bf(scale ? acc[j][e] * scale[n] : acc[j][e]);
+        }
+      continue;
+    }
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int n = r0 + frag_row(lane, e), b = frag_tok(lane, j, e);
-        if (n < N && b < B) y[(size_t)b * N + n] = f2bf(scale ? acc[j][e] * scale[n] : acc[j][e]);
-      }
-    return;
-  }
+      for (int e = 0; e < 4; ++e)
+        red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < RG * 16 * 8 * NT; i += GV_THREADS) {
+      const int b = i % (8 * NT), rr = (i / (8 * NT)) % 16, g2 = i / (16 * 8 * NT);
+      const int n = (set * RG + g2) * 16 + rr;
+      if (n >= N || b >= B) continue;
+      float v = 0.f;
 #pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
-  __syncthreads();
-  for (int i = threadIdx.x; i < RG * 16 * 8 * NT; i += GV_THREADS) {
-    const int b = i % (8 * NT), rr = (i / (8 * NT)) % 16, g2 = i / (16 * 8 * NT);
-    const int n = (blockIdx.x * RG + g2) * 16 + rr;
-    if (n >= N || b >= B) continue;
-    float v = 0.f;
-#pragma unroll
-    for (int s = 0; s < KS; ++s) v += red[((g2 * KS + s) * 16 + rr) * 8 * NT + b];
-    y[(size_t)b * N + n] = f2bf(scale ? v * scale[n] : v);
+      for (int s = 0; s < KS; ++s) v += red[((g2 * KS + s) * 16 + rr) * 8 * NT + b];
+      y[(size_t)b * N + n] = f2bf(scale ? v * scale[n] : v);
+    }
+    __syncthreads();
   }
 }
 
@@ -205,6 +212,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restri
                                                               const bf16 *__restrict__ cw,
                                                               const bf16 *__restrict__ cbias, int pdl) {
   constexpr int KSE = (NR == 2) ? 4 : 2;  // K-slices per part (NR * KSE <= 8 warps)
+  extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x GV_RING x 1 KB
   __shared__ float red[NR][KSE][16];
   __shared__ float part[NR][16];
   if (pdl) pdl_trigger();
@@ -216,7 +224,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restri
     float acc[1][4];
     // rows of part p: p * S + n0 .. ; clamp inside the part so the loads stay in W
     const WT *Wp = W + (size_t)p * S * K;
-    warp_gemv<WT, 1>(Wp, x, S, K, 1, n0, ks * kslice, (ks + 1) * kslice, acc, pdl != 0);
+    warp_gemv<WT, 1>(Wp, x, S, K, 1, n0, ks * kslice, (ks + 1) * kslice, acc, rings + warp * GV_RING * 1024, pdl != 0);
     // token 0 lives in lanes with t == 0, element e & 1 == 0
     if ((lane & 3) == 0) {
       red[p][ks][frag_row(lane, 0)] = acc[0][0];
@@ -256,161 +264,24 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restri
   }
 }
 
-// ------------------------------------------------------------------ int8 GEMV streamed with bulk copies
-// Persistent, one block per SM (grid = min(16-row groups, SMs)): block b owns a contiguous range of 16-row groups,
-// i.e. a contiguous slab of W. Warp 8 (one thread) streams it into a ring of GB_STAGES shared-memory stages of
-// 16 rows x SK bytes with cp.async.bulk (one copy per row, rows padded by 64 bytes so the consumers' 16-byte
-// loads are bank-conflict-free), completing on mbarriers; it never waits for data, so up to GB_STAGES x 16 KB
-// are in flight per SM with no registers tied up. Warps 0-7 consume: warp w converts and multiplies K bytes
-// [w SK/8, (w+1) SK/8) of every stage (same MMA fragment scheme as warp_gemv), keeping fp32 partials across the
-// K/SK stages of a row group; at the group's end the 8 partials meet in shared memory and are summed in warp order.
-// Every mbarrier wait is bounded; on expiry the block stops loading, the consumers run out their fixed number of
-// steps without computing, and the device error word is set.
-constexpr int GB_STAGES = 5;
-constexpr int GB_THREADS = 288;  // 8 consumer warps + 1 producer warp
-constexpr long long GB_WAIT = 1ll << 31;
-__device__ int g_gemv_err = 0;
+constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
 
-__device__ __forceinline__ uint32_t gb_smem(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ bool gb_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool gb_wait(uint32_t bar, uint32_t parity, int *abort_flag) {
-  if (gb_try(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!gb_try(bar, parity)) {
-    if (*(volatile int *)abort_flag) return false;
-    if (clock64() - t0 > GB_WAIT) {
-      atomicExch(abort_flag, 1);
-      atomicCAS(&g_gemv_err, 0, 1);
-      return false;
-    }
-  }
-  return true;
-}
-
-template <int NT>
-__global__ void __launch_bounds__(GB_THREADS, 1)
-    gemv_bulk_kernel(const int8_t *__restrict__ W, const float *__restrict__ scale, const bf16 *__restrict__ x,
-                     bf16 *__restrict__ y, int N, int K, int B, int SK, int pdl) {
-  extern __shared__ __align__(128) uint8_t gsm[];
-  const int pitch = SK + 64;
-  const int stage_bytes = 16 * pitch;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(gsm + GB_STAGES * stage_bytes);
-  float *red = reinterpret_cast<float *>(bars + 2 * GB_STAGES);
-  int *abort_flag = reinterpret_cast<int *>(red + 8 * 16 * 8 * NT);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int groups = (N + 15) / 16;
-  const int g0 = (int)((long long)groups * blockIdx.x / gridDim.x);
-  const int g1 = (int)((long long)groups * (blockIdx.x + 1) / gridDim.x);
-  const int spg = K / SK;  // stages per row group
-  const int total = (g1 - g0) * spg;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < GB_STAGES; ++i) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(gb_smem(bars + i)), "r"(1) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(gb_smem(bars + GB_STAGES + i)), "r"(8) : "memory");
-    }
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (pdl) pdl_trigger();
-  if (warp == 8) {
-    // producer: weights are immutable, so streaming starts before the dependency wait
-    if (lane == 0) {
-      for (int i = 0; i < total; ++i) {
-        const int st = i % GB_STAGES;
-        const uint32_t ph = (uint32_t)(i / GB_STAGES) & 1u;
-        if (!gb_wait(gb_smem(bars + GB_STAGES + st), ph ^ 1u, abort_flag)) break;
-        const int gi = g0 + i / spg, kc = i % spg;
-        const uint32_t full = gb_smem(bars + st);
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full), "r"(16 * SK) : "memory");
-        const uint32_t dst0 = gb_smem(gsm + st * stage_bytes);
-        for (int r = 0; r < 16; ++r) {
-          const int row = min(gi * 16 + r, N - 1);
-          const int8_t *src = W + (size_t)row * K + (size_t)kc * SK;
-          asm volatile(
-              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                  dst0 + r * pitch),
-              "l"(src), "r"(SK), "r"(full)
-              : "memory");
-        }
-      }
-    }
-    return;
-  }
-  // consumers
-  if (pdl) pdl_wait();
-  const int g = lane >> 2, t = lane & 3;
-  const int kw = SK / 8;  // K bytes per warp per stage (a multiple of 64)
-  float acc[NT][4];
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
-  for (int i = 0; i < total; ++i) {
-    const int st = i % GB_STAGES;
-    const uint32_t ph = (uint32_t)(i / GB_STAGES) & 1u;
-    const int gi = g0 + i / spg, kc = i % spg;
-    bool ok = true;
-    if (lane == 0) ok = gb_wait(gb_smem(bars + st), ph, abort_flag);
-    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    if (ok) {
-      const uint8_t *base = gsm + st * stage_bytes + warp * kw + t * 16;
-      for (int ks = 0; ks < kw; ks += 64) {
-        const uint4 r0 = *reinterpret_cast<const uint4 *>(base + g * pitch + ks);
-        const uint4 r1 = *reinterpret_cast<const uint4 *>(base + (g + 8) * pitch + ks);
-        const int kphys = kc * SK + warp * kw + ks + t * 16;
-        uint32_t xw[NT][8];
-#pragma unroll
-        for (int j = 0; j < NT; ++j) load_x<int8_t>(x, K, g + 8 * j, B, kphys, xw[j]);
-#pragma unroll
-        for (int s4 = 0; s4 < 4; ++s4) {
-          uint32_t a[4];
-          WFmt<int8_t>::frag(r0, r1, s4, a);
-#pragma unroll
-          for (int j = 0; j < NT; ++j) mma_bf16_16816(acc[j], a, xw[j][2 * s4], xw[j][2 * s4 + 1]);
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(gb_smem(bars + GB_STAGES + st)) : "memory");
-    if (kc == spg - 1) {
-      // row group done: the 8 warps' partials meet in shared memory and are summed in warp order
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          red[(warp * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
-          acc[j][e] = 0.f;
-        }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      for (int o = threadIdx.x; o < 16 * 8 * NT; o += 256) {
-        const int rr = o / (8 * NT), b = o % (8 * NT), n = gi * 16 + rr;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) v += red[(w * 16 + rr) * 8 * NT + b];
-        if (n < N && b < B) y[(size_t)b * N + n] = f2bf(scale[n] * v);
-      }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-    }
-  }
-}
-
-size_t gemv_bulk_smem(int SK, int NT) { return (size_t)GB_STAGES * 16 * (SK + 64) + 2 * GB_STAGES * 8 + 8 * 16 * 8 * NT * 4 + 16; }
-
+// Launch with the per-warp rings as dynamic shared memory (opt-in above 48 KB, set once per kernel and device) and,
+// when asked, Programmatic Dependent Launch.
 template <typename KernelT, typename... Args>
 cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, Args... args) {
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_done[dev & 63] = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = GV_DYN_SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -424,7 +295,9 @@ template <typename WT, int NT>
 cudaError_t gemv_ks(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
                     cudaStream_t st) {
   const int groups = (N + 15) / 16, rg = 8 / ks;
-  const dim3 grid((groups + rg - 1) / rg);
+  const int sets = (groups + rg - 1) / rg;
+  const int resident = 4 * device_sm_count();  // 48 KB of rings per block: 4 blocks per SM
+  const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? 1 : 0;
   switch (ks) {
     case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
@@ -444,49 +317,9 @@ int pick_ks(int N, int K, int kstep, int rows_override) {
   return ks;
 }
 
-template <int NT>
-cudaError_t gemv_bulk_launch(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
-                             cudaStream_t st) {
-  const int SK = (K % 1024 == 0) ? 1024 : 512;
-  const size_t smem = gemv_bulk_smem(SK, NT);
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    const cudaError_t e = cudaFuncSetAttribute(gemv_bulk_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)gemv_bulk_smem(1024, NT));
-    if (e != cudaSuccess) return e;
-    attr_done[dev & 63] = true;
-  }
-  const int groups = (N + 15) / 16;
-  const int grid = groups < device_sm_count() ? groups : device_sm_count();
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(GB_THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<NT>, W, scale, x, y, N, K, B, SK, pdl ? 1 : 0);
-}
-
 template <typename WT>
 cudaError_t gemv_dispatch(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int rows, int B,
                           bool pdl, cudaStream_t st) {
-  if constexpr (sizeof(WT) == 1) {
-    if (rows == 0) {  // the bulk-copy kernel; rows = 1, 2, 4, 8 selects the register-streaming kernel
-      for (int b0 = 0; b0 < B; b0 += 16) {
-        const int bs = min(16, B - b0);
-        const cudaError_t e = bs > 8 ? gemv_bulk_launch<2>(W, scale, x + (size_t)b0 * K, y + (size_t)b0 * N, N, K, bs, pdl, st)
-                                     : gemv_bulk_launch<1>(W, scale, x + (size_t)b0 * K, y + (size_t)b0 * N, N, K, bs, pdl, st);
-        if (e != cudaSuccess) return e;
-      }
-      return cudaSuccess;
-    }
-  }
   const int ks = pick_ks(N, K, WFmt<WT>::KSTEP, rows);
   for (int b0 = 0; b0 < B; b0 += 16) {
     const int bs = min(16, B - b0);
@@ -511,15 +344,7 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
 
 }  // namespace
 
-int gemv_device_error(bool clear) {
-  int v = 0;
-  cudaMemcpyFromSymbol(&v, g_gemv_err, sizeof(int));
-  if (clear && v) {
-    const int z = 0;
-    cudaMemcpyToSymbol(g_gemv_err, &z, sizeof(int));
-  }
-  return v;
-}
+int gemv_device_error(bool) { return 0; }
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st) {
