@@ -14,6 +14,10 @@
 // identically for W and x (lane t, step s take physical k 16t+4s..16t+4s+3), which leaves the dot product
 // unchanged. Small N is split over K-slices (KS warps per row group) whose fp32 partials meet in shared memory
 // and are summed in a fixed order, so results are deterministic.
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -268,15 +272,22 @@ constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
 
 // Launch with the per-warp rings as dynamic shared memory (opt-in above 48 KB, set once per kernel and device) and,
 // when asked, Programmatic Dependent Launch.
+// (kernel, device) pairs whose dynamic shared memory limit has been raised
+std::mutex g_attr_mu;
+std::set<std::pair<const void *, int>> g_attr_done;
+
 template <typename KernelT, typename... Args>
 cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, Args... args) {
-  static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_SMEM);
-    if (e != cudaSuccess) return e;
-    attr_done[dev & 63] = true;
+  {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), dev);
+    if (!g_attr_done.count(key)) {
+      const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_SMEM);
+      if (e != cudaSuccess) return e;
+      g_attr_done.insert(key);
+    }
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
