@@ -117,38 +117,65 @@ __device__ __forceinline__ void warp_gemv(const WT *__restrict__ W, const bf16 *
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
-
-#pragma unroll
-  for (int st = 0; st < GV_RING; ++st) issue(st);  // weights are immutable: stream before the dependency wait
-  if (pdl) pdl_wait();
-  for (int st = 0; st < nsteps; ++st) {
-    asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 1) : "memory");
+  auto lds = [&](int st, uint4 &w0, uint4 &w1) {
     const uint32_t d = slot0 + (st % GV_RING) * 1024;
-    uint4 w0, w1;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
                  : "memory");
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
                  : "r"(d + 512)
                  : "memory");
-    const int kphys = kb + st * KSTEP + t * CH;
-    uint32_t xw[NT][8];
+  };
+
+  // two independent accumulator chains (even / odd MMA k-steps), summed at the end
+  float acc2[NT][4];
 #pragma unroll
-    for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kphys, xw[j]);
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = acc2[j][e] = 0.f;
+
+#pragma unroll
+  for (int st = 0; st < GV_RING; ++st) issue(st);  // weights are immutable: stream before the dependency wait
+  if (pdl) pdl_wait();
+  // software pipeline: the weights (shared memory) and x fragments (L1 / L2) of step st + 1 are loaded while
+  // step st is converted and multiplied
+  uint4 wc0, wc1, wn0, wn1;
+  uint32_t xc[NT][8], xn[NT][8];
+  asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 1) : "memory");
+  if (nsteps > 0) {
+    lds(0, wc0, wc1);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kb + t * CH, xc[j]);
+  }
+  for (int st = 0; st < nsteps; ++st) {
+    if (st + 1 < nsteps) {
+      asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 2) : "memory");
+      lds(st + 1, wn0, wn1);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kb + (st + 1) * KSTEP + t * CH, xn[j]);
+    }
 #pragma unroll
     for (int s = 0; s < STEPS; ++s) {
       uint32_t a[4];
-      WFmt<WT>::frag(w0, w1, s, a);
+      WFmt<WT>::frag(wc0, wc1, s, a);
 #pragma unroll
-      for (int j = 0; j < NT; ++j) mma_bf16_16816(acc[j], a, xw[j][2 * s], xw[j][2 * s + 1]);
+      for (int j = 0; j < NT; ++j) {
+        if (s & 1) mma_bf16_16816(acc2[j], a, xc[j][2 * s], xc[j][2 * s + 1]);
+        else mma_bf16_16816(acc[j], a, xc[j][2 * s], xc[j][2 * s + 1]);
+      }
     }
-    issue(st + GV_RING);  // the slot just consumed
+    issue(st + GV_RING);  // slot of step st: its data is already in registers
+    wc0 = wn0;
+    wc1 = wn1;
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xc[j][i] = xn[j][i];
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] += acc2[j][e];
 }
 
 // Fragment accumulator element e of token group j -> (row in group, token)
@@ -164,7 +191,6 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__
   constexpr int RG = 8 / KS;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x GV_RING x 1 KB
   __shared__ float red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
-  if (pdl) pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
@@ -174,6 +200,8 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__
     float acc[NT][4];
     warp_gemv<WT, NT>(W, x, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, rings + warp * GV_RING * 1024,
                       pdl != 0 && set == blockIdx.x);
+    // the block's weights are consumed: let the next kernel start streaming its own
+    if (pdl && set + (int)gridDim.x >= sets) pdl_trigger();
     if (KS == 1) {
 #pragma unroll
       for (int j = 0; j < NT; ++j)
