@@ -368,9 +368,14 @@ class E2E:
 
 # ----------------------------------------------------------------------------------------------- GEMV sweep
 def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
+    """Decode GEMV stack (16 layers + lm_head, distinct weights: 1.17 GB > L2) replayed from a CUDA graph, for both
+    decode paths: `w16` = the reference's weight-only GEMV (bf16 activations, lfm2q_gemv) and `a8` = per-token int8
+    activations (quant_rows, then lfm2q_gemv_a8: exact int32 sums). Bytes per GEMV = N*K + 4N + 2BK + 2BN."""
+    from lfm2opt import _capi
     from lfm2opt.kernels import ext
 
     E = ext()
+    L = _capi.lib()
     g = torch.Generator(device=dev).manual_seed(777)
     layers = []
     for l in range(LM_LAYERS):
@@ -380,56 +385,50 @@ def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
                            torch.rand(N, generator=g, device=dev) * 1e-3 + 1e-4))
     layers.append((torch.randint(-127, 128, (65536, 2048), generator=g, device=dev, dtype=torch.int8),
                    torch.rand(65536, generator=g, device=dev) * 1e-3 + 1e-4))
-    res = {}
-    for B in batches:
-        xs = {K: torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16) for K in (2048, 8192)}
-        ys = [torch.empty(B, W.shape[0], device=dev, dtype=torch.bfloat16) for W, _ in layers]
-        nbytes = sum(W.shape[0] * W.shape[1] + 4 * W.shape[0] + 2 * B * W.shape[1] + 2 * B * W.shape[0]
-                     for W, _ in layers)
+    res = {"w16": {}, "a8": {}}
+    for mode in ("w16", "a8"):
+        for B in batches:
+            xs = {K: torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16) for K in (2048, 8192)}
+            xq = {K: torch.empty(B, K, device=dev, dtype=torch.int8) for K in (2048, 8192)}
+            sx = {K: torch.empty(B, device=dev, dtype=torch.float32) for K in (2048, 8192)}
+            ys = [torch.empty(B, W.shape[0], device=dev, dtype=torch.bfloat16) for W, _ in layers]
+            nbytes = sum(W.shape[0] * W.shape[1] + 4 * W.shape[0] + 2 * B * W.shape[1] + 2 * B * W.shape[0]
+                         for W, _ in layers)
 
-        def sweep():
-            for (W, s), y in zip(layers, ys):
-                E.gemv(W, s, xs[W.shape[1]], y)
+            def sweep():
+                stream = torch.cuda.current_stream(dev).cuda_stream
+                for (W, s), y in zip(layers, ys):
+                    K = W.shape[1]
+                    if mode == "w16":
+                        E.gemv(W, s, xs[K], y)
+                    else:
+                        L.lfm2q_quant_rows(xs[K].data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), B, K, stream)
+                        L.lfm2q_gemv_a8(W.data_ptr(), s.data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), None,
+                                        y.data_ptr(), W.shape[0], K, B, 0, stream)
 
-        s = torch.cuda.Stream(dev)
-        s.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(s):
-            for _ in range(2):
+            st = torch.cuda.Stream(dev)
+            st.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(st):
+                for _ in range(2):
+                    sweep()
+            torch.cuda.current_stream(dev).wait_stream(st)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
                 sweep()
-        torch.cuda.current_stream(dev).wait_stream(s)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            sweep()
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(replays):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / replays
-        ms = max_over_ranks(ms, world)
-        res[B] = {"us_per_sweep": round(ms * 1e3, 2), "gbs": round(world * nbytes / (ms * 1e-3) / 1e9, 1),
-                  "bytes_per_sweep": nbytes, "launches": len(layers)}
-        del graph
-    # lm_head alone at B = 1 (134 MB > L2), back to back
-    W, s = layers[-1]
-    x = torch.randn(1, 2048, generator=g, device=dev).to(torch.bfloat16)
-    y = torch.empty(1, 65536, device=dev, dtype=torch.bfloat16)
-    for _ in range(3):
-        E.gemv(W, s, x, y)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(50):
-        E.gemv(W, s, x, y)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / 50, world)
-    nb = 65536 * 2048 + 4 * 65536 + 2 * 2048 + 2 * 65536
-    res["lm_head_b1"] = {"us": round(ms * 1e3, 2), "gbs": round(nb / (ms * 1e-3) / 1e9, 1)}
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(replays):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = max_over_ranks(e0.elapsed_time(e1) / replays, world)
+            res[mode][B] = {"us_per_sweep": round(ms * 1e3, 2), "gbs": round(world * nbytes / (ms * 1e-3) / 1e9, 1),
+                            "bytes_per_sweep": nbytes,
+                            "launches": len(layers) * (1 if mode == "w16" else 2)}
+            del graph
     return res
 
 
@@ -556,9 +555,16 @@ def run_gemv_case(a):
     E = ext()
     per = 20
 
+    a8 = os.environ.get("GEMV_MODE", "w16") == "a8"
+    xq = torch.randint(-127, 128, (B, K), generator=g, device=dev, dtype=torch.int8)
+    sx = torch.rand(B, generator=g, device=dev) * 1e-2
+
     def burst():
         for i in range(per):
-            E.gemv(Ws[i % copies], s, x, y, rows)
+            if a8:
+                E.gemv_a8(Ws[i % copies], s, xq, sx, y)
+            else:
+                E.gemv(Ws[i % copies], s, x, y, rows)
 
     st = torch.cuda.Stream(dev)
     st.wait_stream(torch.cuda.current_stream(dev))
@@ -572,7 +578,8 @@ def run_gemv_case(a):
     nbytes = N * K + 4 * N + 2 * B * K + 2 * B * N
     peak = load_peaks().get("hbm_gbs")
     gbs = nbytes / (ms * 1e-3) / 1e9
-    print(json.dumps({"gemv_case": a.gemv_case, "pdl": os.environ.get("LFM2_PDL", "1"), "us": round(ms * 1e3, 2),
+    print(json.dumps({"gemv_case": a.gemv_case, "mode": "a8" if a8 else "w16", "pdl": os.environ.get("LFM2_PDL", "1"),
+                      "us": round(ms * 1e3, 2),
                       "gbs": round(gbs, 1), "frac_hbm": round(gbs / peak, 4) if peak else None, "copies": copies}),
           flush=True)
 
@@ -689,10 +696,14 @@ def main():
                 "launches_timed_per_gpu": n_gemm, "avg_launch_us": round(g_ms * 1e3 / max(1, n_gemm), 1),
                 "traffic": traffic.get("dram_bytes_per_launch") if traffic else None}
         if gemv:
-            b1 = gemv[1]["gbs"] / world
-            gemv_out = {"metric": "decode GEMV HBM GB/s", "per_batch": {str(k): v for k, v in gemv.items()},
-                        "stack_b1_gbs_per_gpu": round(b1, 1),
-                        "hbm_peak_gbs": hbm, "frac_b1": round(b1 / hbm, 4) if hbm else None,
+            w1 = gemv["w16"][1]["gbs"] / world
+            a1 = gemv["a8"][1]["gbs"] / world
+            gemv_out = {"metric": "decode GEMV HBM GB/s (16-layer LFM2 stack + lm_head, CUDA graph)",
+                        "w16_weight_only": {str(k): v for k, v in gemv["w16"].items()},
+                        "a8_int8_tokens": {str(k): v for k, v in gemv["a8"].items()},
+                        "b1_gbs_per_gpu": {"w16": round(w1, 1), "a8": round(a1, 1)},
+                        "hbm_peak_gbs": hbm,
+                        "frac_b1": {"w16": round(w1 / hbm, 4), "a8": round(a1 / hbm, 4)} if hbm else None,
                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy bandwidth)"}
         else:
             gemv_out = None

@@ -102,6 +102,15 @@ int lfm2q_silu_mul_q(const uint16_t *g, int8_t *q, float *s, int rows, int I, in
 int lfm2q_gemv(const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int N, int K,
                int rows, int B, void *stream);
 
+/* A8 decode GEMV, bit-exact at int32: the W8A8 path of gemm_i8 for few tokens (no single counterpart in the
+ * reference, whose decode GEMV is weight-only; the result equals gemm_i8 (kernels/int8_gemm.cpp:39-50) on the same
+ * int8 inputs, and lfm2q_gemm_i8 itself routes M <= 16 per-token calls here).
+ * y bf16 [B, N] = bf16(act(((float)(xq . W^T)[b, n] * sx[b]) * sw[n] + bias[n])), xq int8 [B, K] quantized per token
+ * (lfm2q_quant_rows), sx fp32 [B], W int8 [N, K], sw fp32 [N], bias bf16 [N] or NULL, act = GELU(tanh) if gelu.
+ * Needs K % 64 == 0, B >= 1 (any B: chunks of 16 tokens per launch). */
+int lfm2q_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const uint16_t *bias,
+                  uint16_t *y, int N, int K, int B, int gelu, void *stream);
+
 /* Replaces launch_gemv_epi (kernels/lfm2_decode.cu:818-827) behind gemv_epi (kernels/lfm2_decode.cpp:130-150).
  * Batch 1. epi 0: W = w1|w3 [2S, K] -> y [S] = bf16(bf16(silu(g)) * u).
  *          epi 1: W = in_proj [3S, K] (B|C|x) -> short-conv step, state bf16 [S, 3] updated in place,

@@ -117,6 +117,23 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// ------------------------------------------------------------------ W8A8 epilogue (shared by every W8A8 kernel)
+// F.gelu(v, approximate="tanh") = 0.5 v (1 + tanh(u)), u = sqrt(2/pi) (v + 0.044715 v^3), evaluated as the equal
+// v / (1 + exp(-2u)): no cancellation near tanh = -1, one exponential and one reciprocal per element.
+__device__ __forceinline__ float gelu_tanh(float v) {
+  const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  return __fdividef(v, 1.f + __expf(-2.f * u));
+}
+// y = act(((float)acc * sx[m]) * sw[n] + b[n]) in the reference's fp32 operation order (kernels/int8_gemm.cu:93-115,
+// no contraction); (float)acc rounds the exact int32 to nearest even, as torch's .float() does.
+template <bool GELU>
+__device__ __forceinline__ float epi_token(int acc, float sxm, float sw, float b) {
+  float y = __fmul_rn((float)acc, sxm);
+  y = __fadd_rn(__fmul_rn(y, sw), b);
+  if (GELU) y = gelu_tanh(y);
+  return y;
+}
+
 // ------------------------------------------------------------------ programmatic dependent launch
 // A kernel launched with programmatic stream serialization may start while its predecessor drains.
 // Before pdl_wait() it may only read immutable data (weights); pdl_wait() returns once the previous

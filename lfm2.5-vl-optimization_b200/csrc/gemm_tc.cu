@@ -173,12 +173,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
-// F.gelu(v, approximate="tanh") = 0.5 v (1 + tanh(u)), u = sqrt(2/pi) (v + 0.044715 v^3), evaluated as the equal
-// v / (1 + exp(-2u)): no cancellation near tanh = -1, one exponential and one reciprocal per element.
-__device__ __forceinline__ float gelu_tanh(float v) {
-  const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-  return __fdividef(v, 1.f + __expf(-2.f * u));
-}
 // exact (float)v for |v| < 2^22: add into the mantissa of 1.5 * 2^23 and subtract it again
 __device__ __forceinline__ float i2f_small(int v) { return __int_as_float(v + 0x4B400000) - 12582912.f; }
 
@@ -223,14 +217,6 @@ struct Smem {
 };
 
 // ------------------------------------------------------------------ epilogue helpers
-template <bool GELU>
-__device__ __forceinline__ float epi_token(int acc, float sxm, float sw, float b) {
-  float y = __fmul_rn((float)acc, sxm);  // cvt.rn: the int32 sum rounds to fp32 exactly as torch's .float()
-  y = __fadd_rn(__fmul_rn(y, sw), b);
-  if (GELU) y = gelu_tanh(y);
-  return y;
-}
-
 __device__ __forceinline__ void load8f(const float *p, float (&v)[8]) {
   const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
   const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
@@ -733,6 +719,10 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
     GemmArgs a = base_args(sa, sb, bias, M, N, K, N, 128);
     a.Y = (bf16 *)Y;
     return gelu ? run_tc<128, 6, 4, EPI_GROUP, true>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false>(A, B, a, st);
+  }
+  if (M <= 16 && K % 64 == 0 && !g_tile_override) {
+    // skinny: the A8 GEMV streams W once with int8 MMAs (same exact int32 sums and the same epilogue)
+    return launch_gemv_a8(B, sb, A, sa, bias, Y, N, K, M, gelu, false, st);
   }
   int bn = g_tile_override;
   if (!bn) {

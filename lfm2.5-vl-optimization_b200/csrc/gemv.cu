@@ -35,16 +35,18 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// 4 int8 codes (bytes of w) -> two bf16x2 words (lo: bytes 0,1; hi: bytes 2,3), exact
+// 4 int8 codes (bytes of w) -> two bf16x2 words (lo: bytes 0,1; hi: bytes 2,3), exact: each byte + 128 goes into
+// the mantissa of 2^23 (one byte permute), a packed fp32 subtraction of 2^23 + 128 leaves the code as an exact fp32,
+// whose upper half is its bf16 encoding (|q| <= 127 has at most 7 significant bits).
 __device__ __forceinline__ void i8x4_to_bf16x2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
   const uint32_t u = w ^ 0x80808080u;  // q + 128 in 0..255
-  const float bias = 8388736.f;        // 2^23 + 128
-  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - bias;
-  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - bias;
-  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - bias;
-  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - bias;
-  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+  const float2 bias = make_float2(8388736.f, 8388736.f);  // 2^23 + 128
+  const float2 f01 = fsub2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651))), bias);
+  const float2 f23 = fsub2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653))), bias);
+  lo = __byte_perm(__float_as_uint(f01.x), __float_as_uint(f01.y), 0x7632);
+  hi = __byte_perm(__float_as_uint(f23.x), __float_as_uint(f23.y), 0x7632);
 }
 
 template <typename WT>
@@ -178,6 +180,83 @@ __device__ __forceinline__ void warp_gemv(const WT *__restrict__ W, const bf16 *
     for (int e = 0; e < 4; ++e) acc[j][e] += acc2[j][e];
 }
 
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// A8 core: int8 weights x int8 tokens (quantized per token) -> exact int32 sums, rows [r0, r0 + 16) x K-slice
+// [kb, ke). Same cp.async ring and software pipeline as warp_gemv; no conversion at all: the 16 bytes a lane holds
+// of rows g and g + 8 feed two m16n8k32 s8 MMAs directly. Lane (g, t), MMA s of a 64-byte step: logical k slots
+// 4t..4t+3 / 16+4t..16+4t+3 take physical bytes 16t+8s..+3 / 16t+8s+4..+7, for W and x alike.
+template <int NT>
+__device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const int8_t *__restrict__ xq, int N, int K,
+                                             int B, int r0, int kb, int ke, int (&acc)[NT][4], uint8_t *ring, bool pdl) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int8_t *row0 = W + (size_t)min(r0 + g, N - 1) * K + kb + t * 16;
+  const int8_t *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K + kb + t * 16;
+  const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(ring) + g * 64 + t * 16;
+  const int nsteps = (ke - kb) / 64;
+  auto issue = [&](int st) {
+    if (st < nsteps) {
+      const uint32_t d = slot0 + (st % GV_RING) * 1024;
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + st * 64) : "memory");
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(row1 + st * 64) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  auto lds = [&](int st, uint4 &w0, uint4 &w1) {
+    const uint32_t d = slot0 + (st % GV_RING) * 1024;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
+                 : "memory");
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
+                 : "r"(d + 512)
+                 : "memory");
+  };
+  auto ldx = [&](int st, uint4 (&xw)[NT]) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int tok = g + 8 * j;
+      xw[j] = tok < B ? __ldg(reinterpret_cast<const uint4 *>(xq + (size_t)tok * K + kb + st * 64 + t * 16))
+                      : make_uint4(0, 0, 0, 0);
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0;
+#pragma unroll
+  for (int st = 0; st < GV_RING; ++st) issue(st);
+  if (pdl) pdl_wait();
+  uint4 wc0, wc1, wn0, wn1, xc[NT], xn[NT];
+  asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 1) : "memory");
+  if (nsteps > 0) {
+    lds(0, wc0, wc1);
+    ldx(0, xc);
+  }
+  for (int st = 0; st < nsteps; ++st) {
+    if (st + 1 < nsteps) {
+      asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 2) : "memory");
+      lds(st + 1, wn0, wn1);
+      ldx(st + 1, xn);
+    }
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const uint32_t a[4] = {(&wc0.x)[2 * s], (&wc1.x)[2 * s], (&wc0.x)[2 * s + 1], (&wc1.x)[2 * s + 1]};
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mma_s8_16832(acc[j], a, (&xc[j].x)[2 * s], (&xc[j].x)[2 * s + 1]);
+    }
+    issue(st + GV_RING);
+    wc0 = wn0;
+    wc1 = wn1;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) xc[j] = xn[j];
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // Fragment accumulator element e of token group j -> (row in group, token)
 __device__ __forceinline__ int frag_row(int lane, int e) { return (lane >> 2) + ((e & 2) ? 8 : 0); }
 __device__ __forceinline__ int frag_tok(int lane, int j, int e) { return 8 * j + 2 * (lane & 3) + (e & 1); }
@@ -226,6 +305,57 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__
 #pragma unroll
       for (int s = 0; s < KS; ++s) v += red[((g2 * KS + s) * 16 + rr) * 8 * NT + b];
       y[(size_t)b * N + n] = f2bf(scale ? v * scale[n] : v);
+    }
+    __syncthreads();
+  }
+}
+
+// A8 decode GEMV: y[b, n] = bf16(act(((float)(xq[b] . W[n]) * sx[b]) * sw[n] + bias[n])), the per-token W8A8
+// epilogue of gemm_i8 on an exact int32 sum, for 1..16 tokens per launch. Block = RG row groups x KS K-slices;
+// the K-slices' int32 partials are added in shared memory (exact, so the result does not depend on the split).
+template <int NT, int KS, bool GELU>
+__global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__restrict__ W, const float *__restrict__ sw,
+                                                             const int8_t *__restrict__ xq, const float *__restrict__ sx,
+                                                             const bf16 *__restrict__ bias, bf16 *__restrict__ y, int N,
+                                                             int K, int B, int pdl) {
+  constexpr int RG = 8 / KS;
+  extern __shared__ __align__(128) uint8_t rings[];
+  __shared__ int red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rg = warp / KS, ks = warp % KS;
+  const int kslice = K / KS;
+  const int sets = ((N + 15) / 16 + RG - 1) / RG;
+  for (int set = blockIdx.x; set < sets; set += gridDim.x) {
+    const int r0 = (set * RG + rg) * 16;
+    int acc[NT][4];
+    warp_gemv_a8<NT>(W, xq, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, rings + warp * GV_RING * 1024,
+                     pdl != 0 && set == blockIdx.x);
+    if (pdl && set + (int)gridDim.x >= sets) pdl_trigger();
+    if (KS == 1) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = r0 + frag_row(lane, e), b = frag_tok(lane, j, e);
+          if (n < N && b < B)
+            y[(size_t)b * N + n] = f2bf(epi_token<GELU>(acc[j][e], sx[b], sw[n], bias ? bf2f(bias[n]) : 0.f));
+        }
+      continue;
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < RG * 16 * 8 * NT; i += GV_THREADS) {
+      const int b = i % (8 * NT), rr = (i / (8 * NT)) % 16, g2 = i / (16 * 8 * NT);
+      const int n = (set * RG + g2) * 16 + rr;
+      if (n >= N || b >= B) continue;
+      int v = 0;
+#pragma unroll
+      for (int s2 = 0; s2 < KS; ++s2) v += red[((g2 * KS + s2) * 16 + rr) * 8 * NT + b];
+      y[(size_t)b * N + n] = f2bf(epi_token<GELU>(v, sx[b], sw[n], bias ? bf2f(bias[n]) : 0.f));
     }
     __syncthreads();
   }
@@ -383,6 +513,22 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
 
 }  // namespace
 
+template <int NT, bool GELU>
+cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const bf16 *bias, bf16 *y,
+                       int N, int K, int B, int ks, bool pdl, cudaStream_t st) {
+  const int groups = (N + 15) / 16, rg = 8 / ks;
+  const int sets = (groups + rg - 1) / rg;
+  const int resident = 4 * device_sm_count();
+  const dim3 grid(sets < resident ? sets : resident);
+  const int p = pdl ? 1 : 0;
+  switch (ks) {
+    case 1: return launch_ex(gemv_a8_kernel<NT, 1, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
+    case 2: return launch_ex(gemv_a8_kernel<NT, 2, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
+    case 4: return launch_ex(gemv_a8_kernel<NT, 4, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
+    default: return launch_ex(gemv_a8_kernel<NT, 8, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
+  }
+}
+
 int gemv_device_error(bool) { return 0; }
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
@@ -401,6 +547,28 @@ cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scal
                                      (const bf16 *)cw, (const bf16 *)cbias, pdl, st);
   return gemv_epi_dispatch<bf16>(epi, (const bf16 *)W, scale, (const bf16 *)x, (bf16 *)y, S, K, (bf16 *)state,
                                  (const bf16 *)cw, (const bf16 *)cbias, pdl, st);
+}
+
+cudaError_t launch_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const void *bias, void *y,
+                           int N, int K, int B, bool gelu, bool pdl, cudaStream_t st) {
+  if (N <= 0 || B <= 0) return cudaSuccess;
+  const int ks = pick_ks(N, K, 64, 0);
+  for (int b0 = 0; b0 < B; b0 += 16) {
+    const int bs = min(16, B - b0);
+    const int8_t *xb = xq + (size_t)b0 * K;
+    const float *sb = sx + b0;
+    bf16 *yb = (bf16 *)y + (size_t)b0 * N;
+    const bf16 *bi = (const bf16 *)bias;
+    cudaError_t e;
+    if (bs > 8)
+      e = gelu ? gemv_a8_ks<2, true>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<2, false>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st);
+    else
+      e = gelu ? gemv_a8_ks<1, true>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<1, false>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace lfm2q

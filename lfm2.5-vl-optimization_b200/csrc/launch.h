@@ -22,7 +22,10 @@ cudaError_t launch_silu_mul_q(const void *g, int8_t *q, float *s, int rows, int 
 // gemv.cu
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st);
-int gemv_device_error(bool clear);  // sticky code written by a bounded wait of the bulk-copy GEMV (0 = none)
+int gemv_device_error(bool clear);
+// A8 decode GEMV: int8 tokens (per-token scales) x int8 W, exact int32, the per-token W8A8 epilogue (gemm_i8's)
+cudaError_t launch_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const void *bias, void *y,
+                           int N, int K, int B, bool gelu, bool pdl, cudaStream_t st);  // sticky code written by a bounded wait of the bulk-copy GEMV (0 = none)
 cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,
                             void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st);
 

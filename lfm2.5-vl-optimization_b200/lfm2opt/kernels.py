@@ -5,7 +5,7 @@ prebuilt sm_100a library liblfm2q.so instead of a JIT build.
                 gemm_i8, gemm_i8_q, gemm_w8, quant_rows, add_layernorm_q, add_rmsnorm_q, silu_mul_q,
                 plus gemm_i8_silu (W8A8 GEMM with the SiLU(w1) * w3 gate fused into its epilogue)
     ext()       the GEMV part of the reference's lfm2_decode extension (kernels/lfm2_decode.cpp:152-168):
-                gemv, gemv_epi, set_pdl, set_gemv_impl
+                gemv, gemv_epi, set_pdl, set_gemv_impl, plus gemv_a8 (int8 tokens x int8 weights, exact int32)
 
 Argument names, meaning, in-place outputs and the RuntimeError messages of the shape checks follow the reference
 bindings (kernels/int8_gemm.cpp:20-141, kernels/lfm2_decode.cpp:30-150). Every op enqueues on PyTorch's current
@@ -264,6 +264,27 @@ class DecodeGemvExt:
             _capi.call("lfm2q_gemv_epi", int(epi), W.data_ptr(), int(int8), _ptr(scale), x.data_ptr(), y.data_ptr(),
                        S, K, _ptr(state) if epi == 1 else None, _ptr(cw) if epi == 1 else None,
                        _ptr(cbias) if epi == 1 else None, _stream(x))
+
+    def gemv_a8(self, W, sw, xq, sx, y, bias=None, gelu=False):
+        """A8 decode GEMV (no counterpart in the reference): y [B, N] = bf16(act((xq . W^T) * sx[b] * sw[n] + bias)),
+        xq int8 [B, K] with per-token scales sx [B] (from quant_rows), exact int32 sums: equal to gemm_i8 on the same
+        operands."""
+        _check(W, _I8, "W")
+        _check(sw, _F32, "sw")
+        _check(xq, _I8, "xq")
+        _check(sx, _F32, "sx")
+        _check(y, _BF, "y")
+        N, K = W.shape
+        B = xq.numel() // K
+        _req(W.dim() == 2 and xq.numel() == B * K and B >= 1 and y.numel() == B * N, "xq [B, K], y [B, N]")
+        _req(sx.numel() == B and sw.numel() == N, "sx [B], sw [N]")
+        _req(K % 64 == 0, "K must be a multiple of 64")
+        if bias is not None:
+            _check(bias, _BF, "(*bias)")
+            _req(bias.numel() == N, "bias shape")
+        with _DeviceOf(xq):
+            _capi.call("lfm2q_gemv_a8", W.data_ptr(), sw.data_ptr(), xq.data_ptr(), sx.data_ptr(), _ptr(bias),
+                       y.data_ptr(), N, K, B, int(bool(gelu)), _stream(xq))
 
     def set_pdl(self, on):
         """Enable/disable Programmatic Dependent Launch for the GEMV kernels (default on)."""

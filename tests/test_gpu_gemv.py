@@ -139,3 +139,24 @@ def test_gemv_epi_shortconv(cuda_dev, int8, with_bias):
     assert torch.equal(out.cpu().reshape(-1), ref)
     new_state = torch.stack([s0[:, 1], s0[:, 2], bx], 1).to(BF)
     assert torch.equal(st.cpu().reshape(H, 3), new_state)
+
+
+@pytest.mark.parametrize("N,K", [(3072, 2048), (2048, 8192), (65536, 2048), (16384, 2048), (40, 512), (264, 1152)])
+@pytest.mark.parametrize("B", [1, 2, 7, 8, 9, 16, 19])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemv_a8_bit_exact(cuda_dev, N, K, B, gelu):
+    """A8 GEMV = the per-token W8A8 epilogue on the exact int32 sum: identical to the gemm_i8 oracle."""
+    if N * K > 40_000_000 and (B not in (1, 16) or gelu):
+        pytest.skip("large shape: a few cases suffice")
+    g = torch.Generator().manual_seed(N + K + B + gelu)
+    W = (torch.randn(N, K, generator=g) * 0.02).to(BF)
+    Wq, sw = quantize_int8(W)
+    x = torch.randn(B, K, generator=g).to(BF)
+    b = (torch.randn(N, generator=g) * 0.1).to(BF) if gelu else None
+    xq, sx = oracle.quant_rows_ref(x)
+    y = torch.empty(B, N, device=cuda_dev, dtype=BF)
+    ext().gemv_a8(Wq.to(cuda_dev), sw.to(cuda_dev), xq.to(cuda_dev), sx.to(cuda_dev), y,
+                  None if b is None else b.to(cuda_dev), gelu)
+    r = oracle.gemm_i8_ref(xq, sx, Wq, sw, b, gelu)
+    from test_gpu_gemm import assert_close_bf16
+    assert_close_bf16(y.cpu(), r, gelu)
