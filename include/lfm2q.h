@@ -124,6 +124,10 @@ int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, co
 void lfm2q_set_pdl(int on);
 void lfm2q_set_gemv_impl(int impl);
 
+/* GEMV kernels launched with Programmatic Dependent Launch let the next kernel launch after their K loop
+ * (early == 0, default) or at their start (early != 0). Tuning only; results are unchanged. */
+void lfm2q_set_gemv_trigger(int early);
+
 /* Forces the per-token GEMM tile width (128 or 256; 0 = automatic). Tuning and testing only. */
 void lfm2q_set_gemm_tile(int bn);
 

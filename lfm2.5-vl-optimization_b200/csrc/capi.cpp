@@ -100,6 +100,7 @@ int lfm2q_check_device(int clear) {
 }
 
 void lfm2q_set_pdl(int on) { g_pdl.store(on != 0); }
+void lfm2q_set_gemv_trigger(int early) { gemv_set_early_trigger(early != 0); }
 void lfm2q_set_gemv_impl(int) {}
 void lfm2q_set_gemm_tile(int bn) { gemm_set_tile_override(bn); }
 
@@ -111,7 +112,8 @@ int lfm2q_quant_rows(const uint16_t *x, int8_t *q, float *s, int rows, int K, vo
   REQUIRE(aligned16(x) && aligned16(q), "x and q must be 16-byte aligned");
   if (rows == 0) return LFM2Q_OK;
   if (int e = device_gate()) return e;
-  return launched(launch_quant_rows(x, q, s, rows, K, (cudaStream_t)stream), "quant_rows");
+  // decode-sized batches ride the same programmatic-dependent-launch chain as the GEMVs
+  return launched(launch_quant_rows(x, q, s, rows, K, g_pdl.load() && rows <= 64, (cudaStream_t)stream), "quant_rows");
 }
 
 int lfm2q_quant_groups(const uint16_t *x, int8_t *q, float *sT, int rows, int K, void *stream) {
@@ -121,7 +123,8 @@ int lfm2q_quant_groups(const uint16_t *x, int8_t *q, float *sT, int rows, int K,
   REQUIRE(aligned16(x) && aligned16(q), "x and q must be 16-byte aligned");
   if (rows == 0) return LFM2Q_OK;
   if (int e = device_gate()) return e;
-  return launched(launch_quant_groups(x, q, sT, rows, K, (cudaStream_t)stream), "quant_groups");
+  return launched(launch_quant_groups(x, q, sT, rows, K, g_pdl.load() && rows <= 64, (cudaStream_t)stream),
+                  "quant_groups");
 }
 
 // ------------------------------------------------------------------ GEMMs

@@ -270,6 +270,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__
   constexpr int RG = 8 / KS;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x GV_RING x 1 KB
   __shared__ float red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
+  if (pdl == 2) pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
@@ -279,8 +280,8 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__
     float acc[NT][4];
     warp_gemv<WT, NT>(W, x, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, rings + warp * GV_RING * 1024,
                       pdl != 0 && set == blockIdx.x);
-    // the block's weights are consumed: let the next kernel start streaming its own
-    if (pdl && set + (int)gridDim.x >= sets) pdl_trigger();
+    // the block's weights are consumed: let the next kernel start streaming its own (pdl == 2: done at the start)
+    if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();
     if (KS == 1) {
 #pragma unroll
       for (int j = 0; j < NT; ++j)
@@ -321,6 +322,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
   constexpr int RG = 8 / KS;
   extern __shared__ __align__(128) uint8_t rings[];
   __shared__ int red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
+  if (pdl == 2) pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
@@ -330,7 +332,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
     int acc[NT][4];
     warp_gemv_a8<NT>(W, xq, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, rings + warp * GV_RING * 1024,
                      pdl != 0 && set == blockIdx.x);
-    if (pdl && set + (int)gridDim.x >= sets) pdl_trigger();
+    if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();
     if (KS == 1) {
 #pragma unroll
       for (int j = 0; j < NT; ++j)
@@ -427,6 +429,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restri
 }
 
 constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
+bool g_early_trigger = false;
 
 // Launch with the per-warp rings as dynamic shared memory (opt-in above 48 KB, set once per kernel and device) and,
 // when asked, Programmatic Dependent Launch.
@@ -467,7 +470,7 @@ cudaError_t gemv_ks(const WT *W, const float *scale, const bf16 *x, bf16 *y, int
   const int sets = (groups + rg - 1) / rg;
   const int resident = 4 * device_sm_count();  // 48 KB of rings per block: 4 blocks per SM
   const dim3 grid(sets < resident ? sets : resident);
-  const int p = pdl ? 1 : 0;
+  const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
   switch (ks) {
     case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
     case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
@@ -520,7 +523,7 @@ cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const
   const int sets = (groups + rg - 1) / rg;
   const int resident = 4 * device_sm_count();
   const dim3 grid(sets < resident ? sets : resident);
-  const int p = pdl ? 1 : 0;
+  const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
   switch (ks) {
     case 1: return launch_ex(gemv_a8_kernel<NT, 1, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
     case 2: return launch_ex(gemv_a8_kernel<NT, 2, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
@@ -530,6 +533,7 @@ cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const
 }
 
 int gemv_device_error(bool) { return 0; }
+void gemv_set_early_trigger(bool early) { g_early_trigger = early; }
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st) {

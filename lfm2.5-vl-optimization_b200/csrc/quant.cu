@@ -24,7 +24,13 @@ constexpr int QC = 8;    // 16-byte chunks held per lane
 
 template <int RW, bool GROUPED>
 __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, int8_t *__restrict__ q,
-                                                   float *__restrict__ s, int rows, int K) {
+                                                   float *__restrict__ s, int rows, int K, int pdl) {
+  // launched with programmatic serialization: let the next kernel (the GEMV / GEMM that reads q, s) start its own
+  // weight streaming, and wait for the producer of x before reading it
+  if (pdl) {
+    pdl_trigger();
+    pdl_wait();
+  }
   constexpr int ROWS_PER_BLOCK = (QT / 32) / RW;
   __shared__ float red[QT / 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,31 +118,39 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
 }
 
 template <bool GROUPED>
-cudaError_t run_quant(const void *x, int8_t *q, float *s, int rows, int K, cudaStream_t st) {
+cudaError_t run_quant(const void *x, int8_t *q, float *s, int rows, int K, bool pdl, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const int K8 = K / 8;
   // smallest RW whose RW * 32 lanes * QC chunks cover the row
   int rw = 1;
   while (rw * 32 * QC < K8) rw *= 2;
   const bf16 *xx = (const bf16 *)x;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(QT);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const int p = pdl ? 1 : 0;
   switch (rw) {
-    case 1: quant_kernel<1, GROUPED><<<(rows + 7) / 8, QT, 0, st>>>(xx, q, s, rows, K); break;
-    case 2: quant_kernel<2, GROUPED><<<(rows + 3) / 4, QT, 0, st>>>(xx, q, s, rows, K); break;
-    case 4: quant_kernel<4, GROUPED><<<(rows + 1) / 2, QT, 0, st>>>(xx, q, s, rows, K); break;
-    case 8: quant_kernel<8, GROUPED><<<rows, QT, 0, st>>>(xx, q, s, rows, K); break;
+    case 1: cfg.gridDim = dim3((rows + 7) / 8); return cudaLaunchKernelEx(&cfg, quant_kernel<1, GROUPED>, xx, q, s, rows, K, p);
+    case 2: cfg.gridDim = dim3((rows + 3) / 4); return cudaLaunchKernelEx(&cfg, quant_kernel<2, GROUPED>, xx, q, s, rows, K, p);
+    case 4: cfg.gridDim = dim3((rows + 1) / 2); return cudaLaunchKernelEx(&cfg, quant_kernel<4, GROUPED>, xx, q, s, rows, K, p);
+    case 8: cfg.gridDim = dim3(rows); return cudaLaunchKernelEx(&cfg, quant_kernel<8, GROUPED>, xx, q, s, rows, K, p);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_quant_rows(const void *x, int8_t *q, float *s, int rows, int K, cudaStream_t st) {
-  return run_quant<false>(x, q, s, rows, K, st);
+cudaError_t launch_quant_rows(const void *x, int8_t *q, float *s, int rows, int K, bool pdl, cudaStream_t st) {
+  return run_quant<false>(x, q, s, rows, K, pdl, st);
 }
 
-cudaError_t launch_quant_groups(const void *x, int8_t *q, float *sT, int rows, int K, cudaStream_t st) {
-  return run_quant<true>(x, q, sT, rows, K, st);
+cudaError_t launch_quant_groups(const void *x, int8_t *q, float *sT, int rows, int K, bool pdl, cudaStream_t st) {
+  return run_quant<true>(x, q, sT, rows, K, pdl, st);
 }
 
 }  // namespace lfm2q

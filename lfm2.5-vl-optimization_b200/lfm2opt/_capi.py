@@ -36,8 +36,9 @@ SIGNATURES = {
     "lfm2q_set_pdl": [_i],
     "lfm2q_set_gemv_impl": [_i],
     "lfm2q_set_gemm_tile": [_i],
+    "lfm2q_set_gemv_trigger": [_i],
 }
-_VOID = {"lfm2q_set_pdl", "lfm2q_set_gemv_impl", "lfm2q_set_gemm_tile"}
+_VOID = {"lfm2q_set_pdl", "lfm2q_set_gemv_impl", "lfm2q_set_gemm_tile", "lfm2q_set_gemv_trigger"}
 _STR = {"lfm2q_last_error", "lfm2q_version"}
 
 _LIB = None

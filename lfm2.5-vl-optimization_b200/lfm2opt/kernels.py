@@ -315,4 +315,5 @@ def ext():
         _capi.lib()
         _DEC = DecodeGemvExt()
         _DEC.set_pdl(os.environ.get("LFM2_PDL", "1") != "0")
+        _capi.lib().lfm2q_set_gemv_trigger(int(os.environ.get("LFM2_GEMV_TRIGGER", "late") == "early"))
     return _DEC
