@@ -111,6 +111,13 @@ int lfm2q_gemv(const void *W, int w_is_int8, const float *scale, const uint16_t 
 int lfm2q_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const uint16_t *bias,
                   uint16_t *y, int N, int K, int B, int gelu, void *stream);
 
+/* Per-token W8A8 linear for a few tokens in one launch: the composition quant_rows (kernels/int8_gemm.cpp:83-96)
+ * -> gemm_i8 (kernels/int8_gemm.cpp:39-50) that the reference's Int8Linear.__call__ (src/lfm2opt/int8.py:84-88)
+ * performs for group 0, with the quantization fused into the A8 GEMV. x bf16 [B, K] -> y bf16 [B, N]; identical to
+ * lfm2q_quant_rows + lfm2q_gemm_i8 on the same inputs. Needs K % 64 == 0 (any B: chunks of up to 16 tokens). */
+int lfm2q_linear_a8(const uint16_t *x, const int8_t *W, const float *sw, const uint16_t *bias, uint16_t *y, int N,
+                    int K, int B, int gelu, void *stream);
+
 /* Replaces launch_gemv_epi (kernels/lfm2_decode.cu:818-827) behind gemv_epi (kernels/lfm2_decode.cpp:130-150).
  * Batch 1. epi 0: W = w1|w3 [2S, K] -> y [S] = bf16(bf16(silu(g)) * u).
  *          epi 1: W = in_proj [3S, K] (B|C|x) -> short-conv step, state bf16 [S, 3] updated in place,

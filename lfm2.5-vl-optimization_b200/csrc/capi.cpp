@@ -248,6 +248,17 @@ int lfm2q_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const floa
                   "gemv_a8");
 }
 
+int lfm2q_linear_a8(const uint16_t *x, const int8_t *W, const float *sw, const uint16_t *bias, uint16_t *y, int N,
+                    int K, int B, int gelu, void *stream) {
+  REQUIRE(N > 0 && K > 0 && B >= 1, "x [B, K], y [B, N]: need N > 0, K > 0, B >= 1");
+  REQUIRE(K % 64 == 0 && K <= 16384, "K must be a multiple of 64, <= 16384");
+  REQUIRE(W && sw && x && y, "W, sw, x and y must be non-null");
+  REQUIRE(aligned16(W) && aligned16(x) && aligned16(y) && aligned16(bias), "W, x, bias and y must be 16-byte aligned");
+  if (int e = device_gate()) return e;
+  return launched(launch_linear_a8(x, W, sw, bias, y, N, K, B, gelu != 0, g_pdl.load(), (cudaStream_t)stream),
+                  "linear_a8");
+}
+
 int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int S,
                    int K, uint16_t *state, const uint16_t *cw, const uint16_t *cbias, void *stream) {
   REQUIRE(epi == 0 || epi == 1, "epi 0 (swiglu) or 1 (shortconv)");

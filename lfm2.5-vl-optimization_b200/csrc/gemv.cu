@@ -191,9 +191,11 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], const uint32_t (&a)[4]
 // [kb, ke). Same cp.async ring and software pipeline as warp_gemv; no conversion at all: the 16 bytes a lane holds
 // of rows g and g + 8 feed two m16n8k32 s8 MMAs directly. Lane (g, t), MMA s of a 64-byte step: logical k slots
 // 4t..4t+3 / 16+4t..16+4t+3 take physical bytes 16t+8s..+3 / 16t+8s+4..+7, for W and x alike.
+// phase 0: prefetch + compute; 1: only issue the first GV_RING steps (weights, immutable); 2: compute after phase 1.
 template <int NT>
-__device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const int8_t *__restrict__ xq, int N, int K,
-                                             int B, int r0, int kb, int ke, int (&acc)[NT][4], uint8_t *ring, bool pdl) {
+__device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const int8_t *xq, int xstride, int N, int K,
+                                             int B, int r0, int kb, int ke, int (&acc)[NT][4], uint8_t *ring, bool pdl,
+                                             int phase = 0) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int8_t *row0 = W + (size_t)min(r0 + g, N - 1) * K + kb + t * 16;
   const int8_t *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K + kb + t * 16;
@@ -219,16 +221,19 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
       const int tok = g + 8 * j;
-      xw[j] = tok < B ? __ldg(reinterpret_cast<const uint4 *>(xq + (size_t)tok * K + kb + st * 64 + t * 16))
+      xw[j] = tok < B ? *reinterpret_cast<const uint4 *>(xq + (size_t)tok * xstride + kb + st * 64 + t * 16)
                       : make_uint4(0, 0, 0, 0);
     }
   };
+  if (phase != 2) {
+#pragma unroll
+    for (int st = 0; st < GV_RING; ++st) issue(st);
+  }
+  if (phase == 1) return;
 #pragma unroll
   for (int j = 0; j < NT; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[j][e] = 0;
-#pragma unroll
-  for (int st = 0; st < GV_RING; ++st) issue(st);
   if (pdl) pdl_wait();
   uint4 wc0, wc1, wn0, wn1, xc[NT], xn[NT];
   asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 1) : "memory");
@@ -314,24 +319,67 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__
 // A8 decode GEMV: y[b, n] = bf16(act(((float)(xq[b] . W[n]) * sx[b]) * sw[n] + bias[n])), the per-token W8A8
 // epilogue of gemm_i8 on an exact int32 sum, for 1..16 tokens per launch. Block = RG row groups x KS K-slices;
 // the K-slices' int32 partials are added in shared memory (exact, so the result does not depend on the split).
-template <int NT, int KS, bool GELU>
+// FUSEQ: x is bf16 [B, K]; every block first quantizes it per token into shared memory (rows padded by 64 bytes so
+// the fragment loads are bank-conflict-free), with the quant_rows arithmetic (same scale, same rounding), so one
+// launch computes Int8Linear's per-token W8A8 result for a few tokens.
+template <int NT, int KS, bool GELU, bool FUSEQ>
 __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__restrict__ W, const float *__restrict__ sw,
-                                                             const int8_t *__restrict__ xq, const float *__restrict__ sx,
-                                                             const bf16 *__restrict__ bias, bf16 *__restrict__ y, int N,
-                                                             int K, int B, int pdl) {
+                                                             const int8_t *__restrict__ xq_g, const float *__restrict__ sx_g,
+                                                             const bf16 *__restrict__ xbf, const bf16 *__restrict__ bias,
+                                                             bf16 *__restrict__ y, int N, int K, int B, int pdl) {
   constexpr int RG = 8 / KS;
   extern __shared__ __align__(128) uint8_t rings[];
   __shared__ int red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
+  __shared__ float sx_s[16];
   if (pdl == 2) pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int8_t *xq = xq_g;
+  const float *sx = sx_g;
+  int xstride = K;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
   const int sets = ((N + 15) / 16 + RG - 1) / RG;
+  {
+    // stream the first set's weights before anything waits on the previous kernel
+    int dummy[NT][4];
+    warp_gemv_a8<NT>(W, xq, xstride, N, K, B, (blockIdx.x * RG + rg) * 16, ks * kslice, (ks + 1) * kslice, dummy,
+                     rings + warp * GV_RING * 1024, false, 1);
+  }
+  if (FUSEQ) {
+    int8_t *xs = reinterpret_cast<int8_t *>(rings + 8 * GV_RING * 1024);
+    xstride = K + 64;
+    xq = xs;
+    sx = sx_s;
+    // weights first (the rings are filled inside warp_gemv_a8), so here only x: warp w quantizes tokens w, w + 8
+    if (pdl) pdl_wait();
+    for (int b = warp; b < B; b += 8) {
+      const uint4 *xr = reinterpret_cast<const uint4 *>(xbf + (size_t)b * K);
+      uint32_t m2 = 0;
+      for (int c = lane; c < K / 8; c += 32) {
+        const uint4 v = __ldg(xr + c);
+        m2 = __vmaxu2(m2, __vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu));
+        m2 = __vmaxu2(m2, __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+      }
+      const float sc = __fdiv_rn(fmaxf(warp_max(fmaxf(bf_lo(m2), bf_hi(m2))), 1e-8f), 127.f);
+      const float rinv = __frcp_rn(sc);
+      if (lane == 0) sx_s[b] = sc;
+      for (int c = lane; c < K / 8; c += 32) {
+        const uint4 v = __ldg(xr + c);
+        const uint32_t o0 = pack_sums4(q8r2(make_float2(bf_lo(v.x), bf_hi(v.x)), sc, rinv),
+                                       q8r2(make_float2(bf_lo(v.y), bf_hi(v.y)), sc, rinv));
+        const uint32_t o1 = pack_sums4(q8r2(make_float2(bf_lo(v.z), bf_hi(v.z)), sc, rinv),
+                                       q8r2(make_float2(bf_lo(v.w), bf_hi(v.w)), sc, rinv));
+        *reinterpret_cast<uint2 *>(xs + (size_t)b * xstride + c * 8) = make_uint2(o0, o1);
+      }
+    }
+    __syncthreads();
+  }
   for (int set = blockIdx.x; set < sets; set += gridDim.x) {
     const int r0 = (set * RG + rg) * 16;
     int acc[NT][4];
-    warp_gemv_a8<NT>(W, xq, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc, rings + warp * GV_RING * 1024,
-                     pdl != 0 && set == blockIdx.x);
+    warp_gemv_a8<NT>(W, xq, xstride, N, K, B, r0, ks * kslice, (ks + 1) * kslice, acc,
+                     rings + warp * GV_RING * 1024, !FUSEQ && pdl != 0 && set == blockIdx.x,
+                     set == blockIdx.x ? 2 : 0);
     if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();
     if (KS == 1) {
 #pragma unroll
@@ -429,6 +477,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restri
 }
 
 constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
+constexpr int GV_X_SMEM_MAX = 64 * 1024;  // fused-quantization A8 GEMV: B * (K + 64) bytes of int8 tokens
 bool g_early_trigger = false;
 
 // Launch with the per-warp rings as dynamic shared memory (opt-in above 48 KB, set once per kernel and device) and,
@@ -438,14 +487,16 @@ std::mutex g_attr_mu;
 std::set<std::pair<const void *, int>> g_attr_done;
 
 template <typename KernelT, typename... Args>
-cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, Args... args) {
+cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, size_t extra_smem,
+                      Args... args) {
   int dev = 0;
   cudaGetDevice(&dev);
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
     const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), dev);
     if (!g_attr_done.count(key)) {
-      const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_SMEM);
+      const cudaError_t e =
+          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_SMEM + GV_X_SMEM_MAX);
       if (e != cudaSuccess) return e;
       g_attr_done.insert(key);
     }
@@ -453,7 +504,7 @@ cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStrea
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = GV_DYN_SMEM;
+  cfg.dynamicSmemBytes = GV_DYN_SMEM + extra_smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -472,10 +523,10 @@ cudaError_t gemv_ks(const WT *W, const float *scale, const bf16 *x, bf16 *y, int
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
   switch (ks) {
-    case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
-    case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
-    case 4: return launch_ex(gemv_kernel<WT, NT, 4>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
-    default: return launch_ex(gemv_kernel<WT, NT, 8>, grid, GV_THREADS, pdl, st, W, scale, x, y, N, K, B, p);
+    case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
+    case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
+    case 4: return launch_ex(gemv_kernel<WT, NT, 4>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
+    default: return launch_ex(gemv_kernel<WT, NT, 8>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
   }
 }
 
@@ -510,25 +561,26 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
   const dim3 grid((S + 15) / 16);
   const int p = pdl ? 1 : 0;
   if (epi == 0)
-    return launch_ex(gemv_epi_kernel<WT, 2, 0>, grid, GV_THREADS, pdl, st, W, scale, x, y, S, K, state, cw, cbias, p);
-  return launch_ex(gemv_epi_kernel<WT, 3, 1>, grid, GV_THREADS, pdl, st, W, scale, x, y, S, K, state, cw, cbias, p);
+    return launch_ex(gemv_epi_kernel<WT, 2, 0>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, S, K, state, cw, cbias, p);
+  return launch_ex(gemv_epi_kernel<WT, 3, 1>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, S, K, state, cw, cbias, p);
 }
 
 }  // namespace
 
-template <int NT, bool GELU>
-cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const bf16 *bias, bf16 *y,
-                       int N, int K, int B, int ks, bool pdl, cudaStream_t st) {
+template <int NT, bool GELU, bool FUSEQ>
+cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const bf16 *xbf,
+                       const bf16 *bias, bf16 *y, int N, int K, int B, int ks, bool pdl, cudaStream_t st) {
   const int groups = (N + 15) / 16, rg = 8 / ks;
   const int sets = (groups + rg - 1) / rg;
   const int resident = 4 * device_sm_count();
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
+  const size_t extra = FUSEQ ? (size_t)B * (K + 64) : 0;
   switch (ks) {
-    case 1: return launch_ex(gemv_a8_kernel<NT, 1, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
-    case 2: return launch_ex(gemv_a8_kernel<NT, 2, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
-    case 4: return launch_ex(gemv_a8_kernel<NT, 4, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
-    default: return launch_ex(gemv_a8_kernel<NT, 8, GELU>, grid, GV_THREADS, pdl, st, W, sw, xq, sx, bias, y, N, K, B, p);
+    case 1: return launch_ex(gemv_a8_kernel<NT, 1, GELU, FUSEQ>, grid, GV_THREADS, pdl, st, extra, W, sw, xq, sx, xbf, bias, y, N, K, B, p);
+    case 2: return launch_ex(gemv_a8_kernel<NT, 2, GELU, FUSEQ>, grid, GV_THREADS, pdl, st, extra, W, sw, xq, sx, xbf, bias, y, N, K, B, p);
+    case 4: return launch_ex(gemv_a8_kernel<NT, 4, GELU, FUSEQ>, grid, GV_THREADS, pdl, st, extra, W, sw, xq, sx, xbf, bias, y, N, K, B, p);
+    default: return launch_ex(gemv_a8_kernel<NT, 8, GELU, FUSEQ>, grid, GV_THREADS, pdl, st, extra, W, sw, xq, sx, xbf, bias, y, N, K, B, p);
   }
 }
 
@@ -565,11 +617,38 @@ cudaError_t launch_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, c
     const bf16 *bi = (const bf16 *)bias;
     cudaError_t e;
     if (bs > 8)
-      e = gelu ? gemv_a8_ks<2, true>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st)
-               : gemv_a8_ks<2, false>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st);
+      e = gelu ? gemv_a8_ks<2, true, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<2, false, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st);
     else
-      e = gelu ? gemv_a8_ks<1, true>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st)
-               : gemv_a8_ks<1, false>(W, sw, xb, sb, bi, yb, N, K, bs, ks, pdl, st);
+      e = gelu ? gemv_a8_ks<1, true, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<1, false, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+int gemv_a8_fused_max_tokens(int K) {
+  const int b = GV_X_SMEM_MAX / (K + 64);
+  return b < 16 ? b : 16;
+}
+
+cudaError_t launch_linear_a8(const void *x, const int8_t *W, const float *sw, const void *bias, void *y, int N, int K,
+                             int B, bool gelu, bool pdl, cudaStream_t st) {
+  if (N <= 0 || B <= 0) return cudaSuccess;
+  const int ks = pick_ks(N, K, 64, 0);
+  const int chunk = gemv_a8_fused_max_tokens(K);
+  for (int b0 = 0; b0 < B; b0 += chunk) {
+    const int bs = min(chunk, B - b0);
+    const bf16 *xb = (const bf16 *)x + (size_t)b0 * K;
+    bf16 *yb = (bf16 *)y + (size_t)b0 * N;
+    const bf16 *bi = (const bf16 *)bias;
+    cudaError_t e;
+    if (bs > 8)
+      e = gelu ? gemv_a8_ks<2, true, true>(W, sw, nullptr, nullptr, xb, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<2, false, true>(W, sw, nullptr, nullptr, xb, bi, yb, N, K, bs, ks, pdl, st);
+    else
+      e = gelu ? gemv_a8_ks<1, true, true>(W, sw, nullptr, nullptr, xb, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<1, false, true>(W, sw, nullptr, nullptr, xb, bi, yb, N, K, bs, ks, pdl, st);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -33,6 +33,7 @@ SIGNATURES = {
     "lfm2q_gemv": [_p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
     "lfm2q_gemv_epi": [_i, _p, _i, _p, _p, _p, _i, _i, _p, _p, _p, _p],
     "lfm2q_gemv_a8": [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p],
+    "lfm2q_linear_a8": [_p, _p, _p, _p, _p, _i, _i, _i, _i, _p],
     "lfm2q_set_pdl": [_i],
     "lfm2q_set_gemv_impl": [_i],
     "lfm2q_set_gemm_tile": [_i],

@@ -23,6 +23,8 @@ import torch
 from .kernels import int8_ext
 from .quant import quantize_int8
 
+SMALL_M = 16  # per-token W8A8 calls with at most this many tokens take the fused A8 GEMV
+
 
 def a16_kinds():
     """Layer kinds that keep BF16 activations (W8A16); the rest run W8A8."""
@@ -104,7 +106,10 @@ class Int8Linear:
             return y.view(*xq.shape[:-1], self.N)
         x2 = x.reshape(-1, self.K)
         y = torch.empty(x2.shape[0], self.N, device=x.device, dtype=torch.bfloat16)
-        if self.a8:
+        if self.a8 and self.group == 0 and x2.shape[0] <= SMALL_M and self.K % 64 == 0:
+            # decode-sized batches: quantization fused into the A8 GEMV, one launch, same result
+            self.ext.linear_a8(x2.contiguous(), self.q, self.s, self.bias, y, gelu)
+        elif self.a8:
             xq, sx = quantize_rows(x2.contiguous(), self.group)
             self.ext.gemm_i8(xq, sx, self.q, self.s, self.bias, y, gelu)
         else:

@@ -131,6 +131,18 @@ class Int8GemmExt:
             _capi.call("lfm2q_gemm_i8_silu", xq.data_ptr(), sx.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias),
                        y.data_ptr(), M, I, K, _stream(xq))
 
+    def linear_a8(self, x, w, sw, bias, y, gelu):
+        """Per-token W8A8 for a few tokens in one launch: quant_rows(x) fused into the A8 GEMV, bit-identical to
+        quant_rows followed by gemm_i8 (no counterpart op in the reference)."""
+        _check(x, _BF, "x")
+        K = x.size(-1)
+        M = x.numel() // K
+        N = self._common(w, sw, bias, y, M, K)
+        _req(K % 64 == 0 and K <= 16384, "K must be a multiple of 64, <= 16384")
+        with _DeviceOf(x):
+            _capi.call("lfm2q_linear_a8", x.data_ptr(), w.data_ptr(), sw.data_ptr(), _ptr(bias), y.data_ptr(), N, K, M,
+                       int(bool(gelu)), _stream(x))
+
     def gemm_w8(self, x, w, sw, bias, y, gelu):
         """W8A16: y[M, N] = (x[M, K] . w[N, K]^T) * sw[n] (+ bias) (GELU), bf16 in / out."""
         _check(x, _BF, "x")

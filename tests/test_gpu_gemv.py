@@ -160,3 +160,25 @@ def test_gemv_a8_bit_exact(cuda_dev, N, K, B, gelu):
     r = oracle.gemm_i8_ref(xq, sx, Wq, sw, b, gelu)
     from test_gpu_gemm import assert_close_bf16
     assert_close_bf16(y.cpu(), r, gelu)
+
+
+@pytest.mark.parametrize("N,K", [(3072, 2048), (2048, 8192), (65536, 2048), (264, 1152), (40, 4352)])
+@pytest.mark.parametrize("B", [1, 3, 8, 9, 16, 40])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_linear_a8_fused_quant(cuda_dev, N, K, B, gelu):
+    """quant_rows fused into the A8 GEMV equals quant_rows followed by the gemm_i8 oracle, bit for bit."""
+    if N * K > 40_000_000 and (B not in (1, 16) or gelu):
+        pytest.skip("large shape: a few cases suffice")
+    from lfm2opt.kernels import int8_ext
+    g = torch.Generator().manual_seed(N + 3 * K + B)
+    W = (torch.randn(N, K, generator=g) * 0.02).to(BF)
+    Wq, sw = quantize_int8(W)
+    x = (torch.randn(B, K, generator=g) * (1 + torch.rand(B, 1, generator=g) * 4)).to(BF)
+    b = (torch.randn(N, generator=g) * 0.1).to(BF) if gelu else None
+    y = torch.empty(B, N, device=cuda_dev, dtype=BF)
+    int8_ext().linear_a8(x.to(cuda_dev), Wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y,
+                         gelu)
+    xq, sx = oracle.quant_rows_ref(x)
+    r = oracle.gemm_i8_ref(xq, sx, Wq, sw, b, gelu)
+    from test_gpu_gemm import assert_close_bf16
+    assert_close_bf16(y.cpu(), r, gelu)
