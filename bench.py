@@ -370,7 +370,7 @@ class E2E:
 def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
     """Decode GEMV stack (16 layers + lm_head, distinct weights: 1.17 GB > L2) replayed from a CUDA graph, for both
     decode paths: `w16` = the reference's weight-only GEMV (bf16 activations, lfm2q_gemv) and `a8` = per-token int8
-    activations quantized inside the GEMV (lfm2q_linear_a8: exact int32 sums). Bytes = N*K + 4N + 2BK + 2BN."""
+    activations (lfm2q_quant_rows, then lfm2q_gemv_a8: exact int32 sums). Bytes = N*K + 4N + 2BK + 2BN."""
     from lfm2opt import _capi
     from lfm2opt.kernels import ext
 
@@ -401,9 +401,10 @@ def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
                     K = W.shape[1]
                     if mode == "w16":
                         E.gemv(W, s, xs[K], y)
-                    else:  # per-token quantization fused into the A8 GEMV (what Int8Linear does for <= 16 tokens)
-                        L.lfm2q_linear_a8(xs[K].data_ptr(), W.data_ptr(), s.data_ptr(), None, y.data_ptr(),
-                                          W.shape[0], K, B, 0, stream)
+                    else:  # Int8Linear's a8 flow: quant_rows, then gemm_i8 (routed to the A8 GEMV), both under PDL
+                        L.lfm2q_quant_rows(xs[K].data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), B, K, stream)
+                        L.lfm2q_gemv_a8(W.data_ptr(), s.data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), None,
+                                        y.data_ptr(), W.shape[0], K, B, 0, stream)
 
             st = torch.cuda.Stream(dev)
             st.wait_stream(torch.cuda.current_stream(dev))
@@ -426,7 +427,7 @@ def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
             ms = max_over_ranks(e0.elapsed_time(e1) / replays, world)
             res[mode][B] = {"us_per_sweep": round(ms * 1e3, 2), "gbs": round(world * nbytes / (ms * 1e-3) / 1e9, 1),
                             "bytes_per_sweep": nbytes,
-                            "launches": len(layers)}
+                            "launches": len(layers) * (1 if mode == "w16" else 2)}
             del graph
     return res
 

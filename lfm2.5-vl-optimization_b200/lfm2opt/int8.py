@@ -5,7 +5,8 @@ act_group :27-36, a16_kinds :22-24): same names, arguments, environment variable
 
   a8  (W8A8):  activations quantized on the fly (quantize_rows) with one scale per token (LFM2_INT8_GROUP=0) or per
                token and group of 64 input channels (LFM2_INT8_GROUP=64, the default), int8 x int8 tcgen05 GEMM with
-               the scales, bias and GELU in the epilogue.
+               the scales, bias and GELU in the epilogue (per-token calls of <= 16 tokens run the A8 GEMV inside
+               gemm_i8: same exact int32 sums, same epilogue).
   a16 (W8A16): bf16 activations, int8 weights (LFM2_INT8_A16 lists the layer kinds).
 
 Additions over the reference (all optional, defaults keep the reference's behaviour):
@@ -22,8 +23,6 @@ import torch
 
 from .kernels import int8_ext
 from .quant import quantize_int8
-
-SMALL_M = 16  # per-token W8A8 calls with at most this many tokens take the fused A8 GEMV
 
 
 def a16_kinds():
@@ -106,10 +105,7 @@ class Int8Linear:
             return y.view(*xq.shape[:-1], self.N)
         x2 = x.reshape(-1, self.K)
         y = torch.empty(x2.shape[0], self.N, device=x.device, dtype=torch.bfloat16)
-        if self.a8 and self.group == 0 and x2.shape[0] <= SMALL_M and self.K % 64 == 0:
-            # decode-sized batches: quantization fused into the A8 GEMV, one launch, same result
-            self.ext.linear_a8(x2.contiguous(), self.q, self.s, self.bias, y, gelu)
-        elif self.a8:
+        if self.a8:
             xq, sx = quantize_rows(x2.contiguous(), self.group)
             self.ext.gemm_i8(xq, sx, self.q, self.s, self.bias, y, gelu)
         else:
