@@ -135,7 +135,9 @@ void lfm2q_set_gemv_impl(int impl);
  * (early == 0, default) or at their start (early != 0). Tuning only; results are unchanged. */
 void lfm2q_set_gemv_trigger(int early);
 
-/* Forces the per-token GEMM tile width (128 or 256; 0 = automatic). Tuning and testing only. */
+/* Forces the per-token GEMM tile: 128 or 256 = one CTA per 128-row tile of that many columns; -192 or -256 = a CTA
+ * pair (cluster of two, tcgen05 cta_group::2) per 256-row tile of that many columns; 0 = automatic. The SiLU GEMM
+ * follows the sign (one CTA or a pair, 128 output columns per tile). Tuning and testing only. */
 void lfm2q_set_gemm_tile(int bn);
 
 #ifdef __cplusplus

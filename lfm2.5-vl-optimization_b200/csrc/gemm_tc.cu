@@ -70,22 +70,34 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// CL: acquire at cluster scope, for a barrier that threads of the other CTA of a pair arrive on
+template <bool CL = false>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
+  if (CL)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
   return ok != 0;
 }
 // Bounded wait for the phase with the given parity. Returns false when this or another role gave up.
+template <bool CL = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait<CL>(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait<CL>(bar, parity)) {
     if (*(volatile int *)abort_flag) return false;
     if (clock64() - t0 > WAIT_LIMIT) {
       atomicExch(abort_flag, 1);
@@ -103,6 +115,33 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
+// CTA-pair form: the destination is this CTA's shared memory, the mbarrier may be the pair leader's (a
+// shared::cluster address), so both CTAs' bytes complete one transaction count. No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -117,9 +156,9 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;                    // 128-byte swizzle
   return d;
 }
-// Instruction descriptor: s8 x s8 -> s32, both operands K-major, M = 128
-__host__ __device__ constexpr uint32_t idesc_i8(int n) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+// Instruction descriptor: s8 x s8 -> s32, both operands K-major, M = 128 (one CTA) or 256 (CTA pair)
+__host__ __device__ constexpr uint32_t idesc_i8(int n, int m) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -133,6 +172,24 @@ __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// CTA pair: M = 256 MMA from the leader; A rows 0-127 / B rows [0, N/2) come from the leader's shared memory, A rows
+// 128-255 / B rows [N/2, N) from the same offsets in the peer's, and D lands in both CTAs' TMEM (128 lanes each)
+__device__ __forceinline__ void umma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on the mbarrier at this offset in both CTAs of the pair once the leader's MMAs so far have retired
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -238,16 +295,23 @@ __device__ __forceinline__ void load8b(const bf16 *p, float (&v)[8]) {
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int BN, int STAGES, int NACC, int EPI, bool GELU>
+// CG = 1: one CTA per 128 x BN tile. CG = 2: a cluster of two CTAs (a CTA pair) per 256 x BN tile; CTA r loads A
+// rows 128r.. and B rows [r BN/2, (r+1) BN/2) of the tile (SILU: r = 0 the gate rows, r = 1 the up rows), the leader
+// (r = 0) issues the M = 256 MMAs, and each CTA's epilogue drains its own 128 TMEM lanes. Per SM this halves the B
+// bytes staged in shared memory and cuts the L2 -> SM bytes per MMA by a third against one CTA on a 128 x 256 tile.
+template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmY, const GemmArgs args) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN / CG, STAGES>;  // per CTA: A 128 rows, B BN / CG rows per stage
   constexpr bool GROUPED = (EPI == EPI_GROUP || EPI == EPI_GROUP_Q);
-  constexpr int TMEM_COLS = NACC * BN;
-  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(NACC * BN <= 512, "accumulators exceed TMEM");
+  constexpr int TMEM_COLS = NACC * BN <= 256 ? 256 : 512;  // allocations are powers of two
   static_assert(!GROUPED || BN == 128, "grouped tiles are 128 columns wide");
-  constexpr uint32_t IDESC = idesc_i8(BN);
+  static_assert(CG == 1 || (CG == 2 && !GROUPED && BN % 32 == 0), "CTA pairs run the per-token epilogues");
+  static_assert(EPI != EPI_SILU || BN == 256, "the SiLU tile holds 128 gate and 128 up rows");
+  constexpr int TMU = TM * CG;  // output rows per tile
+  constexpr uint32_t IDESC = idesc_i8(BN, TMU);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -265,27 +329,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int KB = (K + TK - 1) / TK;      // pipeline stages per tile
   const int G = K / 64;                  // grouped: 64-wide K groups (K % 64 == 0)
   const int tiles = args.tiles_m * args.tiles_n;
+  // work unit = one CTA (CG = 1) or one CTA pair (CG = 2, consecutive blockIdx.x form a cluster)
+  const int unit = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  // shared::cluster address of a barrier in the pair leader (its own address when CG = 1)
+  auto lead = [&](uint32_t bar) { return CG == 2 ? mapa_shared(bar, 0) : bar; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full(s), 1);
-      mbar_init(bar_empty(s), 1);
+      mbar_init(bar_full(s), 1);   // leader: its producer's arrive (expect_tx for both CTAs' bytes)
+      mbar_init(bar_empty(s), 1);  // every CTA: one commit from the (leader's) MMA thread
     }
     for (int a = 0; a < 4; ++a) {
       mbar_init(bar_tfull(a), 1);
-      mbar_init(bar_tempty(a), EPI_WARPS);  // one arrival per epilogue warp
+      mbar_init(bar_tempty(a), EPI_WARPS * CG);  // one arrival per epilogue warp of every CTA of the unit
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (CG == 2) {  // the same warp of both CTAs allocates the pair's TMEM, same columns in both
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrive or transaction
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -296,21 +376,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tma_prefetch_desc(&tmB);
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      for (int tile = unit; tile < tiles; tile += units) {
         int mt, nt;
         tile_coord(tile, args, mt, nt);
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(bar_empty(stage), phase ^ 1, abort_flag)) goto producer_done;
-          mbar_expect_tx(bar_full(stage), L::A_BYTES + L::B_BYTES);
           const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
           const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
-          tma_load_2d(sa, &tmA, bar_full(stage), kb * TK, mt * TM);
-          if (EPI == EPI_SILU) {
-            tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * (BN / 2));
-            tma_load_2d(sb + (BN / 2) * TK, &tmB, bar_full(stage), kb * TK, args.Nout + nt * (BN / 2));
+          if constexpr (CG == 2) {
+            const uint32_t fb = lead(bar_full(stage));
+            if (rank == 0) mbar_expect_tx(bar_full(stage), 2 * (L::A_BYTES + L::B_BYTES));
+            tma_load_2d_pair(sa, &tmA, fb, kb * TK, mt * TMU + (int)rank * TM);
+            const int brow = (EPI == EPI_SILU) ? (rank ? args.Nout : 0) + nt * (BN / 2) : nt * BN + (int)rank * (BN / 2);
+            tma_load_2d_pair(sb, &tmB, fb, kb * TK, brow);
           } else {
-            tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * BN);
+            mbar_expect_tx(bar_full(stage), L::A_BYTES + L::B_BYTES);
+            tma_load_2d(sa, &tmA, bar_full(stage), kb * TK, mt * TM);
+            if (EPI == EPI_SILU) {
+              tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * (BN / 2));
+              tma_load_2d(sb + (BN / 2) * TK, &tmB, bar_full(stage), kb * TK, args.Nout + nt * (BN / 2));
+            } else {
+              tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * BN);
+            }
           }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // CTA pair: wait until every stage has been released once more, so no commit from the leader is still on its
+      // way to this CTA's barriers when it exits
+      if constexpr (CG == 2) {
+        for (int i = 0; i < STAGES; ++i) {
+          if (!mbar_wait(bar_empty(stage), phase ^ 1, abort_flag)) break;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -320,15 +419,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     producer_done:;
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer (the leader's, for a CTA pair)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t aphase = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      for (int tile = unit; tile < tiles; tile += units) {
         if (!GROUPED) {
-          if (!mbar_wait(bar_tempty(acc), aphase ^ 1, abort_flag)) goto mma_done;
+          if (!mbar_wait<CG == 2>(bar_tempty(acc), aphase ^ 1, abort_flag)) goto mma_done;
           tc_fence_after();
           const uint32_t d = tmem_base + acc * BN;
           for (int kb = 0; kb < KB; ++kb) {
@@ -337,15 +436,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint64_t ad = sw128_desc(sbase + L::A_OFF + stage * L::A_BYTES);
             const uint64_t bd = sw128_desc(sbase + L::B_OFF + stage * L::B_BYTES);
 #pragma unroll
-            for (int k = 0; k < TK / 32; ++k)  // +32 bytes of K per MMA = +2 in the 16-byte address field
-              umma_i8(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
-            umma_commit(bar_empty(stage));
+            for (int k = 0; k < TK / 32; ++k) {  // +32 bytes of K per MMA = +2 in the 16-byte address field
+              if constexpr (CG == 2)
+                umma_i8_pair(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+              else
+                umma_i8(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+            }
+            if constexpr (CG == 2)
+              umma_commit_pair(bar_empty(stage));
+            else
+              umma_commit(bar_empty(stage));
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1;
             }
           }
-          umma_commit(bar_tfull(acc));
+          if constexpr (CG == 2)
+            umma_commit_pair(bar_tfull(acc));
+          else
+            umma_commit(bar_tfull(acc));
           if (++acc == NACC) {
             acc = 0;
             aphase ^= 1;
@@ -404,7 +513,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (tile_i >= tiles) return;
       int pmt, pnt;
       tile_coord(tile_i, args, pmt, pnt);
-      const int pm = pmt * TM + row;
+      const int pm = pmt * TMU + (int)rank * TM + row;
       pf_sx = (pm < M && !GROUPED) ? __ldg(args.sa + pm) : 0.f;
       const int width = (EPI == EPI_SILU) ? BN / 4 : BN / 2;
       const int c0 = (EPI == EPI_SILU) ? pnt * (BN / 2) + half * width : pnt * BN + half * width;
@@ -451,23 +560,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto release_acc = [&]() {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_tempty(acc));
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_cluster(lead(bar_tempty(acc)));
+        else
+          mbar_arrive(bar_tempty(acc));
+      }
       if (++acc == NACC) {
         acc = 0;
         aphase ^= 1;
       }
     };
 
-    prefetch(blockIdx.x);
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    prefetch(unit);
+    for (int tile = unit; tile < tiles; tile += units) {
       int mt, nt;
       tile_coord(tile, args, mt, nt);
-      const int m = mt * TM + row;
+      const int r0 = mt * TMU + (int)rank * TM;  // first row of this CTA's part of the tile
+      const int m = r0 + row;
       const bool mrow = m < M;
-      const int yrow = mt * TM + q * 32;  // first output row of this warp's blocks
+      const int yrow = r0 + q * 32;  // first output row of this warp's blocks
       const float sxm = pf_sx;
       stage_params();
-      prefetch(tile + gridDim.x);
+      prefetch(tile + units);
       if (EPI == EPI_TOKEN) {
         constexpr int CW = BN / 2, NCH = CW / 32;  // this warp's columns
         const int c0 = nt * BN + half * CW;
@@ -604,11 +719,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // the peer's last remote arrivals have landed and its epilogue has left TMEM
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
-                 : "memory");
+    if constexpr (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                   : "memory");
   }
 }
 
@@ -657,20 +780,41 @@ bool make_map(CUtensorMap *map, const void *ptr, int inner, int rows, int box_ro
 
 int g_tile_override = 0;
 
-template <int BN, int STAGES, int NACC, int EPI, bool GELU>
+template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
 cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) {
-  using L = Smem<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES, NACC, EPI, GELU>;
+  using L = Smem<BN / CG, STAGES>;
+  auto kern = gemm_tc_kernel<BN, STAGES, NACC, EPI, GELU, CG>;
   static std::once_flag once[64];
+  static int max_units[64];  // co-resident work units (CTAs, or CTA pairs) per device
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = CG > 1 ? 1 : 0;
   std::call_once(once[dev & 63], [&] {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    int n = device_sm_count() / CG;
+    if (attr_err == cudaSuccess && CG > 1) {
+      cudaLaunchConfig_t q = cfg;
+      q.gridDim = dim3(CG * n);
+      int c = 0;
+      if (cudaOccupancyMaxActiveClusters(&c, kern, &q) == cudaSuccess && c > 0) n = c < n ? c : n;
+      cudaGetLastError();
+    }
+    max_units[dev & 63] = n;
   });
   if (attr_err != cudaSuccess) return attr_err;
   CUtensorMap ta, tb, ty;
-  const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN;
+  const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN / CG;
   if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, box_b)) return cudaErrorInvalidValue;
   if (EPI == EPI_GROUP_Q) {
     memset(&ty, 0, sizeof(ty));  // int8 output: written with plain stores, the map is unused
@@ -678,12 +822,13 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
     return cudaErrorInvalidValue;
   }
   const int tiles = a.tiles_m * a.tiles_n;
-  const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
-  kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, ty, a);
-  return cudaGetLastError();
+  const int units = tiles < max_units[dev & 63] ? tiles : max_units[dev & 63];
+  cfg.gridDim = dim3(CG * units);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, a);
 }
 
-GemmArgs base_args(const float *sa, const float *sb, const void *bias, int M, int N, int K, int nout, int tile_n) {
+GemmArgs base_args(const float *sa, const float *sb, const void *bias, int M, int N, int K, int nout, int tile_n,
+                   int tile_m = TM) {
   GemmArgs a = {};
   a.sa = sa;
   a.sb = sb;
@@ -692,7 +837,7 @@ GemmArgs base_args(const float *sa, const float *sb, const void *bias, int M, in
   a.N = N;
   a.K = K;
   a.Nout = nout;
-  a.tiles_m = (M + TM - 1) / TM;
+  a.tiles_m = (M + tile_m - 1) / tile_m;
   a.tiles_n = (nout + tile_n - 1) / tile_n;
   a.m_fast = M <= nout ? 1 : 0;  // walk the dimension whose operand is smaller, so it stays in L2
   return a;
@@ -710,7 +855,9 @@ int gemm_device_error(bool clear) {
   return v;
 }
 
-void gemm_set_tile_override(int bn) { g_tile_override = (bn == 128 || bn == 256) ? bn : 0; }
+void gemm_set_tile_override(int bn) {
+  g_tile_override = (bn == 128 || bn == 256 || bn == -192 || bn == -256) ? bn : 0;
+}
 
 cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias, void *Y,
                            int M, int N, int K, bool gelu, bool grouped, cudaStream_t st) {
@@ -718,7 +865,7 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
   if (grouped) {
     GemmArgs a = base_args(sa, sb, bias, M, N, K, N, 128);
     a.Y = (bf16 *)Y;
-    return gelu ? run_tc<128, 6, 4, EPI_GROUP, true>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false>(A, B, a, st);
+    return gelu ? run_tc<128, 6, 4, EPI_GROUP, true, 1>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false, 1>(A, B, a, st);
   }
   if (M <= 16 && K % 64 == 0 && !g_tile_override) {
     // skinny: the A8 GEMV streams W once with int8 MMAs (same exact int32 sums and the same epilogue)
@@ -726,14 +873,27 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
   }
   int bn = g_tile_override;
   if (!bn) {
+    // enough 128 x 256 tiles to fill the GPU: 256 x 256 CTA-pair tiles from K = 2048 up (measured 3-5% faster there),
+    // one CTA per 128 x 256 tile below (the pair waits for the slower of its two epilogues, which short K exposes);
+    // otherwise one CTA per 128 x 128 tile for more parallelism
     const long tiles256 = (long)((M + TM - 1) / TM) * ((N + 255) / 256);
-    bn = tiles256 >= device_sm_count() ? 256 : 128;
+    if (tiles256 >= device_sm_count())
+      bn = K >= 2048 ? -256 : 256;
+    else
+      bn = 128;
   }
-  GemmArgs a = base_args(sa, sb, bias, M, N, K, N, bn);
+  GemmArgs a = base_args(sa, sb, bias, M, N, K, N, bn < 0 ? -bn : bn, bn < 0 ? 2 * TM : TM);
   a.Y = (bf16 *)Y;
+  if (bn == -256)
+    return gelu ? run_tc<256, 6, 2, EPI_TOKEN, true, 2>(A, B, a, st)
+                : run_tc<256, 6, 2, EPI_TOKEN, false, 2>(A, B, a, st);
+  if (bn == -192)
+    return gelu ? run_tc<192, 6, 2, EPI_TOKEN, true, 2>(A, B, a, st)
+                : run_tc<192, 6, 2, EPI_TOKEN, false, 2>(A, B, a, st);
   if (bn == 256)
-    return gelu ? run_tc<256, 4, 2, EPI_TOKEN, true>(A, B, a, st) : run_tc<256, 4, 2, EPI_TOKEN, false>(A, B, a, st);
-  return gelu ? run_tc<128, 6, 2, EPI_TOKEN, true>(A, B, a, st) : run_tc<128, 6, 2, EPI_TOKEN, false>(A, B, a, st);
+    return gelu ? run_tc<256, 4, 2, EPI_TOKEN, true, 1>(A, B, a, st)
+                : run_tc<256, 4, 2, EPI_TOKEN, false, 1>(A, B, a, st);
+  return gelu ? run_tc<128, 6, 2, EPI_TOKEN, true, 1>(A, B, a, st) : run_tc<128, 6, 2, EPI_TOKEN, false, 1>(A, B, a, st);
 }
 
 cudaError_t launch_gemm_i8_q(const int8_t *A, const float *saT, const int8_t *B, const float *sb, const void *bias,
@@ -742,16 +902,21 @@ cudaError_t launch_gemm_i8_q(const int8_t *A, const float *saT, const int8_t *B,
   GemmArgs a = base_args(saT, sb, bias, M, N, K, N, 128);
   a.Yq = Yq;
   a.YsT = YsT;
-  return gelu ? run_tc<128, 6, 4, EPI_GROUP_Q, true>(A, B, a, st)
-              : run_tc<128, 6, 4, EPI_GROUP_Q, false>(A, B, a, st);
+  return gelu ? run_tc<128, 6, 4, EPI_GROUP_Q, true, 1>(A, B, a, st)
+              : run_tc<128, 6, 4, EPI_GROUP_Q, false, 1>(A, B, a, st);
 }
 
 cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias,
                                 void *Y, int M, int I, int K, cudaStream_t st) {
   if (M <= 0 || I <= 0) return cudaSuccess;
-  GemmArgs a = base_args(sa, sb, bias, M, 2 * I, K, I, 128);
+  // CTA pairs (256 rows x 128 output columns per tile) when one-CTA tiles would fill the GPU, unless a one-CTA tile
+  // width is forced
+  const long tiles1 = (long)((M + TM - 1) / TM) * ((I + 127) / 128);
+  const bool pair = g_tile_override < 0 || (g_tile_override == 0 && tiles1 >= device_sm_count());
+  GemmArgs a = base_args(sa, sb, bias, M, 2 * I, K, I, 128, pair ? 2 * TM : TM);
   a.Y = (bf16 *)Y;
-  return run_tc<256, 4, 2, EPI_SILU, false>(A, B, a, st);
+  if (pair) return run_tc<256, 6, 2, EPI_SILU, false, 2>(A, B, a, st);
+  return run_tc<256, 4, 2, EPI_SILU, false, 1>(A, B, a, st);
 }
 
 }  // namespace lfm2q

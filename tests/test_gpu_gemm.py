@@ -45,8 +45,10 @@ def make(M, K, N, bias, seed, outlier_ch=False):
     return x, w, b
 
 
-@pytest.fixture(params=[0, 128, 256], ids=["auto", "bn128", "bn256"])
+@pytest.fixture(params=[0, 128, 256, -192, -256], ids=["auto", "bn128", "bn256", "pair192", "pair256"])
 def tile(request):
+    """Tile override: 0 = automatic; 128 / 256 = one CTA per 128 x that many columns; -192 / -256 = a CTA pair
+    (cluster of 2, tcgen05 cta_group::2) per 256 x that many columns."""
     _capi.lib().lfm2q_set_gemm_tile(request.param)
     yield request.param
     _capi.lib().lfm2q_set_gemm_tile(0)
@@ -55,7 +57,8 @@ def tile(request):
 TOKEN_CASES = [(9216, 1152, 3456, True, False), (9216, 1152, 4304, True, True), (2327, 2048, 16384, False, False),
                (272, 2048, 3072, False, False), (17, 2048, 2048, False, False), (1, 1152, 1152, True, False),
                (300, 1152, 1152, True, True), (16, 2048, 8192, False, False), (130, 4304, 1152, False, False),
-               (129, 144, 264, True, False), (5, 16, 8, False, False), (4096, 8192, 2048, False, False)]
+               (129, 144, 264, True, False), (5, 16, 8, False, False), (4096, 8192, 2048, False, False),
+               (383, 1152, 200, True, True), (640, 2048, 1152, True, False)]
 
 
 @pytest.mark.parametrize("M,K,N,bias,gelu", TOKEN_CASES)
@@ -157,9 +160,18 @@ def test_gemm_i8_q(cuda_dev, M, K, N, bias, gelu):
         assert torch.equal(q.cpu(), oq) and torch.equal(s.cpu(), os_)
 
 
+@pytest.fixture(params=[0, 256, -256], ids=["auto", "one_cta", "pair"])
+def silu_tile(request):
+    _capi.lib().lfm2q_set_gemm_tile(request.param)
+    yield request.param
+    _capi.lib().lfm2q_set_gemm_tile(0)
+
+
 @pytest.mark.parametrize("M,K,I", [(4096, 2048, 8192), (1024, 2048, 8192), (17, 2048, 8192), (300, 1152, 264),
-                                   (1, 64, 8)])
-def test_gemm_i8_silu(cuda_dev, M, K, I):
+                                   (1, 64, 8), (385, 2048, 200)])
+def test_gemm_i8_silu(cuda_dev, silu_tile, M, K, I):
+    if silu_tile and M * I > 20_000_000:
+        pytest.skip("forced tiles: the automatic run covers the big shapes")
     x, w, _ = make(M, K, 2 * I, False, M * 3 + I)
     xq, sx = quantize_rows(x.to(cuda_dev))
     wq, sw = quantize_int8(w)
