@@ -134,6 +134,26 @@ __device__ __forceinline__ float epi_token(int acc, float sxm, float sw, float b
   return y;
 }
 
+// The first product of two adjacent columns is one packed f32x2 multiply; the scale-and-bias step stays scalar:
+// ptxas may contract a packed mul.rn.f32x2 feeding an add into a fused multiply-add (observed on sm_100a), which
+// would skip the reference's rounding of the product. Each value is rounded as in epi_token, bit for bit.
+__device__ __forceinline__ float2 epi_pair(uint32_t acc0, uint32_t acc1, float sxm, float sw0, float sw1, float b0,
+                                           float b1) {
+  const float2 y = fmul2(make_float2((float)(int)acc0, (float)(int)acc1), make_float2(sxm, sxm));
+  return make_float2(__fadd_rn(__fmul_rn(y.x, sw0), b0), __fadd_rn(__fmul_rn(y.y, sw1), b1));
+}
+// Two adjacent columns of epi_token, returned as two packed bf16.
+template <bool GELU>
+__device__ __forceinline__ uint32_t epi_token2(uint32_t acc0, uint32_t acc1, float sxm, float sw0, float sw1,
+                                               float b0, float b1) {
+  float2 y = epi_pair(acc0, acc1, sxm, sw0, sw1, b0, b1);
+  if (GELU) {
+    y.x = gelu_tanh(y.x);
+    y.y = gelu_tanh(y.y);
+  }
+  return pack_bf16x2(y.x, y.y);
+}
+
 // ------------------------------------------------------------------ programmatic dependent launch
 // A kernel launched with programmatic stream serialization may start while its predecessor drains.
 // Before pdl_wait() it may only read immutable data (weights); pdl_wait() returns once the previous

@@ -13,15 +13,20 @@
 //   EPI_SILU    weight rows [0, I) = gate, [I, 2I) = up; g, u = bf16 of the per-token epilogue;
 //               y[m, n] = bf16( bf16(silu(g)) * u ),  silu(g) = g / (1 + __expf(-g)),  y is [M, I]
 //
-// B200 structure (one persistent CTA per SM, 192 threads, warp-specialised):
+// B200 structure (one persistent CTA per SM, 320 threads, warp-specialised):
 //   warp 0      TMA producer: 128 x 128-byte A tile and BN x 128-byte B tile per stage, 128-byte swizzle,
 //               OOB rows / K columns zero-filled by the copy engine (M, N and K tails need no code)
-//   warp 1      allocates TMEM and issues tcgen05.mma.cta_group::1.kind::i8 (M=128, N=BN, K=32) from one thread;
+//   warp 1      allocates TMEM and issues tcgen05.mma.kind::i8 (K = 32 per instruction) from one thread;
 //               tcgen05.commit releases a smem stage when its MMAs retire and hands a finished accumulator over
-//   warps 2-5   epilogue: tcgen05.ld (32 lanes x 32 columns per load) -> fp32 math -> global stores; each thread
-//               owns one output row, so per-row scales and the QOUT row-group maxima stay in registers
-//   TMEM        512 columns: 2 accumulators of 256 (TOKEN / SILU) or 4 of 128 (GROUP: one per 64-wide K group, so
-//               the int32 partial sums of group g are folded while the MMAs of groups g+1.. run)
+//   warps 2-9   epilogue, two warps per TMEM lane quarter (one per half of the tile's columns): tcgen05.ld
+//               (32 lanes x 32 columns per load) -> fp32 math -> a per-warp shared-memory transpose -> coalesced
+//               16-byte global stores; each thread owns one output row, so per-row scales and the QOUT row-group
+//               maxima stay in registers
+//   TMEM        2 accumulators of BN columns (TOKEN / SILU) or 4 of 128 (GROUP: one per 64-wide K group, so the
+//               int32 partial sums of group g are folded while the MMAs of groups g+1.. run)
+//   CTA pairs   (CG = 2, per-token and SiLU epilogues at large M x N): a cluster of two CTAs computes a 256-row tile
+//               with tcgen05 cta_group::2 — each CTA stages its 128 A rows and half of the tile's B rows, the
+//               leader issues M = 256 MMAs into both CTAs' TMEM.
 // Every mbarrier wait is bounded (~1 s of SM clocks). On expiry the kernel records an error code in a device word,
 // tells the other roles to stop through shared memory, frees its TMEM and returns; the host reads the code.
 #include <cuda.h>
@@ -139,8 +144,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Arrive on a barrier of either CTA of the pair (release at CTA scope: what it orders is this thread's completed
+// TMEM reads, made visible to the MMA by the tcgen05 fences around the barrier; a cluster-scope release would also
+// wait for every global store this thread has in flight)
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -206,16 +214,14 @@ __device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
       :
       : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(x), "r"(y)
-               : "memory");
+__device__ __forceinline__ void st_shared16(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read2() { asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ uint4 ld_shared16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -264,35 +270,13 @@ struct Smem {
   // epilogue: per-warp staging of its columns' weight scales and bias (2 x 128 fp32 per warp)
   static constexpr int PAR_OFF = ((MISC_OFF + 16 + 1023) / 1024) * 1024;
   static constexpr int PAR_FLOATS = 256;
-  // epilogue: per-warp double-buffered 32 x 16 bf16 output blocks (32-byte rows, 32-byte swizzle) for TMA stores
+  // epilogue: per-warp 32 x 32 bf16 output block (64-byte rows), the transpose buffer for coalesced stores
   static constexpr int OUT_OFF = PAR_OFF + EPI_WARPS * PAR_FLOATS * 4;
-  static constexpr int OUT_BLOCK = 32 * 32;
-  static constexpr int OUT_BUFS = 3;
-  static constexpr int BYTES = OUT_OFF + EPI_WARPS * OUT_BUFS * OUT_BLOCK;
+  static constexpr int OUT_BLOCK = 32 * 64;
+  static constexpr int BYTES = OUT_OFF + EPI_WARPS * OUT_BLOCK;
   static constexpr int ALLOC = BYTES + 1024;  // room to align the base to 1024
   static_assert(ALLOC <= 232448, "shared memory per block");
 };
-
-// ------------------------------------------------------------------ epilogue helpers
-__device__ __forceinline__ void load8f(const float *p, float (&v)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
-  const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-__device__ __forceinline__ void load8b(const bf16 *p, float (&v)[8]) {
-  if (p == nullptr) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0.f;
-    return;
-  }
-  const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p));
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = bf_lo(w[i]);
-    v[2 * i + 1] = bf_hi(w[i]);
-  }
-}
 
 // ------------------------------------------------------------------ the kernel
 // CG = 1: one CTA per 128 x BN tile. CG = 2: a cluster of two CTAs (a CTA pair) per 256 x BN tile; CTA r loads A
@@ -302,7 +286,7 @@ __device__ __forceinline__ void load8b(const bf16 *p, float (&v)[8]) {
 template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmY, const GemmArgs args) {
+                   const GemmArgs args) {
   using L = Smem<BN / CG, STAGES>;  // per CTA: A 128 rows, B BN / CG rows per stage
   constexpr bool GROUPED = (EPI == EPI_GROUP || EPI == EPI_GROUP_Q);
   static_assert(NACC * BN <= 512, "accumulators exceed TMEM");
@@ -499,8 +483,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * L::PAR_FLOATS;  // [128] weight scales
     float *par_b = par_sw + 128;                                                           // [128] bias
-    const uint32_t out_base = sbase + L::OUT_OFF + ew * L::OUT_BUFS * L::OUT_BLOCK;
-    uint32_t out_count = 0;  // 32 x 16 blocks this warp has handed to the TMA engine
+    const uint32_t out_buf = sbase + L::OUT_OFF + ew * L::OUT_BLOCK;
     int acc = 0;
     uint32_t aphase = 0;
 
@@ -537,25 +520,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       __syncwarp();
     };
-    // Hand a 32-row x 16-column bf16 block (this lane's row: 8 packed words) to the TMA engine at (column x, row y).
-    auto store_block = [&](const uint32_t *o, int x, int y) {
-      const uint32_t buf = out_base + (out_count % L::OUT_BUFS) * L::OUT_BLOCK;
-      if (lane == 0) bulk_wait_read2();  // the buffer's previous store (3 blocks ago) has finished reading it
-      __syncwarp();
+    // Store a 32-row x 32-column bf16 block (this lane's row: 16 packed words, 64 bytes) at (column x, row y0):
+    // transposed through the warp's shared buffer so that each 16-byte global store instruction writes 8 whole
+    // 64-byte row segments (4 lanes per row) instead of 32 scattered pieces. The 16-byte unit j of row r sits at
+    // unit j ^ ((r >> 1) & 3), which keeps both the row-wise writes and the transposed reads free of bank
+    // conflicts. Rows >= M and columns >= Nout (Nout % 8 == 0) are skipped. Plain stores keep the TMA engine free
+    // for the operand loads.
+    auto store_chunk = [&](const uint32_t *o, int x, int y0) {
+      const uint32_t sw = (uint32_t)((lane >> 1) & 3);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t addr = buf + lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(o[4 * j]), "r"(o[4 * j + 1]),
-                     "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
-                     : "memory");
-      }
-      fence_proxy_async_smem();
+      for (int j = 0; j < 4; ++j)
+        st_shared16(out_buf + lane * 64 + ((j ^ sw) << 4), o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
       __syncwarp();
-      if (lane == 0) {
-        tma_store_2d(&tmY, buf, x, y);
-        bulk_commit();
+      const int c = lane & 3;
+      const int col = x + 8 * c;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int r = 8 * t + (lane >> 2);
+        const uint4 v = ld_shared16(out_buf + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+        const int grow = y0 + r;
+        if (grow < M && col < args.Nout) *reinterpret_cast<uint4 *>(args.Y + (size_t)grow * args.Nout + col) = v;
       }
-      ++out_count;
+      __syncwarp();
     };
     auto release_acc = [&]() {
       tc_fence_before();
@@ -598,13 +584,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, r[nxt]);
           else release_acc();  // every column of this warp is in registers
           uint32_t o[16];
+          const float4 *ps = reinterpret_cast<const float4 *>(par_sw + c * 32);  // broadcast 16-byte reads
+          const float4 *pb = reinterpret_cast<const float4 *>(par_b + c * 32);
 #pragma unroll
-          for (int j = 0; j < 32; j += 2)
-            o[j / 2] = pack_bf16x2(epi_token<GELU>((int)r[cur][j], sxm, par_sw[c * 32 + j], par_b[c * 32 + j]),
-                                   epi_token<GELU>((int)r[cur][j + 1], sxm, par_sw[c * 32 + j + 1],
-                                                   par_b[c * 32 + j + 1]));
-          store_block(o, c0 + c * 32, yrow);
-          store_block(o + 8, c0 + c * 32 + 16, yrow);
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 s4 = ps[j4], b4 = pb[j4];
+            o[2 * j4] = epi_token2<GELU>(r[cur][4 * j4], r[cur][4 * j4 + 1], sxm, s4.x, s4.y, b4.x, b4.y);
+            o[2 * j4 + 1] = epi_token2<GELU>(r[cur][4 * j4 + 2], r[cur][4 * j4 + 3], sxm, s4.z, s4.w, b4.z, b4.w);
+          }
+          store_chunk(o, c0 + c * 32, yrow);
           if (c + 1 < NCH) tmem_wait_tie(r[nxt]);
         }
       } else if (EPI == EPI_SILU) {
@@ -626,20 +614,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t o[16];
+          const float4 *pgs = reinterpret_cast<const float4 *>(par_sw + c * 32);  // broadcast 16-byte reads
+          const float4 *pgb = reinterpret_cast<const float4 *>(par_b + c * 32);
+          const float4 *pus = reinterpret_cast<const float4 *>(par_sw + CW + c * 32);
+          const float4 *pub = reinterpret_cast<const float4 *>(par_b + CW + c * 32);
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float out[2];
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 gs = pgs[j4], gb = pgb[j4], us = pus[j4], ub = pub[j4];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int i = c * 32 + j + h;
-              const float g = rbf(epi_token<false>((int)rg[c][j + h], sxm, par_sw[i], par_b[i]));
-              const float u = rbf(epi_token<false>((int)ru[c][j + h], sxm, par_sw[CW + i], par_b[CW + i]));
-              out[h] = rbf(__fdividef(g, 1.f + __expf(-g))) * u;
+              const int j = 4 * j4 + 2 * h;
+              const float2 g = epi_pair(rg[c][j], rg[c][j + 1], sxm, h ? gs.z : gs.x, h ? gs.w : gs.y,
+                                        h ? gb.z : gb.x, h ? gb.w : gb.y);
+              const float2 u = epi_pair(ru[c][j], ru[c][j + 1], sxm, h ? us.z : us.x, h ? us.w : us.y,
+                                        h ? ub.z : ub.x, h ? ub.w : ub.y);
+              const float g0 = rbf(g.x), g1 = rbf(g.y);
+              const float2 sg = make_float2(rbf(__fdividef(g0, 1.f + __expf(-g0))), rbf(__fdividef(g1, 1.f + __expf(-g1))));
+              const float2 y = fmul2(sg, make_float2(rbf(u.x), rbf(u.y)));
+              o[j / 2] = pack_bf16x2(y.x, y.y);
             }
-            o[j / 2] = pack_bf16x2(out[0], out[1]);
           }
-          store_block(o, c0 + c * 32, yrow);
-          store_block(o + 8, c0 + c * 32 + 16, yrow);
+          store_chunk(o, c0 + c * 32, yrow);
         }
       } else {
         // grouped: fold every 64-wide K group into fp32 running sums held in registers (64 columns per warp)
@@ -673,19 +668,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!ok) break;
         if (EPI == EPI_GROUP) {
 #pragma unroll
-          for (int c = 0; c < CW; c += 16) {
-            uint32_t o[8];
+          for (int c = 0; c < CW; c += 32) {
+            uint32_t o[16];
+            const float4 *ps = reinterpret_cast<const float4 *>(par_sw + c);  // broadcast 16-byte reads
+            const float4 *pb = reinterpret_cast<const float4 *>(par_b + c);
 #pragma unroll
-            for (int j = 0; j < 16; j += 2) {
-              float y0 = __fadd_rn(__fmul_rn(f[c + j], par_sw[c + j]), par_b[c + j]);
-              float y1 = __fadd_rn(__fmul_rn(f[c + j + 1], par_sw[c + j + 1]), par_b[c + j + 1]);
-              if (GELU) {
-                y0 = gelu_tanh(y0);
-                y1 = gelu_tanh(y1);
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 s4 = ps[j4], b4 = pb[j4];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int j = c + 4 * j4 + 2 * h;
+                float2 y = make_float2(__fadd_rn(__fmul_rn(f[j], h ? s4.z : s4.x), h ? b4.z : b4.x),
+                                       __fadd_rn(__fmul_rn(f[j + 1], h ? s4.w : s4.y), h ? b4.w : b4.y));
+                if (GELU) {
+                  y.x = gelu_tanh(y.x);
+                  y.y = gelu_tanh(y.y);
+                }
+                o[2 * j4 + h] = pack_bf16x2(y.x, y.y);
               }
-              o[j / 2] = pack_bf16x2(y0, y1);
             }
-            store_block(o, c0 + c, yrow);
+            store_chunk(o, c0 + c, yrow);
           }
         } else if (mrow) {
           // QOUT: bf16-round the outputs, then one scale per (row, 64 columns): this warp's 64 columns are one
@@ -714,8 +716,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
     }
-    if (lane == 0) bulk_wait_all();  // every TMA store of this warp has completed
-    __syncwarp();
   }
 
   tc_fence_before();
@@ -747,21 +747,6 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   });
   return fn;
-}
-
-// bf16 output [rows, cols] row-major, stored in 32-row x 16-column blocks from 32-byte-swizzled shared memory; rows / columns
-// beyond the matrix are clipped by the copy engine
-bool make_out_map(CUtensorMap *map, const void *ptr, int cols, int rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {16, 32};
-  cuuint32_t es[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
 }
 
 // 2-D int8 matrix [rows, inner] row-major, box = 128 bytes x box_rows, 128-byte swizzle, OOB reads as zero
@@ -813,18 +798,13 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
     max_units[dev & 63] = n;
   });
   if (attr_err != cudaSuccess) return attr_err;
-  CUtensorMap ta, tb, ty;
+  CUtensorMap ta, tb;
   const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN / CG;
   if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, box_b)) return cudaErrorInvalidValue;
-  if (EPI == EPI_GROUP_Q) {
-    memset(&ty, 0, sizeof(ty));  // int8 output: written with plain stores, the map is unused
-  } else if (!make_out_map(&ty, a.Y, a.Nout, a.M)) {
-    return cudaErrorInvalidValue;
-  }
   const int tiles = a.tiles_m * a.tiles_n;
   const int units = tiles < max_units[dev & 63] ? tiles : max_units[dev & 63];
   cfg.gridDim = dim3(CG * units);
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, a);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
 }
 
 GemmArgs base_args(const float *sa, const float *sb, const void *bias, int M, int N, int K, int nout, int tile_n,
@@ -873,14 +853,10 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
   }
   int bn = g_tile_override;
   if (!bn) {
-    // enough 128 x 256 tiles to fill the GPU: 256 x 256 CTA-pair tiles from K = 2048 up (measured 3-5% faster there),
-    // one CTA per 128 x 256 tile below (the pair waits for the slower of its two epilogues, which short K exposes);
-    // otherwise one CTA per 128 x 128 tile for more parallelism
+    // enough 128 x 256 tiles to fill the GPU: 256 x 256 CTA-pair tiles (measured 3-10% faster than one CTA per
+    // 128 x 256 tile at K = 1152 .. 8192); otherwise one CTA per 128 x 128 tile for more parallelism
     const long tiles256 = (long)((M + TM - 1) / TM) * ((N + 255) / 256);
-    if (tiles256 >= device_sm_count())
-      bn = K >= 2048 ? -256 : 256;
-    else
-      bn = 128;
+    bn = tiles256 >= device_sm_count() ? -256 : 128;
   }
   GemmArgs a = base_args(sa, sb, bias, M, N, K, N, bn < 0 ? -bn : bn, bn < 0 ? 2 * TM : TM);
   a.Y = (bf16 *)Y;

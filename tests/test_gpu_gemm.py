@@ -167,17 +167,17 @@ def silu_tile(request):
     _capi.lib().lfm2q_set_gemm_tile(0)
 
 
-@pytest.mark.parametrize("M,K,I", [(4096, 2048, 8192), (1024, 2048, 8192), (17, 2048, 8192), (300, 1152, 264),
-                                   (1, 64, 8), (385, 2048, 200)])
-def test_gemm_i8_silu(cuda_dev, silu_tile, M, K, I):
+@pytest.mark.parametrize("M,K,I,bias", [(4096, 2048, 8192, False), (1024, 2048, 8192, True), (17, 2048, 8192, False),
+                                        (300, 1152, 264, True), (1, 64, 8, False), (385, 2048, 200, True)])
+def test_gemm_i8_silu(cuda_dev, silu_tile, M, K, I, bias):
     if silu_tile and M * I > 20_000_000:
         pytest.skip("forced tiles: the automatic run covers the big shapes")
-    x, w, _ = make(M, K, 2 * I, False, M * 3 + I)
+    x, w, b = make(M, K, 2 * I, bias, M * 3 + I)
     xq, sx = quantize_rows(x.to(cuda_dev))
     wq, sw = quantize_int8(w)
     y = torch.empty(M, I, device=cuda_dev, dtype=BF)
-    int8_ext().gemm_i8_silu(xq, sx, wq.to(cuda_dev), sw.to(cuda_dev), None, y)
-    r = oracle.gemm_i8_silu_ref(xq.cpu(), sx.cpu(), wq, sw)
+    int8_ext().gemm_i8_silu(xq, sx, wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y)
+    r = oracle.gemm_i8_silu_ref(xq.cpu(), sx.cpu(), wq, sw, b)
     assert oracle.bf16_ulps(y.cpu(), r) <= 1
     frac = (y.cpu() != r).float().mean().item()
     assert frac < 1e-3, frac
