@@ -577,7 +577,10 @@ def run_gemv_case(a):
     E = ext()
     per = 20
 
-    a8 = os.environ.get("GEMV_MODE", "w16") == "a8"
+    mode = os.environ.get("GEMV_MODE", "w16")  # w16 (default path), w16bf (bf16-MMA path forced), a8
+    a8 = mode == "a8"
+    from lfm2opt import _capi
+    _capi.lib().lfm2q_set_gemv_path(1 if mode == "w16bf" else 0)
     xq = torch.randint(-127, 128, (B, K), generator=g, device=dev, dtype=torch.int8)
     sx = torch.rand(B, generator=g, device=dev) * 1e-2
 
@@ -600,7 +603,7 @@ def run_gemv_case(a):
     nbytes = N * K + 4 * N + 2 * B * K + 2 * B * N
     peak = load_peaks().get("hbm_gbs")
     gbs = nbytes / (ms * 1e-3) / 1e9
-    print(json.dumps({"gemv_case": a.gemv_case, "mode": "a8" if a8 else "w16", "pdl": os.environ.get("LFM2_PDL", "1"),
+    print(json.dumps({"gemv_case": a.gemv_case, "mode": mode, "pdl": os.environ.get("LFM2_PDL", "1"),
                       "us": round(ms * 1e3, 2),
                       "gbs": round(gbs, 1), "frac_hbm": round(gbs / peak, 4) if peak else None, "copies": copies}),
           flush=True)

@@ -131,6 +131,13 @@ int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, co
 void lfm2q_set_pdl(int on);
 void lfm2q_set_gemv_impl(int impl);
 
+/* Path of the int8 weight-only GEMV (lfm2q_gemv and lfm2q_gemv_epi with w_is_int8): 0 (default) = int8 tensor path
+ * with the tokens sliced into exact fixed-point bytes where it applies (N * K >= 8 M for lfm2q_gemv, B <= 4,
+ * B * slices * (K + 64) <= 64 KB), else the bf16 path; 1 = always the bf16 path (weights converted exactly to bf16,
+ * bf16 MMAs). No counterpart in the reference
+ * (its set_gemv_impl chooses how x is loaded, kernels/lfm2_decode.cu:662-675). Tuning and testing only. */
+void lfm2q_set_gemv_path(int path);
+
 /* GEMV kernels launched with Programmatic Dependent Launch let the next kernel launch after their K loop
  * (early == 0, default) or at their start (early != 0). Tuning only; results are unchanged. */
 void lfm2q_set_gemv_trigger(int early);

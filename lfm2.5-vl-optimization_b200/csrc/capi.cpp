@@ -102,6 +102,7 @@ int lfm2q_check_device(int clear) {
 void lfm2q_set_pdl(int on) { g_pdl.store(on != 0); }
 void lfm2q_set_gemv_trigger(int early) { gemv_set_early_trigger(early != 0); }
 void lfm2q_set_gemv_impl(int) {}
+void lfm2q_set_gemv_path(int path) { gemv_set_impl(path == 1 ? 1 : 0); }
 void lfm2q_set_gemm_tile(int bn) { gemm_set_tile_override(bn); }
 
 // ------------------------------------------------------------------ quantizers

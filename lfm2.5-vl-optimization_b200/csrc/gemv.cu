@@ -14,8 +14,10 @@
 // identically for W and x (lane t, step s take physical k 16t+4s..16t+4s+3), which leaves the dot product
 // unchanged. Small N is split over K-slices (KS warps per row group) whose fp32 partials meet in shared memory
 // and are summed in a fixed order, so results are deterministic.
+#include <map>
 #include <mutex>
 #include <set>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
@@ -191,8 +193,8 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], const uint32_t (&a)[4]
 // [kb, ke). Same cp.async ring and software pipeline as warp_gemv; no conversion at all: the 16 bytes a lane holds
 // of rows g and g + 8 feed two m16n8k32 s8 MMAs directly. Lane (g, t), MMA s of a 64-byte step: logical k slots
 // 4t..4t+3 / 16+4t..16+4t+3 take physical bytes 16t+8s..+3 / 16t+8s+4..+7, for W and x alike.
-// phase 0: prefetch + compute; 1: only issue the first GV_RING steps (weights, immutable); 2: compute after phase 1.
-template <int NT>
+// phase 0: prefetch + compute; 1: only issue the first RING steps (weights, immutable); 2: compute after phase 1.
+template <int NT, int RING = GV_RING>
 __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const int8_t *xq, int xstride, int N, int K,
                                              int B, int r0, int kb, int ke, int (&acc)[NT][4], uint8_t *ring, bool pdl,
                                              int phase = 0) {
@@ -203,14 +205,14 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
   const int nsteps = (ke - kb) / 64;
   auto issue = [&](int st) {
     if (st < nsteps) {
-      const uint32_t d = slot0 + (st % GV_RING) * 1024;
+      const uint32_t d = slot0 + (st % RING) * 1024;
       asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + st * 64) : "memory");
       asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(row1 + st * 64) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   auto lds = [&](int st, uint4 &w0, uint4 &w1) {
-    const uint32_t d = slot0 + (st % GV_RING) * 1024;
+    const uint32_t d = slot0 + (st % RING) * 1024;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
                  : "memory");
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
@@ -227,7 +229,7 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
   };
   if (phase != 2) {
 #pragma unroll
-    for (int st = 0; st < GV_RING; ++st) issue(st);
+    for (int st = 0; st < RING; ++st) issue(st);
   }
   if (phase == 1) return;
 #pragma unroll
@@ -236,14 +238,14 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
     for (int e = 0; e < 4; ++e) acc[j][e] = 0;
   if (pdl) pdl_wait();
   uint4 wc0, wc1, wn0, wn1, xc[NT], xn[NT];
-  asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 1) : "memory");
+  asm volatile("cp.async.wait_group %0;" ::"n"(RING - 1) : "memory");
   if (nsteps > 0) {
     lds(0, wc0, wc1);
     ldx(0, xc);
   }
   for (int st = 0; st < nsteps; ++st) {
     if (st + 1 < nsteps) {
-      asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 2) : "memory");
+      asm volatile("cp.async.wait_group %0;" ::"n"(RING - 2) : "memory");
       lds(st + 1, wn0, wn1);
       ldx(st + 1, xn);
     }
@@ -253,7 +255,7 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
 #pragma unroll
       for (int j = 0; j < NT; ++j) mma_s8_16832(acc[j], a, (&xc[j].x)[2 * s], (&xc[j].x)[2 * s + 1]);
     }
-    issue(st + GV_RING);
+    issue(st + RING);
     wc0 = wn0;
     wc1 = wn1;
 #pragma unroll
@@ -411,6 +413,197 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
   }
 }
 
+// Writes tokens 0..B-1 of x (bf16 [B, K]) as NSL-byte fixed point into shared memory, row b * NSL + s holding byte s
+// of every element (q = sum_s q_s 256^s, balanced bytes), and the token's exponent E (x = q * 2^E) into e_s[b].
+// All threads of the block take part (16-byte chunks c = tid, tid + 256, ..., held in registers across the absmax
+// reduction, XS_CH chunks per thread and token at most: K <= 8 * 256 * XS_CH / B); the block is synchronised inside
+// and the caller synchronises again before reading the slices.
+constexpr int XS_CH = 8;
+template <int NSL>
+__device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride, int *e_s,
+                                             float (&red_max)[4][8]) {
+  constexpr int QBITS = 8 * NSL - 2;  // |q| < 2^QBITS
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K8 = K / 8, total = B * K8;
+  // this thread's chunks over all tokens: index i = tid + j * 256 -> token i / K8, chunk i % K8
+  uint4 v[XS_CH];
+#pragma unroll
+  for (int j = 0; j < XS_CH; ++j) {
+    const int i = threadIdx.x + j * GV_THREADS;
+    v[j] = i < total ? __ldg(reinterpret_cast<const uint4 *>(x) + i) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  {
+    float m[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < XS_CH; ++j) {
+      if (threadIdx.x + j * GV_THREADS < total) {
+        const int b = (threadIdx.x + j * GV_THREADS) / K8;
+        const uint32_t m2 = __vmaxu2(__vmaxu2(v[j].x & 0x7FFF7FFFu, v[j].y & 0x7FFF7FFFu),
+                                     __vmaxu2(v[j].z & 0x7FFF7FFFu, v[j].w & 0x7FFF7FFFu));
+        const float mm = fmaxf(bf_lo(m2), bf_hi(m2));
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb)
+          if (bb == b) m[bb] = fmaxf(m[bb], mm);
+      }
+    }
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) {
+      const float w = warp_max(m[bb]);
+      if (lane == 0 && bb < B) red_max[bb][warp] = w;
+    }
+  }
+  __syncthreads();
+  int E[4], f1b[4], f2b[4];
+#pragma unroll
+  for (int bb = 0; bb < 4; ++bb) {
+    float amax = 0.f;
+    if (bb < B) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) amax = fmaxf(amax, red_max[bb][w]);
+    }
+    // amax < 2^(ex + 1) with ex its binary exponent (bf16 subnormals: below the smallest normal, ex = -126 bounds
+    // them); E = ex + 1 - QBITS. The scale 2^-E is applied as two exact power-of-two factors (it can exceed 2^127).
+    const int ex = amax > 0.f ? max(((__float_as_int(amax) >> 23) & 255) - 127, -126) : 0;
+    E[bb] = ex + 1 - QBITS;
+    const int ne1 = min(max(-E[bb], -126), 127), ne2 = -E[bb] - ne1;
+    f1b[bb] = (ne1 + 127) << 23;
+    f2b[bb] = (ne2 + 127) << 23;
+  }
+  if (threadIdx.x < B)
+    e_s[threadIdx.x] = threadIdx.x == 0 ? E[0] : (threadIdx.x == 1 ? E[1] : (threadIdx.x == 2 ? E[2] : E[3]));
+#pragma unroll
+  for (int j = 0; j < XS_CH; ++j) {
+    const int i = threadIdx.x + j * GV_THREADS;
+    if (i >= total) break;
+    const int b = i / K8, c = i - b * K8;
+    int fb1 = f1b[0], fb2 = f2b[0];
+#pragma unroll
+    for (int bb = 1; bb < 4; ++bb)
+      if (bb == b) {
+        fb1 = f1b[bb];
+        fb2 = f2b[bb];
+      }
+    const float f1 = __int_as_float(fb1), f2 = __int_as_float(fb2);
+    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    uint32_t o[NSL][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t acc[NSL];
+#pragma unroll
+      for (int sl = 0; sl < NSL; ++sl) acc[sl] = 0u;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float xv = (e & 1) ? bf_hi(w[2 * h + (e >> 1)]) : bf_lo(w[2 * h + (e >> 1)]);
+        int q = __float2int_rn(__fmul_rn(__fmul_rn(xv, f1), f2));  // exact scaling, one rounding
+#pragma unroll
+        for (int sl = 0; sl < NSL; ++sl) {
+          const int qs = ((q + 128) & 255) - 128;  // balanced byte: q = qs + 256 * q'
+          acc[sl] |= (uint32_t)(qs & 255) << (8 * e);
+          q = (q - qs) >> 8;
+        }
+      }
+#pragma unroll
+      for (int sl = 0; sl < NSL; ++sl) o[sl][h] = acc[sl];
+    }
+#pragma unroll
+    for (int sl = 0; sl < NSL; ++sl)
+      *reinterpret_cast<uint2 *>(xs + (size_t)(b * NSL + sl) * xstride + c * 8) = make_uint2(o[sl][0], o[sl][1]);
+  }
+}
+
+// Largest K the sliced path handles for B tokens (chunks held in registers by the 256 threads of a block)
+__host__ __device__ constexpr int xs_max_k(int B) { return 8 * GV_THREADS * XS_CH / (B > 0 ? B : 1); }
+
+// Weight-only GEMV on the int8 tensor path ("x-sliced"), for 1..8/NSL tokens. Each token's bf16 activations are
+// written exactly as NSL-byte fixed point, q = x * 2^-E with E from the token's absmax so that |q| < 2^(8 NSL - 2),
+// and q is split into NSL balanced signed bytes, q = sum_s q_s 256^s. The bytes of token b are the NSL MMA columns
+// b * NSL + s, so the int8 weights feed m16n8k32 s8 MMAs unconverted (the A8 inner loop) and every partial sum
+// A_s = sum_k W[n, k] q_s[k] is an exact int32. y[b, n] = bf16( ((sum_s 256^s A_s) * scale[n]) * 2^E ), combined in
+// fp32: the sum is exact up to the fp32 rounding of the combination and of elements below |x| < 2^(E-1) (at most
+// 2^-(8 NSL - 2) of the token's absmax each), so the result is the exact dot product rounded, at least as accurate
+// as the reference's fp32 accumulation (kernels/lfm2_decode.cu:576-661). Every block slices x into shared memory
+// after its first weights are in flight (rows of K + 64 bytes, bank-conflict-free fragment loads).
+template <int KS, int NSL, int RING>
+__global__ void __launch_bounds__(GV_THREADS) gemv_xs_kernel(const int8_t *__restrict__ W, const float *__restrict__ scale,
+                                                             const bf16 *__restrict__ x, bf16 *__restrict__ y, int N,
+                                                             int K, int B, int pdl) {
+  constexpr int RG = 8 / KS;
+  extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x RING x 1 KB, then the sliced tokens
+  __shared__ int red[RG * KS * 16 * 8];
+  __shared__ int e_s[4];
+  __shared__ float red_max[4][8];
+  if (pdl == 2) pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rg = warp / KS, ks = warp % KS;
+  const int kslice = K / KS;
+  const int sets = ((N + 15) / 16 + RG - 1) / RG;
+  const int xstride = K + 64;
+  int8_t *xs = reinterpret_cast<int8_t *>(rings + 8 * RING * 1024);
+  {
+    // stream the first set's weights before anything waits on the previous kernel
+    int dummy[1][4];
+    warp_gemv_a8<1, RING>(W, xs, xstride, N, K, B * NSL, (blockIdx.x * RG + rg) * 16, ks * kslice, (ks + 1) * kslice, dummy,
+                    rings + warp * RING * 1024, false, 1);
+  }
+  if (pdl) pdl_wait();
+  slice_tokens<NSL>(x, K, B, xs, xstride, e_s, red_max);
+  __syncthreads();
+  for (int set = blockIdx.x; set < sets; set += gridDim.x) {
+    const int r0 = (set * RG + rg) * 16;
+    int acc[1][4];
+    warp_gemv_a8<1, RING>(W, xs, xstride, N, K, B * NSL, r0, ks * kslice, (ks + 1) * kslice, acc,
+                    rings + warp * RING * 1024, false, set == blockIdx.x ? 2 : 0);
+    if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 + frag_tok(lane, 0, e)] = acc[0][e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < RG * 16 * B; i += GV_THREADS) {
+      const int b = i % B, rr = (i / B) % 16, g2 = i / (16 * B);
+      const int n = (set * RG + g2) * 16 + rr;
+      if (n >= N) continue;
+      float f = 0.f;
+#pragma unroll
+      for (int sl = NSL - 1; sl >= 0; --sl) {
+        int a = 0;
+#pragma unroll
+        for (int s2 = 0; s2 < KS; ++s2) a += red[((g2 * KS + s2) * 16 + rr) * 8 + b * NSL + sl];
+        f = __fmaf_rn(f, 256.f, (float)a);
+      }
+      y[(size_t)b * N + n] = f2bf(ldexpf(__fmul_rn(f, scale[n]), e_s[b]));
+    }
+    __syncthreads();
+  }
+}
+
+// Elementwise epilogue of the fused decode GEMVs on the NR bf16 GEMV values of output index n0 + threadIdx.x
+// (threads 0..15; kernels/lfm2_decode.cu:770-805).
+template <int NR, int EPI>
+__device__ __forceinline__ void epi_tail(const float (&part)[NR][16], bf16 *__restrict__ y, int S, int n0,
+                                         bf16 *__restrict__ state, const bf16 *__restrict__ cw,
+                                         const bf16 *__restrict__ cbias) {
+  if (threadIdx.x >= 16) return;
+  const int m = n0 + threadIdx.x;
+  if (m >= S) return;
+  if (EPI == 0) {
+    const float g = part[0][threadIdx.x], u = part[1][threadIdx.x];
+    y[m] = f2bf(rbf(g / (1.f + __expf(-g))) * u);
+  } else {
+    const float bx = rbf(part[0][threadIdx.x] * part[NR - 1][threadIdx.x]);
+    bf16 *st = state + (size_t)m * 3;
+    const float s1 = bf2f(st[1]), s2 = bf2f(st[2]);
+    st[0] = st[1];
+    st[1] = st[2];
+    st[2] = f2bf(bx);
+    // conv = w0 * s1 + w1 * s2 + w2 * bx (+ bias), evaluated left to right with explicit fp32 roundings
+    float acc2 = __fmul_rn(bf2f(cw[m * 3 + 0]), s1);
+    acc2 = __fadd_rn(acc2, __fmul_rn(bf2f(cw[m * 3 + 1]), s2));
+    acc2 = __fadd_rn(acc2, __fmul_rn(bf2f(cw[m * 3 + 2]), bx));
+    if (cbias) acc2 = __fadd_rn(acc2, bf2f(cbias[m]));
+    y[m] = f2bf(part[1][threadIdx.x] * rbf(acc2));
+  }
+}
+
 // Batch-1 GEMV over NR stacked [S, K] blocks of W followed by an elementwise epilogue on the NR values of one
 // output index (kernels/lfm2_decode.cu:718-805):
 //   EPI 0, NR 2 (w1 | w3):         y[n] = bf16( bf16(silu(g)) * u ),  g, u = the bf16 the plain GEMV would store
@@ -454,57 +647,126 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_kernel(const WT *__restri
     part[pp][r] = (n < S) ? rbf(scale ? v * scale[pp * S + n] : v) : 0.f;
   }
   __syncthreads();
-  if (threadIdx.x >= 16) return;
-  const int m = n0 + threadIdx.x;
-  if (m >= S) return;
-  if (EPI == 0) {
-    const float g = part[0][threadIdx.x], u = part[1][threadIdx.x];
-    y[m] = f2bf(rbf(g / (1.f + __expf(-g))) * u);
-  } else {
-    const float bx = rbf(part[0][threadIdx.x] * part[2][threadIdx.x]);
-    bf16 *st = state + (size_t)m * 3;
-    const float s1 = bf2f(st[1]), s2 = bf2f(st[2]);
-    st[0] = st[1];
-    st[1] = st[2];
-    st[2] = f2bf(bx);
-    // conv = w0 * s1 + w1 * s2 + w2 * bx (+ bias), evaluated left to right with explicit fp32 roundings
-    float acc2 = __fmul_rn(bf2f(cw[m * 3 + 0]), s1);
-    acc2 = __fadd_rn(acc2, __fmul_rn(bf2f(cw[m * 3 + 1]), s2));
-    acc2 = __fadd_rn(acc2, __fmul_rn(bf2f(cw[m * 3 + 2]), bx));
-    if (cbias) acc2 = __fadd_rn(acc2, bf2f(cbias[m]));
-    y[m] = f2bf(part[1][threadIdx.x] * rbf(acc2));
+  epi_tail<NR, EPI>(part, y, S, n0, state, cw, cbias);
+}
+
+// gemv_epi on the x-sliced int8 path (see gemv_xs_kernel): the token is sliced into 3 exact fixed-point bytes in
+// shared memory, each warp's int32 slice sums are exact, so the NR bf16 values equal the plain GEMV's outputs
+// whatever the K-slicing. Same block layout and epilogue as gemv_epi_kernel.
+template <int NR, int EPI, int RING>
+__global__ void __launch_bounds__(GV_THREADS) gemv_epi_xs_kernel(const int8_t *__restrict__ W,
+                                                                 const float *__restrict__ scale,
+                                                                 const bf16 *__restrict__ x, bf16 *__restrict__ y,
+                                                                 int S, int K, bf16 *__restrict__ state,
+                                                                 const bf16 *__restrict__ cw,
+                                                                 const bf16 *__restrict__ cbias, int pdl) {
+  constexpr int KSE = (NR == 2) ? 4 : 2;
+  constexpr int NSL = 3;
+  extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x RING x 1 KB, then the sliced token
+  __shared__ int red[NR][KSE][16][NSL];
+  __shared__ float part[NR][16];
+  __shared__ int e_s[4];
+  __shared__ float red_max[4][8];
+  if (pdl) pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = warp / KSE, ks = warp % KSE;
+  const int n0 = blockIdx.x * 16;
+  const int kslice = K / KSE;
+  const int xstride = K + 64;
+  int8_t *xs = reinterpret_cast<int8_t *>(rings + 8 * RING * 1024);
+  const int8_t *Wp = W + (size_t)(p < NR ? p : 0) * S * K;
+  uint8_t *ring = rings + warp * RING * 1024;
+  if (p < NR) {
+    int dummy[1][4];
+    warp_gemv_a8<1, RING>(Wp, xs, xstride, S, K, NSL, n0, ks * kslice, (ks + 1) * kslice, dummy, ring, false, 1);
   }
+  if (pdl) pdl_wait();
+  slice_tokens<NSL>(x, K, 1, xs, xstride, e_s, red_max);
+  __syncthreads();
+  if (p < NR) {
+    int acc[1][4];
+    warp_gemv_a8<1, RING>(Wp, xs, xstride, S, K, NSL, n0, ks * kslice, (ks + 1) * kslice, acc, ring, false, 2);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int col = frag_tok(lane, 0, e);
+      if (col < NSL) red[p][ks][frag_row(lane, e)][col] = acc[0][e];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < NR * 16) {
+    const int pp = threadIdx.x / 16, r = threadIdx.x % 16, n = n0 + r;
+    float f = 0.f;
+#pragma unroll
+    for (int sl = NSL - 1; sl >= 0; --sl) {
+      int a = 0;
+#pragma unroll
+      for (int s2 = 0; s2 < KSE; ++s2) a += red[pp][s2][r][sl];
+      f = __fmaf_rn(f, 256.f, (float)a);
+    }
+    part[pp][r] = (n < S) ? rbf(ldexpf(__fmul_rn(f, scale[pp * S + n]), e_s[0])) : 0.f;
+  }
+  __syncthreads();
+  epi_tail<NR, EPI>(part, y, S, n0, state, cw, cbias);
 }
 
 constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
+constexpr int XS_RING = 6;  // ring depth of the x-sliced kernels (K steps of 1 KB per warp)
 constexpr int GV_X_SMEM_MAX = 64 * 1024;  // fused-quantization A8 GEMV: B * (K + 64) bytes of int8 tokens
 bool g_early_trigger = false;
+int g_gemv_impl = 0;  // 0: x-sliced int8 path where it applies, 1: always the bf16-MMA path
 
-// Launch with the per-warp rings as dynamic shared memory (opt-in above 48 KB, set once per kernel and device) and,
-// when asked, Programmatic Dependent Launch.
 // (kernel, device) pairs whose dynamic shared memory limit has been raised
 std::mutex g_attr_mu;
 std::set<std::pair<const void *, int>> g_attr_done;
 
-template <typename KernelT, typename... Args>
-cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, size_t extra_smem,
-                      Args... args) {
+// Raise the kernel's dynamic shared memory limit (rings + token buffer) once per device.
+template <typename KernelT>
+cudaError_t ensure_smem_attr(KernelT kernel) {
   int dev = 0;
   cudaGetDevice(&dev);
-  {
-    std::lock_guard<std::mutex> lk(g_attr_mu);
-    const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), dev);
-    if (!g_attr_done.count(key)) {
-      const cudaError_t e =
-          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_SMEM + GV_X_SMEM_MAX);
-      if (e != cudaSuccess) return e;
-      g_attr_done.insert(key);
-    }
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), dev);
+  if (!g_attr_done.count(key)) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_SMEM + GV_X_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    g_attr_done.insert(key);
   }
+  return cudaSuccess;
+}
+
+// Blocks of `kernel` with `dyn_smem` bytes of dynamic shared memory that fit on the device at once (cached).
+std::mutex g_occ_mu;
+std::map<std::tuple<const void *, size_t, int>, int> g_occ;
+template <typename KernelT>
+int resident_blocks(KernelT kernel, size_t dyn_smem) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(reinterpret_cast<const void *>(kernel), dyn_smem, dev);
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    const auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+  }
+  int per_sm = 0;
+  if (ensure_smem_attr(kernel) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, GV_THREADS, dyn_smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int n = per_sm * device_sm_count();
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  g_occ[key] = n;
+  return n;
+}
+
+// Launch with `dyn_smem` bytes of dynamic shared memory (per-warp rings, then any token buffer) and, when asked,
+// Programmatic Dependent Launch.
+template <typename KernelT, typename... Args>
+cudaError_t launch_dyn(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, size_t dyn_smem, Args... args) {
+  if (const cudaError_t e = ensure_smem_attr(kernel)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = GV_DYN_SMEM + extra_smem;
+  cfg.dynamicSmemBytes = dyn_smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -512,6 +774,13 @@ cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStrea
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Launch with the default rings (GV_RING steps per warp) plus `extra_smem` bytes.
+template <typename KernelT, typename... Args>
+cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStream_t st, size_t extra_smem,
+                      Args... args) {
+  return launch_dyn(kernel, grid, block, pdl, st, GV_DYN_SMEM + extra_smem, args...);
 }
 
 template <typename WT, int NT>
@@ -560,6 +829,16 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
                               bf16 *state, const bf16 *cw, const bf16 *cbias, bool pdl, cudaStream_t st) {
   const dim3 grid((S + 15) / 16);
   const int p = pdl ? 1 : 0;
+  if (sizeof(WT) == 1 && g_gemv_impl == 0 && 3 * (size_t)(K + 64) <= (size_t)GV_X_SMEM_MAX && K % 256 == 0 &&
+      K <= xs_max_k(1)) {
+    const int8_t *Wi = reinterpret_cast<const int8_t *>(W);
+    const size_t dyn = (size_t)8 * XS_RING * 1024 + 3 * (size_t)(K + 64);
+    if (epi == 0)
+      return launch_dyn(gemv_epi_xs_kernel<2, 0, XS_RING>, grid, GV_THREADS, pdl, st, dyn, Wi, scale, x, y, S, K, state,
+                        cw, cbias, p);
+    return launch_dyn(gemv_epi_xs_kernel<3, 1, XS_RING>, grid, GV_THREADS, pdl, st, dyn, Wi, scale, x, y, S, K, state,
+                      cw, cbias, p);
+  }
   if (epi == 0)
     return launch_ex(gemv_epi_kernel<WT, 2, 0>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, S, K, state, cw, cbias, p);
   return launch_ex(gemv_epi_kernel<WT, 3, 1>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, S, K, state, cw, cbias, p);
@@ -584,12 +863,54 @@ cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const
   }
 }
 
+template <int KS, int NSL>
+cudaError_t gemv_xs_launch(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
+                           cudaStream_t st) {
+  auto kern = gemv_xs_kernel<KS, NSL, XS_RING>;
+  const int groups = (N + 15) / 16, rg = 8 / KS;
+  const int sets = (groups + rg - 1) / rg;
+  const size_t dyn = (size_t)8 * XS_RING * 1024 + (size_t)B * NSL * (K + 64);
+  const int resident = resident_blocks(kern, dyn);  // one wave: the grid strides over the sets
+  const dim3 grid(sets < resident ? sets : resident);
+  const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
+  return launch_dyn(kern, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p);
+}
+
+template <int NSL>
+cudaError_t gemv_xs_ks(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
+                       cudaStream_t st) {
+  switch (ks) {
+    case 1: return gemv_xs_launch<1, NSL>(W, scale, x, y, N, K, B, pdl, st);
+    case 2: return gemv_xs_launch<2, NSL>(W, scale, x, y, N, K, B, pdl, st);
+    case 4: return gemv_xs_launch<4, NSL>(W, scale, x, y, N, K, B, pdl, st);
+    default: return gemv_xs_launch<8, NSL>(W, scale, x, y, N, K, B, pdl, st);
+  }
+}
+
+// Slices per token for the x-sliced path (0: the batch does not fit one MMA column tile, or its slices do not fit
+// the shared-memory budget): 3 bytes up to 2 tokens, 2 bytes up to 4.
+int gemv_xs_slices(int K, int B) {
+  const int nsl = B <= 2 ? 3 : (B <= 4 ? 2 : 0);
+  if (nsl == 0 || (size_t)B * nsl * (K + 64) > (size_t)GV_X_SMEM_MAX || K % 64 != 0 || K > xs_max_k(B)) return 0;
+  return nsl;
+}
+
 int gemv_device_error(bool) { return 0; }
 void gemv_set_early_trigger(bool early) { g_early_trigger = early; }
+void gemv_set_impl(int impl) { g_gemv_impl = impl; }
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st) {
   if (N <= 0 || B <= 0) return cudaSuccess;
+  // the sliced path's token prologue (absmax, slicing, two block barriers) costs ~0.4 us, which the faster weight
+  // stream repays from ~8 M weights up; below that the bf16 path is quicker (measured on B200)
+  if (int8 && g_gemv_impl == 0 && (long)N * K >= 8L * 1024 * 1024) {
+    if (const int nsl = gemv_xs_slices(K, B)) {
+      const int ks = pick_ks(N, K, 64, rows);
+      return nsl == 3 ? gemv_xs_ks<3>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st)
+                      : gemv_xs_ks<2>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st);
+    }
+  }
   if (int8)
     return gemv_dispatch<int8_t>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
   return gemv_dispatch<bf16>((const bf16 *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);

@@ -25,6 +25,7 @@ cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void
                         int B, bool pdl, cudaStream_t st);
 int gemv_device_error(bool clear);
 void gemv_set_early_trigger(bool early);
+void gemv_set_impl(int impl);
 // per-token W8A8 linear for few tokens in one launch: quant_rows(x) fused into the A8 GEMV
 cudaError_t launch_linear_a8(const void *x, const int8_t *W, const float *sw, const void *bias, void *y, int N, int K,
                              int B, bool gelu, bool pdl, cudaStream_t st);  // tuning: let dependents launch at kernel start (default: after the K loop)

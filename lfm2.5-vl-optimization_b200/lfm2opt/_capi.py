@@ -38,8 +38,10 @@ SIGNATURES = {
     "lfm2q_set_gemv_impl": [_i],
     "lfm2q_set_gemm_tile": [_i],
     "lfm2q_set_gemv_trigger": [_i],
+    "lfm2q_set_gemv_path": [_i],
 }
-_VOID = {"lfm2q_set_pdl", "lfm2q_set_gemv_impl", "lfm2q_set_gemm_tile", "lfm2q_set_gemv_trigger"}
+_VOID = {"lfm2q_set_pdl", "lfm2q_set_gemv_impl", "lfm2q_set_gemm_tile", "lfm2q_set_gemv_trigger",
+         "lfm2q_set_gemv_path"}
 _STR = {"lfm2q_last_error", "lfm2q_version"}
 
 _LIB = None

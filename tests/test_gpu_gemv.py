@@ -31,11 +31,22 @@ SHAPES = [(3072, 2048), (6144, 2048), (2048, 2048), (16384, 2048), (2048, 8192),
           (1000, 1536)]
 
 
+@pytest.fixture(params=[0, 1], ids=["auto", "bf16path"])
+def gemv_path(request):
+    """0: the int8 path with the tokens sliced into exact fixed-point bytes (B <= 4), else bf16; 1: always bf16."""
+    from lfm2opt import _capi
+    _capi.lib().lfm2q_set_gemv_path(request.param)
+    yield request.param
+    _capi.lib().lfm2q_set_gemv_path(0)
+
+
 @pytest.mark.parametrize("N,K", SHAPES)
 @pytest.mark.parametrize("B", [1, 2, 3, 4, 7, 8, 13, 16, 19])
-def test_gemv_int8(cuda_dev, N, K, B):
+def test_gemv_int8(cuda_dev, gemv_path, N, K, B):
     if N * K > 40_000_000 and B not in (1, 8, 16):
         pytest.skip("large shape: a few batch sizes suffice")
+    if gemv_path == 1 and B > 4:
+        pytest.skip("the path knob only matters for B <= 4")
     g = torch.Generator().manual_seed(N + K + B)
     W = (torch.randn(N, K, generator=g) * 0.02).to(BF)
     Wq, s = quantize_int8(W)
@@ -45,16 +56,61 @@ def test_gemv_int8(cuda_dev, N, K, B):
     check(y.cpu(), Wq, s, x)
 
 
+def _token_scales():
+    """Tokens spanning the fp range: plain, outlier channels x1000, tiny (1e-30), huge (1e30), all zero, one nonzero
+    element, bf16 subnormals."""
+    g = torch.Generator().manual_seed(11)
+    K = 2048
+    x = torch.randn(7, K, generator=g)
+    x[1, ::97] *= 1000.0
+    x[2] *= 1e-30
+    x[3] *= 1e30
+    x[4] = 0.0
+    x[5] = 0.0
+    x[5, 1234] = -3.5
+    x[6] = torch.randn(K, generator=g) * 2.0 ** -130
+    return x.to(BF)
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 4])
+def test_gemv_int8_sliced_extremes(cuda_dev, B):
+    """The x-sliced int8 path picks a power-of-two scale per token from its absmax: tokens of very different
+    magnitude, zero tokens and subnormal tokens are each within the rounding bound of their own exact result."""
+    xs = _token_scales()
+    g = torch.Generator().manual_seed(B)
+    N = 4096  # N * K = 8 M weights: the sliced path
+    Wq = torch.randint(-127, 128, (N, 2048), generator=g, dtype=torch.int8)
+    s = torch.rand(N, generator=g) * 1e-3 + 1e-4
+    for i0 in range(0, xs.shape[0], B):
+        x = xs[i0:i0 + B]
+        y = torch.empty(x.shape[0], N, device=cuda_dev, dtype=BF)
+        ext().gemv(Wq.to(cuda_dev), s.to(cuda_dev), x.to(cuda_dev), y)
+        r64 = oracle.gemv_f64(Wq, s, x)
+        for b in range(x.shape[0]):
+            if r64[b].abs().max() == 0:
+                assert (y[b].cpu() == 0).all()
+                continue
+            e = ((y[b].cpu().double() - r64[b]).norm() / r64[b].norm()).item()
+            e_round = ((r64[b].to(BF).double() - r64[b]).norm() / r64[b].norm()).item()
+            assert e <= 1.05 * e_round + 1e-6, (i0 + b, e, e_round)
+
+
+@pytest.mark.parametrize("N", [3072, 4096], ids=["bf16path", "sliced"])
 @pytest.mark.parametrize("rows", [1, 2, 4, 8])
-def test_gemv_kslices_agree(cuda_dev, rows):
-    """The K-split tuning knob changes only the fp32 summation order."""
+def test_gemv_kslices_agree(cuda_dev, rows, N):
+    """The K-split tuning knob changes only the fp32 summation order (bf16 path) or nothing at all (sliced path:
+    exact int32 partial sums)."""
     g = torch.Generator().manual_seed(rows)
-    Wq = torch.randint(-127, 128, (3072, 2048), generator=g, dtype=torch.int8)
-    s = torch.rand(3072, generator=g) * 1e-3
-    x = torch.randn(4, 2048, generator=g).to(BF)
-    y = torch.empty(4, 3072, device=cuda_dev, dtype=BF)
+    Wq = torch.randint(-127, 128, (N, 2048), generator=g, dtype=torch.int8)
+    s = torch.rand(N, generator=g) * 1e-3
+    x = torch.randn(2, 2048, generator=g).to(BF)
+    y = torch.empty(2, N, device=cuda_dev, dtype=BF)
     ext().gemv(Wq.to(cuda_dev), s.to(cuda_dev), x.to(cuda_dev), y, rows)
     check(y.cpu(), Wq, s, x)
+    if N == 4096:
+        y1 = torch.empty_like(y)
+        ext().gemv(Wq.to(cuda_dev), s.to(cuda_dev), x.to(cuda_dev), y1, 1)
+        assert torch.equal(y, y1)
 
 
 @pytest.mark.parametrize("B", [1, 5])
