@@ -543,7 +543,10 @@ def run_case(a):
     E = int8_ext()
     grouped = epi in ("group", "groupq")
     xq, sx = quantize_rows(x, 64 if grouped else 0)
-    if epi == "silu":
+    if epi in ("w8", "w8gelu"):  # W8A16: bf16 activations, int8 weights
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        fn = lambda: E.gemm_w8(x, wq, sw, b, y, epi == "w8gelu")  # noqa: E731
+    elif epi == "silu":
         y = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
         fn = lambda: E.gemm_i8_silu(xq, sx, wq, sw, None, y)  # noqa: E731
     elif epi == "groupq":
@@ -555,8 +558,11 @@ def run_case(a):
         fn = lambda: E.gemm_i8(xq, sx, wq, sw, b, y, epi == "gelu")  # noqa: E731
     ms = time_steps(fn, a.steps, max(3, a.warmup), 1) / a.steps
     tops = 2 * M * N * K / (ms * 1e-3) / 1e12
+    peak = load_peaks().get("bf16_tflops") if epi.startswith("w8") else INT8_PEAK_NOMINAL
     print(json.dumps({"case": a.case, "tile": a.tile, "us": round(ms * 1e3, 2), "tops": round(tops, 1),
-                      "frac_nominal": round(tops / INT8_PEAK_NOMINAL, 4)}), flush=True)
+                      "frac_peak": round(tops / peak, 4) if peak else None,
+                      "peak": "measured bf16 (MEASURED_PEAKS.json)" if epi.startswith("w8") else "nominal INT8 4500"}),
+          flush=True)
 
 
 def run_gemv_case(a):
@@ -619,7 +625,8 @@ def main():
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--case", default=None,
-                    help="M,K,N[,epi] — time one GEMM shape (epi: none|gelu|silu|group|groupq); tuning and ncu target")
+                    help="M,K,N[,epi] — time one GEMM shape (epi: none|gelu|silu|group|groupq|w8|w8gelu); tuning "
+                         "and ncu target")
     ap.add_argument("--tile", type=int, default=0, help="force the per-token GEMM tile width (128 or 256)")
     ap.add_argument("--gemv-case", default=None, help="N,K,B[,rows] — time one decode GEMV shape (tuning, ncu target)")
     a = ap.parse_args()

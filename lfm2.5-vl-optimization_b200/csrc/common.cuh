@@ -84,6 +84,20 @@ __device__ __forceinline__ float2 q8r2(float2 v, float sc, float rinv) {
   }
   return tb;
 }
+// 4 int8 codes (bytes of w) -> two bf16x2 words (lo: bytes 0,1; hi: bytes 2,3), exact: each byte + 128 goes into
+// the mantissa of 2^23 (one byte permute), a packed fp32 subtraction of 2^23 + 128 leaves the code as an exact fp32,
+// whose upper half is its bf16 encoding (|q| <= 127 has at most 7 significant bits).
+__device__ __forceinline__ void i8x4_to_bf16x2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  const uint32_t u = w ^ 0x80808080u;  // q + 128 in 0..255
+  const float2 bias = make_float2(8388736.f, 8388736.f);  // 2^23 + 128
+  const float2 f01 = fsub2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651))), bias);
+  const float2 f23 = fsub2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653))), bias);
+  lo = __byte_perm(__float_as_uint(f01.x), __float_as_uint(f01.y), 0x7632);
+  hi = __byte_perm(__float_as_uint(f23.x), __float_as_uint(f23.y), 0x7632);
+}
+
 // low bytes of four rounding sums (see q8r2) -> one word of int8 codes
 __device__ __forceinline__ uint32_t pack_sums4(float2 a, float2 b) {
   return __byte_perm(__byte_perm(__float_as_uint(a.x), __float_as_uint(a.y), 0x0040),

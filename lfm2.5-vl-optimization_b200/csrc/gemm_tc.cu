@@ -47,6 +47,8 @@ namespace {
 constexpr int TM = 128;        // output rows per tile (UMMA M, one TMEM lane per row)
 constexpr int TK = 128;        // K bytes per pipeline stage: one 128-byte swizzle row
 constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (2 per TMEM lane quarter)
+// threads per CTA: W8 adds 4 warps (warps 2-5 epilogue, 6-13 weight converters)
+__host__ __device__ constexpr int cta_threads(int epi) { return epi == EPI_W8 ? NTHREADS + 128 : NTHREADS; }
 constexpr int EPI_WARPS = 8;
 constexpr long long WAIT_LIMIT = 1ll << 31;
 
@@ -61,6 +63,7 @@ struct GemmArgs {
   int Nout;           // output columns
   int tiles_m, tiles_n;
   int m_fast;         // tile raster: 1 = consecutive tiles walk M (A stays in L2), 0 = walk N
+  const int8_t *Wq;   // W8: int8 weights [N, K], staged as bf16 by the converter warps
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -169,6 +172,28 @@ __host__ __device__ constexpr uint32_t idesc_i8(int n, int m) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both operands K-major
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, int m) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+template <int CG>
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  if constexpr (CG == 2)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
   asm volatile(
@@ -214,8 +239,12 @@ __device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
       :
       : "memory");
 }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void st_shared16(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint4 ld_global16(const void *p) {
+  return __ldg(reinterpret_cast<const uint4 *>(p));
 }
 __device__ __forceinline__ uint4 ld_shared16(uint32_t addr) {
   uint4 v;
@@ -284,7 +313,7 @@ struct Smem {
 // (r = 0) issues the M = 256 MMAs, and each CTA's epilogue drains its own 128 TMEM lanes. Per SM this halves the B
 // bytes staged in shared memory and cuts the L2 -> SM bytes per MMA by a third against one CTA on a 128 x 256 tile.
 template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(cta_threads(EPI), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs args) {
   using L = Smem<BN / CG, STAGES>;  // per CTA: A 128 rows, B BN / CG rows per stage
@@ -294,8 +323,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   static_assert(!GROUPED || BN == 128, "grouped tiles are 128 columns wide");
   static_assert(CG == 1 || (CG == 2 && !GROUPED && BN % 32 == 0), "CTA pairs run the per-token epilogues");
   static_assert(EPI != EPI_SILU || BN == 256, "the SiLU tile holds 128 gate and 128 up rows");
+  constexpr bool W8 = (EPI == EPI_W8);
+  constexpr int EW = W8 ? 4 : EPI_WARPS;  // epilogue warps (W8: warps 2-5; warps 6-13 convert the weights)
+  constexpr int KPS = W8 ? TK / 2 : TK;   // K elements per stage (128 bytes of a row: int8 or bf16)
+  static_assert(!W8 || (BN / CG) % 64 == 0, "eight converter warps stage B in 8-row groups");
   constexpr int TMU = TM * CG;  // output rows per tile
-  constexpr uint32_t IDESC = idesc_i8(BN, TMU);
+  constexpr uint32_t IDESC = W8 ? idesc_bf16(BN, TMU) : idesc_i8(BN, TMU);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -310,7 +343,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = args.M, K = args.K;
-  const int KB = (K + TK - 1) / TK;      // pipeline stages per tile
+  const int KB = (K + KPS - 1) / KPS;    // pipeline stages per tile
   const int G = K / 64;                  // grouped: 64-wide K groups (K % 64 == 0)
   const int tiles = args.tiles_m * args.tiles_n;
   // work unit = one CTA (CG = 1) or one CTA pair (CG = 2, consecutive blockIdx.x form a cluster)
@@ -322,12 +355,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full(s), 1);   // leader: its producer's arrive (expect_tx for both CTAs' bytes)
+      // leader: its producer's arrive (expect_tx for both CTAs' TMA bytes), plus W8: one per converter warp of each CTA
+      mbar_init(bar_full(s), W8 ? 1 + 8 * CG : 1);
       mbar_init(bar_empty(s), 1);  // every CTA: one commit from the (leader's) MMA thread
     }
     for (int a = 0; a < 4; ++a) {
       mbar_init(bar_tfull(a), 1);
-      mbar_init(bar_tempty(a), EPI_WARPS * CG);  // one arrival per epilogue warp of every CTA of the unit
+      mbar_init(bar_tempty(a), EW * CG);  // one arrival per epilogue warp of every CTA of the unit
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -369,14 +403,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
           if constexpr (CG == 2) {
             const uint32_t fb = lead(bar_full(stage));
-            if (rank == 0) mbar_expect_tx(bar_full(stage), 2 * (L::A_BYTES + L::B_BYTES));
-            tma_load_2d_pair(sa, &tmA, fb, kb * TK, mt * TMU + (int)rank * TM);
+            if (rank == 0) mbar_expect_tx(bar_full(stage), 2 * (L::A_BYTES + (W8 ? 0 : L::B_BYTES)));
+            tma_load_2d_pair(sa, &tmA, fb, kb * KPS, mt * TMU + (int)rank * TM);
             const int brow = (EPI == EPI_SILU) ? (rank ? args.Nout : 0) + nt * (BN / 2) : nt * BN + (int)rank * (BN / 2);
-            tma_load_2d_pair(sb, &tmB, fb, kb * TK, brow);
+            if (!W8) tma_load_2d_pair(sb, &tmB, fb, kb * TK, brow);
           } else {
-            mbar_expect_tx(bar_full(stage), L::A_BYTES + L::B_BYTES);
-            tma_load_2d(sa, &tmA, bar_full(stage), kb * TK, mt * TM);
-            if (EPI == EPI_SILU) {
+            mbar_expect_tx(bar_full(stage), L::A_BYTES + (W8 ? 0 : L::B_BYTES));
+            tma_load_2d(sa, &tmA, bar_full(stage), kb * KPS, mt * TM);
+            if (W8) {
+              // B: staged by the converter warps
+            } else if (EPI == EPI_SILU) {
               tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * (BN / 2));
               tma_load_2d(sb + (BN / 2) * TK, &tmB, bar_full(stage), kb * TK, args.Nout + nt * (BN / 2));
             } else {
@@ -421,7 +457,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint64_t bd = sw128_desc(sbase + L::B_OFF + stage * L::B_BYTES);
 #pragma unroll
             for (int k = 0; k < TK / 32; ++k) {  // +32 bytes of K per MMA = +2 in the 16-byte address field
-              if constexpr (CG == 2)
+              if constexpr (W8)
+                umma_bf16<CG>(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+              else if constexpr (CG == 2)
                 umma_i8_pair(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
               else
                 umma_i8(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
@@ -473,16 +511,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     mma_done:;
     }
-  } else {
-    // ---------------------------------------------------------------- epilogue warps 2..9
-    // Warp w reads TMEM lane quarter w % 4 (tile rows 32q..32q+31) and owns one half of the tile's output columns.
-    const int ew = warp - 2;          // epilogue warp 0..7
+  } else if (warp < 2 + EW) {
+    // ---------------------------------------------------------------- epilogue warps 2..9 (W8: 2..5)
+    // Warp w reads TMEM lane quarter w % 4 (tile rows 32q..32q+31) and owns one half of the tile's output columns
+    // (W8: all of them).
+    constexpr int PARW = EPI_WARPS * L::PAR_FLOATS / EW;  // parameter floats per warp: weight scales, then bias
+    constexpr int PF = PARW / 64;                         // parameters per lane
+    const int ew = warp - 2;          // epilogue warp 0..EW-1
     const int q = warp & 3;           // TMEM lane quarter this warp may access
     const int half = ew >> 2;         // which half of the columns
     const int row = q * 32 + lane;    // tile row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * L::PAR_FLOATS;  // [128] weight scales
-    float *par_b = par_sw + 128;                                                           // [128] bias
+    float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * PARW;  // [PARW / 2] weight scales
+    float *par_b = par_sw + PARW / 2;                                           // [PARW / 2] bias
     const uint32_t out_buf = sbase + L::OUT_OFF + ew * L::OUT_BLOCK;
     int acc = 0;
     uint32_t aphase = 0;
@@ -491,18 +532,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // next tile in registers (loaded one tile ahead, so their latency hides behind a whole tile of work) and writes
     // them to the warp's shared memory when that tile starts. Entry i: output column c0 + i; with `silu`, entries
     // CW.. hold the up rows (weight rows Nout + column).
-    float pf_sw[4], pf_b[4], pf_sx = 0.f;
+    float pf_sw[PF], pf_b[PF], pf_sx = 0.f;
     auto prefetch = [&](int tile_i) {
       if (tile_i >= tiles) return;
       int pmt, pnt;
       tile_coord(tile_i, args, pmt, pnt);
       const int pm = pmt * TMU + (int)rank * TM + row;
-      pf_sx = (pm < M && !GROUPED) ? __ldg(args.sa + pm) : 0.f;
-      const int width = (EPI == EPI_SILU) ? BN / 4 : BN / 2;
+      pf_sx = (pm < M && !GROUPED && !W8) ? __ldg(args.sa + pm) : 0.f;
+      const int width = (EPI == EPI_SILU) ? BN / 4 : (W8 ? BN : BN / 2);
       const int c0 = (EPI == EPI_SILU) ? pnt * (BN / 2) + half * width : pnt * BN + half * width;
       const int count = (EPI == EPI_SILU) ? 2 * width : width;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < PF; ++k) {
         const int i = lane + 32 * k;
         const int oc = c0 + ((EPI == EPI_SILU) ? (i % width) : i);
         const int col = (EPI == EPI_SILU && i >= width) ? args.Nout + oc : oc;
@@ -514,7 +555,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto stage_params = [&]() {
       __syncwarp();
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < PF; ++k) {
         par_sw[lane + 32 * k] = pf_sw[k];
         par_b[lane + 32 * k] = pf_b[k];
       }
@@ -591,6 +632,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float4 s4 = ps[j4], b4 = pb[j4];
             o[2 * j4] = epi_token2<GELU>(r[cur][4 * j4], r[cur][4 * j4 + 1], sxm, s4.x, s4.y, b4.x, b4.y);
             o[2 * j4 + 1] = epi_token2<GELU>(r[cur][4 * j4 + 2], r[cur][4 * j4 + 3], sxm, s4.z, s4.w, b4.z, b4.w);
+          }
+          store_chunk(o, c0 + c * 32, yrow);
+          if (c + 1 < NCH) tmem_wait_tie(r[nxt]);
+        }
+      } else if (EPI == EPI_W8) {
+        // fp32 accumulators: y = bf16(act(acc * sw[n] + b[n])), the reference's W8A16 epilogue order
+        constexpr int NCH = BN / 32;  // the warp's 32 rows x all BN columns
+        const int c0 = nt * BN;
+        if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem_base + lane_addr + acc * BN;
+        uint32_t r[2][32];
+        tmem_ld32(tb, r[0]);
+        tmem_wait_tie(r[0]);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          const int cur = c & 1, nxt = cur ^ 1;
+          if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, r[nxt]);
+          else release_acc();
+          uint32_t o[16];
+          const float4 *ps = reinterpret_cast<const float4 *>(par_sw + c * 32);
+          const float4 *pb = reinterpret_cast<const float4 *>(par_b + c * 32);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 s4 = ps[j4], b4 = pb[j4];
+            const float sv[4] = {s4.x, s4.y, s4.z, s4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+            float y[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              y[e] = __fadd_rn(__fmul_rn(__uint_as_float(r[cur][4 * j4 + e]), sv[e]), bv[e]);
+              if (GELU) y[e] = gelu_tanh(y[e]);
+            }
+            o[2 * j4] = pack_bf16x2(y[0], y[1]);
+            o[2 * j4 + 1] = pack_bf16x2(y[2], y[3]);
           }
           store_chunk(o, c0 + c * 32, yrow);
           if (c + 1 < NCH) tmem_wait_tie(r[nxt]);
@@ -716,6 +791,89 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
     }
+  } else if constexpr (W8) {
+    // ---------------------------------------------------------------- W8 weight converters, warps 6..13
+    // Each stage, this CTA's BN / CG weight rows x 64 K of int8 become bf16 in the B stage: converter warp cw owns the
+    // 8-row groups cw, cw + 8, ...; in a group, 4 lanes share a row (16 contiguous weights each: coalesced 64-byte
+    // row segments), convert exactly (exponent-bias trick) and write the two 16-byte units of their 32 bf16 bytes
+    // at the 128-byte-swizzled positions the MMA descriptor expects (unit u of row r at u ^ (r & 7)). The loads run
+    // two stages ahead (ping-pong registers); rows >= N and K >= K read as zero. Then: proxy fence (the tensor core
+    // reads through the async proxy), and one arrival per warp on the pair leader's full barrier.
+    constexpr int NCW = 8;                  // converter warps
+    constexpr int BROWS = BN / CG;          // weight rows this CTA stages per tile
+    constexpr int ITER = BROWS / (8 * NCW);  // 8-row groups per converter warp and stage
+    static_assert(BROWS % (8 * NCW) == 0, "converter rows");
+    const int cw = warp - 2 - EW;           // converter warp 0..NCW-1
+    const int lr = lane >> 2, lc = lane & 3;
+    const int my_tiles = unit < tiles ? (tiles - 1 - unit) / units + 1 : 0;
+    const int total = my_tiles * KB;  // stages this CTA runs
+    // next stage to load: walked in order, tile coordinates recomputed once per tile
+    int ld_j = 0, ld_kb = 0, ld_tile = unit, ld_nt = 0;
+    if (ld_tile < tiles) {
+      int mt0;
+      tile_coord(ld_tile, args, mt0, ld_nt);
+    }
+    auto load_next = [&](uint4 (&buf)[ITER]) {
+      if (ld_j >= total) return;
+      const int k = ld_kb * KPS + lc * 16;
+      const int nbase = ld_nt * BN + (int)rank * BROWS + cw * 8 + lr;
+#pragma unroll
+      for (int it = 0; it < ITER; ++it) {
+        const int n = nbase + it * 8 * NCW;
+        buf[it] = (n < args.N && k < K) ? ld_global16(args.Wq + (size_t)n * K + k) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      ++ld_j;
+      if (++ld_kb == KB) {
+        ld_kb = 0;
+        ld_tile += units;
+        if (ld_tile < tiles) {
+          int mt0;
+          tile_coord(ld_tile, args, mt0, ld_nt);
+        }
+      }
+    };
+    int c_stage = 0;
+    uint32_t c_phase = 0;
+    auto consume = [&](const uint4 (&buf)[ITER]) -> bool {
+      const int stage = c_stage;
+      if (!warp_wait(bar_empty(stage), c_phase ^ 1, abort_flag)) return false;
+      const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
+#pragma unroll
+      for (int it = 0; it < ITER; ++it) {
+        const int rr = (it * NCW + cw) * 8 + lr;
+        uint32_t o[8];
+        i8x4_to_bf16x2x2(buf[it].x, o[0], o[1]);
+        i8x4_to_bf16x2x2(buf[it].y, o[2], o[3]);
+        i8x4_to_bf16x2x2(buf[it].z, o[4], o[5]);
+        i8x4_to_bf16x2x2(buf[it].w, o[6], o[7]);
+        const uint32_t rowa = sb + rr * 128;
+        st_shared16(rowa + (((2 * lc) ^ (rr & 7)) << 4), o[0], o[1], o[2], o[3]);
+        st_shared16(rowa + (((2 * lc + 1) ^ (rr & 7)) << 4), o[4], o[5], o[6], o[7]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_cluster(lead(bar_full(stage)));
+        else
+          mbar_arrive(bar_full(stage));
+      }
+      if (++c_stage == STAGES) {
+        c_stage = 0;
+        c_phase ^= 1;
+      }
+      return true;
+    };
+    uint4 ping[ITER], pong[ITER];
+    load_next(ping);
+    load_next(pong);
+    for (int j = 0; j < total; j += 2) {
+      if (!consume(ping)) break;
+      load_next(ping);
+      if (j + 1 >= total) break;
+      if (!consume(pong)) break;
+      load_next(pong);
+    }
   }
 
   tc_fence_before();
@@ -763,6 +921,20 @@ bool make_map(CUtensorMap *map, const void *ptr, int inner, int rows, int box_ro
   return r == CUDA_SUCCESS;
 }
 
+// 2-D bf16 matrix [rows, inner] row-major, box = 64 elements (128 bytes) x box_rows, 128-byte swizzle, OOB reads zero
+bool make_map_bf16(CUtensorMap *map, const void *ptr, int inner, int rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+  cuuint32_t box[2] = {(cuuint32_t)(TK / 2), (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int g_tile_override = 0;
 
 template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
@@ -780,7 +952,7 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(NTHREADS);
+  cfg.blockDim = dim3(cta_threads(EPI));
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -799,8 +971,13 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
   });
   if (attr_err != cudaSuccess) return attr_err;
   CUtensorMap ta, tb;
-  const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN / CG;
-  if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, box_b)) return cudaErrorInvalidValue;
+  if (EPI == EPI_W8) {  // bf16 activations by TMA; the int8 weights are read by the converter warps (a.Wq)
+    memset(&tb, 0, sizeof(tb));
+    if (!make_map_bf16(&ta, A, a.K, a.M, TM)) return cudaErrorInvalidValue;
+  } else {
+    const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN / CG;
+    if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, box_b)) return cudaErrorInvalidValue;
+  }
   const int tiles = a.tiles_m * a.tiles_n;
   const int units = tiles < max_units[dev & 63] ? tiles : max_units[dev & 63];
   cfg.gridDim = dim3(CG * units);
@@ -898,9 +1075,24 @@ cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *
 }  // namespace lfm2q
 
 namespace lfm2q {
-// W8A16 is built in a later step; until then the entry point reports that it is unavailable.
-cudaError_t launch_gemm_w8(const void *, const int8_t *, const float *, const void *, void *, int, int, int, bool,
-                           cudaStream_t) {
-  return cudaErrorNotSupported;
+// W8A16: y = bf16(act(((bf16 x) . (int8 W -> bf16)^T) * sw + b)), fp32 accumulation in TMEM (tcgen05 kind::f16).
+// Reference: gemm_w8_kernel / launch_gemm_w8 (kernels/int8_gemm.cu:306-388, :765-780), op gemm_w8
+// (kernels/int8_gemm.cpp:72-79). CTA pairs on 256 x 256 tiles when one-CTA 128 x 256 tiles fill the GPU, else one
+// CTA per 128 x 128 tile; a forced tile width (lfm2q_set_gemm_tile) picks the same way by sign.
+cudaError_t launch_gemm_w8(const void *x, const int8_t *w, const float *sw, const void *bias, void *y, int M, int N,
+                           int K, bool gelu, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (M <= 16 && bias == nullptr && !gelu && K % 64 == 0 && g_tile_override == 0) {
+    // a few tokens, no bias / activation: y = bf16(acc * sw) is the weight-only decode GEMV, which streams W once
+    return launch_gemv(w, true, sw, x, y, N, K, 0, M, false, st);
+  }
+  const long tiles256 = (long)((M + TM - 1) / TM) * ((N + 255) / 256);
+  const bool pair = g_tile_override < 0 || (g_tile_override == 0 && tiles256 >= device_sm_count());
+  GemmArgs a = base_args(nullptr, sw, bias, M, N, K, N, pair ? 256 : 128, pair ? 2 * TM : TM);
+  a.Y = (bf16 *)y;
+  a.Wq = w;
+  if (pair)
+    return gelu ? run_tc<256, 6, 2, EPI_W8, true, 2>(x, w, a, st) : run_tc<256, 6, 2, EPI_W8, false, 2>(x, w, a, st);
+  return gelu ? run_tc<128, 6, 2, EPI_W8, true, 1>(x, w, a, st) : run_tc<128, 6, 2, EPI_W8, false, 1>(x, w, a, st);
 }
 }  // namespace lfm2q

@@ -36,7 +36,7 @@ cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scal
                             void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st);
 
 // gemm_tc.cu: tcgen05 W8A8 GEMMs
-enum GemmEpi { EPI_TOKEN = 0, EPI_GROUP = 1, EPI_GROUP_Q = 2, EPI_SILU = 3 };
+enum GemmEpi { EPI_TOKEN = 0, EPI_GROUP = 1, EPI_GROUP_Q = 2, EPI_SILU = 3, EPI_W8 = 4 };
 cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias, void *Y,
                            int M, int N, int K, bool gelu, bool grouped, cudaStream_t st);
 cudaError_t launch_gemm_i8_q(const int8_t *A, const float *saT, const int8_t *B, const float *sb, const void *bias,

@@ -186,3 +186,45 @@ def test_gemm_i8_silu(cuda_dev, silu_tile, M, K, I, bias):
 def test_device_error_word_clear(cuda_dev):
     torch.cuda.synchronize()
     assert _capi.lib().lfm2q_check_device(1) == 0
+
+
+# ------------------------------------------------------------------------------------------------ W8A16
+W8_CASES = [(9216, 4304, 1152, True, False), (2327, 8192, 2048, False, False), (272, 8192, 2048, False, False),
+            (9, 2048, 6144, False, False), (1, 2048, 2048, False, False), (1024, 1152, 4304, True, True),
+            (4096, 2048, 8192, False, False), (300, 1152, 264, True, False), (517, 16, 40, True, True)]
+
+
+@pytest.fixture(params=[0, 128, -256], ids=["auto", "one_cta", "pair"])
+def w8_tile(request):
+    _capi.lib().lfm2q_set_gemm_tile(request.param)
+    yield request.param
+    _capi.lib().lfm2q_set_gemm_tile(0)
+
+
+@pytest.mark.parametrize("M,K,N,bias,gelu", W8_CASES)
+def test_gemm_w8(cuda_dev, w8_tile, M, K, N, bias, gelu):
+    """W8A16 (bf16 x, int8 W converted exactly to bf16, fp32 accumulation): products are exact, so against fp64 the
+    relative error is the bf16 output rounding plus fp32 summation (<= 1.05x the rounding error); the reference's own
+    acceptance, <= 1.5x the error of a bf16 GEMM on dequantized weights (tests/test_int8_gemm.py:178-196), follows."""
+    if w8_tile and M * N > 12_000_000:
+        pytest.skip("forced tiles: the automatic run covers the big shapes")
+    g = torch.Generator().manual_seed(M + 7 * N + K)
+    x = torch.randn(M, K, generator=g).to(BF)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(BF)
+    b = torch.randn(N, generator=g).to(BF) if bias else None
+    wq, sw = quantize_int8(w)
+    y = torch.empty(M, N, device=cuda_dev, dtype=BF)
+    int8_ext().gemm_w8(x.to(cuda_dev), wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y, gelu)
+    assert _capi.lib().lfm2q_check_device(0) == 0
+    r64 = oracle.gemm_w8_f64(x, wq, sw, b, gelu)
+    yc = y.cpu().double()
+    e_ours = ((yc - r64).norm() / r64.norm()).item()
+    e_round = ((r64.to(BF).double() - r64).norm() / r64.norm()).item()
+    assert e_ours <= 1.05 * e_round + 1e-6, (e_ours, e_round)
+    if M * N * K <= 4e9:
+        wd = (wq.float() * sw[:, None]).to(BF)
+        rc = torch.nn.functional.linear(x.float(), wd.float(), None if b is None else b.float())
+        if gelu:
+            rc = torch.nn.functional.gelu(rc, approximate="tanh")
+        e_cub = ((rc.to(BF).double() - r64).norm() / r64.norm()).item()
+        assert e_ours <= 1.5 * e_cub + 1e-4, (e_ours, e_cub)
