@@ -20,9 +20,10 @@ namespace lfm2q {
 namespace {
 
 constexpr int QT = 256;  // threads per block (8 warps)
-constexpr int QC = 8;    // 16-byte chunks held per lane
 
-template <int RW, bool GROUPED>
+// QC: 16-byte chunks each lane holds (a row covers RW * 32 * QC chunks); fewer for short rows keeps registers, and
+// with them the rows in flight per SM, up
+template <int RW, bool GROUPED, int QC>
 __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, int8_t *__restrict__ q,
                                                    float *__restrict__ s, int rows, int K, int pdl) {
   // launched with programmatic serialization: let the next kernel (the GEMV / GEMM that reads q, s) start its own
@@ -121,9 +122,9 @@ template <bool GROUPED>
 cudaError_t run_quant(const void *x, int8_t *q, float *s, int rows, int K, bool pdl, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const int K8 = K / 8;
-  // smallest RW whose RW * 32 lanes * QC chunks cover the row
+  // smallest RW whose RW * 32 lanes * 8 chunks cover the row
   int rw = 1;
-  while (rw * 32 * QC < K8) rw *= 2;
+  while (rw * 32 * 8 < K8) rw *= 2;
   const bf16 *xx = (const bf16 *)x;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(QT);
@@ -135,10 +136,16 @@ cudaError_t run_quant(const void *x, int8_t *q, float *s, int rows, int K, bool 
   cfg.numAttrs = pdl ? 1 : 0;
   const int p = pdl ? 1 : 0;
   switch (rw) {
-    case 1: cfg.gridDim = dim3((rows + 7) / 8); return cudaLaunchKernelEx(&cfg, quant_kernel<1, GROUPED>, xx, q, s, rows, K, p);
-    case 2: cfg.gridDim = dim3((rows + 3) / 4); return cudaLaunchKernelEx(&cfg, quant_kernel<2, GROUPED>, xx, q, s, rows, K, p);
-    case 4: cfg.gridDim = dim3((rows + 1) / 2); return cudaLaunchKernelEx(&cfg, quant_kernel<4, GROUPED>, xx, q, s, rows, K, p);
-    case 8: cfg.gridDim = dim3(rows); return cudaLaunchKernelEx(&cfg, quant_kernel<8, GROUPED>, xx, q, s, rows, K, p);
+    case 1:
+      cfg.gridDim = dim3((rows + 7) / 8);
+      if (K8 <= 32 * 5) return cudaLaunchKernelEx(&cfg, quant_kernel<1, GROUPED, 5>, xx, q, s, rows, K, p);
+      return cudaLaunchKernelEx(&cfg, quant_kernel<1, GROUPED, 8>, xx, q, s, rows, K, p);
+    case 2: cfg.gridDim = dim3((rows + 3) / 4); return cudaLaunchKernelEx(&cfg, quant_kernel<2, GROUPED, 8>, xx, q, s, rows, K, p);
+    case 4:
+      cfg.gridDim = dim3((rows + 1) / 2);
+      if (K8 <= 4 * 32 * 5) return cudaLaunchKernelEx(&cfg, quant_kernel<4, GROUPED, 5>, xx, q, s, rows, K, p);
+      return cudaLaunchKernelEx(&cfg, quant_kernel<4, GROUPED, 8>, xx, q, s, rows, K, p);
+    case 8: cfg.gridDim = dim3(rows); return cudaLaunchKernelEx(&cfg, quant_kernel<8, GROUPED, 8>, xx, q, s, rows, K, p);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -19,7 +19,8 @@ def _x(M, K, seed, outlier=True):
 
 
 @pytest.mark.parametrize("M,K", [(1, 2048), (37, 1152), (2327, 2048), (9216, 1152), (5, 4304), (64, 8192),
-                                 (3, 16384), (300, 8), (17, 136), (1000, 2048)])
+                                 (3, 16384), (300, 8), (17, 136), (1000, 2048), (5001, 1280), (4097, 1296),
+                                 (65536, 1152), (700, 8)])
 def test_quant_rows(cuda_dev, M, K):
     x = _x(M, K, M * 7 + K)
     q, s = quantize_rows(x.to(cuda_dev))
