@@ -142,6 +142,12 @@ void lfm2q_set_gemv_path(int path);
  * (early == 0, default) or at their start (early != 0). Tuning only; results are unchanged. */
 void lfm2q_set_gemv_trigger(int early);
 
+/* Failure-detection self-test (no counterpart in the reference): launches one block that runs the GEMM pipeline's
+ * bounded mbarrier wait on a barrier nothing arrives on, with a limit of 2^limit_log2 clock cycles (10..31). The wait
+ * gives up, sets the device error word and the kernel ends normally; lfm2q_check_device then reports LFM2Q_ETIMEOUT
+ * (and clears it with clear != 0). The context stays usable. Asynchronous on `stream`. */
+int lfm2q_selftest_wait_timeout(int limit_log2, void *stream);
+
 /* Forces the per-token GEMM tile: 128 or 256 = one CTA per 128-row tile of that many columns; -192 or -256 = a CTA
  * pair (cluster of two, tcgen05 cta_group::2) per 256-row tile of that many columns; 0 = automatic. The SiLU GEMM
  * follows the sign (one CTA or a pair, 128 output columns per tile). Tuning and testing only. */

@@ -99,6 +99,12 @@ int lfm2q_check_device(int clear) {
   return LFM2Q_OK;
 }
 
+int lfm2q_selftest_wait_timeout(int limit_log2, void *stream) {
+  REQUIRE(limit_log2 >= 10 && limit_log2 <= 31, "limit_log2 must be in [10, 31] (clock cycles = 2^limit_log2)");
+  if (int e = device_gate()) return e;
+  return launched(launch_wait_timeout_selftest(limit_log2, (cudaStream_t)stream), "selftest_wait_timeout");
+}
+
 void lfm2q_set_pdl(int on) { g_pdl.store(on != 0); }
 void lfm2q_set_gemv_trigger(int early) { gemv_set_early_trigger(early != 0); }
 void lfm2q_set_gemv_impl(int) {}

@@ -32,6 +32,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -102,12 +103,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait for the phase with the given parity. Returns false when this or another role gave up.
 template <bool CL = false>
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *abort_flag, long long limit = WAIT_LIMIT) {
   if (mbar_try_wait<CL>(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait<CL>(bar, parity)) {
     if (*(volatile int *)abort_flag) return false;
-    if (clock64() - t0 > WAIT_LIMIT) {
+    if (clock64() - t0 > limit) {
       atomicExch(abort_flag, 1);
       atomicCAS(&g_gemm_err, 0, 1);
       return false;
@@ -935,7 +936,7 @@ bool make_map_bf16(CUtensorMap *map, const void *ptr, int inner, int rows, int b
   return r == CUDA_SUCCESS;
 }
 
-int g_tile_override = 0;
+std::atomic<int> g_tile_override{0};
 
 template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
 cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) {
@@ -1002,6 +1003,27 @@ GemmArgs base_args(const float *sa, const float *sb, const void *bias, int M, in
 
 }  // namespace
 
+namespace {
+// Failure-detection self-test: the pipeline's bounded wait on an mbarrier that nothing ever arrives on, with a short
+// limit. The wait gives up, records the error word and returns; the kernel ends normally and the context stays usable.
+__global__ void wait_timeout_selftest(long long limit) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_addr(&bar), 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(smem_addr(&bar), 0, &abort_flag, limit);
+}
+}  // namespace
+
+cudaError_t launch_wait_timeout_selftest(int limit_log2, cudaStream_t st) {
+  wait_timeout_selftest<<<1, 32, 0, st>>>(1ll << limit_log2);
+  return cudaGetLastError();
+}
+
 int gemm_device_error(bool clear) {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_gemm_err, sizeof(int));
@@ -1024,11 +1046,12 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
     a.Y = (bf16 *)Y;
     return gelu ? run_tc<128, 6, 4, EPI_GROUP, true, 1>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false, 1>(A, B, a, st);
   }
-  if (M <= 16 && K % 64 == 0 && !g_tile_override) {
+  const int ov = g_tile_override.load();
+  if (M <= 16 && K % 64 == 0 && !ov) {
     // skinny: the A8 GEMV streams W once with int8 MMAs (same exact int32 sums and the same epilogue)
     return launch_gemv_a8(B, sb, A, sa, bias, Y, N, K, M, gelu, false, st);
   }
-  int bn = g_tile_override;
+  int bn = ov;
   if (!bn) {
     // enough 128 x 256 tiles to fill the GPU: 256 x 256 CTA-pair tiles (measured 3-10% faster than one CTA per
     // 128 x 256 tile at K = 1152 .. 8192); otherwise one CTA per 128 x 128 tile for more parallelism
@@ -1065,7 +1088,8 @@ cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *
   // CTA pairs (256 rows x 128 output columns per tile) when one-CTA tiles would fill the GPU, unless a one-CTA tile
   // width is forced
   const long tiles1 = (long)((M + TM - 1) / TM) * ((I + 127) / 128);
-  const bool pair = g_tile_override < 0 || (g_tile_override == 0 && tiles1 >= device_sm_count());
+  const int ov = g_tile_override.load();
+  const bool pair = ov < 0 || (ov == 0 && tiles1 >= device_sm_count());
   GemmArgs a = base_args(sa, sb, bias, M, 2 * I, K, I, 128, pair ? 2 * TM : TM);
   a.Y = (bf16 *)Y;
   if (pair) return run_tc<256, 6, 2, EPI_SILU, false, 2>(A, B, a, st);
@@ -1082,12 +1106,13 @@ namespace lfm2q {
 cudaError_t launch_gemm_w8(const void *x, const int8_t *w, const float *sw, const void *bias, void *y, int M, int N,
                            int K, bool gelu, cudaStream_t st) {
   if (M <= 0 || N <= 0) return cudaSuccess;
-  if (M <= 16 && bias == nullptr && !gelu && K % 64 == 0 && g_tile_override == 0) {
+  const int ov = g_tile_override.load();
+  if (M <= 16 && bias == nullptr && !gelu && K % 64 == 0 && ov == 0) {
     // a few tokens, no bias / activation: y = bf16(acc * sw) is the weight-only decode GEMV, which streams W once
     return launch_gemv(w, true, sw, x, y, N, K, 0, M, false, st);
   }
   const long tiles256 = (long)((M + TM - 1) / TM) * ((N + 255) / 256);
-  const bool pair = g_tile_override < 0 || (g_tile_override == 0 && tiles256 >= device_sm_count());
+  const bool pair = ov < 0 || (ov == 0 && tiles256 >= device_sm_count());
   GemmArgs a = base_args(nullptr, sw, bias, M, N, K, N, pair ? 256 : 128, pair ? 2 * TM : TM);
   a.Y = (bf16 *)y;
   a.Wq = w;

@@ -14,6 +14,7 @@
 // identically for W and x (lane t, step s take physical k 16t+4s..16t+4s+3), which leaves the dot product
 // unchanged. Small N is split over K-slices (KS warps per row group) whose fp32 partials meet in shared memory
 // and are summed in a fixed order, so results are deterministic.
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <set>
@@ -698,8 +699,8 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_xs_kernel(const int8_t *_
 constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
 constexpr int XS_RING = 6;  // ring depth of the x-sliced kernels (K steps of 1 KB per warp)
 constexpr int GV_X_SMEM_MAX = 64 * 1024;  // fused-quantization A8 GEMV: B * (K + 64) bytes of int8 tokens
-bool g_early_trigger = false;
-int g_gemv_impl = 0;  // 0: x-sliced int8 path where it applies, 1: always the bf16-MMA path
+std::atomic<bool> g_early_trigger{false};
+std::atomic<int> g_gemv_impl{0};  // 0: x-sliced int8 path where it applies, 1: always the bf16-MMA path
 
 // (kernel, device) pairs whose dynamic shared memory limit has been raised
 std::mutex g_attr_mu;

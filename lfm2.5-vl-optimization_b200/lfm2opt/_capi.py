@@ -39,6 +39,7 @@ SIGNATURES = {
     "lfm2q_set_gemm_tile": [_i],
     "lfm2q_set_gemv_trigger": [_i],
     "lfm2q_set_gemv_path": [_i],
+    "lfm2q_selftest_wait_timeout": [_i, _p],
 }
 _VOID = {"lfm2q_set_pdl", "lfm2q_set_gemv_impl", "lfm2q_set_gemm_tile", "lfm2q_set_gemv_trigger",
          "lfm2q_set_gemv_path"}

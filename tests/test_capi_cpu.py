@@ -90,3 +90,9 @@ def test_python_binding_raises_with_reference_messages():
         ext().gemv(q, s, x, x)
     with pytest.raises(RuntimeError, match="xq must be contiguous CUDA"):
         E.gemm_i8(q, s, q, s, None, x, False)
+
+
+def test_selftest_rejects_bad_limits():
+    L = _capi.lib()
+    assert L.lfm2q_selftest_wait_timeout(5, None) == _capi.EINVAL
+    assert L.lfm2q_selftest_wait_timeout(40, None) == _capi.EINVAL
