@@ -357,24 +357,54 @@ class E2E:
         self.h2d_bytes = (self.hv.numel() + self.hl.numel() + self.hh.numel()) * 2
         self.d2h_bytes = cnt * 2
         self.logits = None
+        self.cs = torch.cuda.Stream(dev)  # host copies overlap the compute stream
+
+    def _d2h_chunk(self, off, dst, work):
+        """Copy this rank's share of a finished logits chunk to the host on the copy stream."""
+        s0, cnt = self.out_slice
+        a, b = max(off, s0), min(off + dst.numel(), s0 + cnt)
+        if a >= b:
+            return
+        if work is None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.job.dev))
+        with torch.cuda.stream(self.cs):
+            if work is None:
+                self.cs.wait_event(ev)
+            else:
+                work.wait()  # the copy stream (only) waits for this chunk's all-gather
+            flat = dst.reshape(-1)
+            self.hout[a - s0:b - s0].copy_(flat[a - off:b - off], non_blocking=True)
 
     def step(self):
+        """One step: inputs H2D, the job, this rank's logits share D2H. The vision input is copied first on the
+        compute stream; the LM and head inputs follow on a copy stream while the vision layers run, and each logits
+        chunk goes to the host on the copy stream as soon as it is complete. The step ends (compute stream) when its
+        outputs are on the host."""
+        cur = torch.cuda.current_stream(self.job.dev)
         self.dv.copy_(self.hv, non_blocking=True)
-        self.dl.copy_(self.hl, non_blocking=True)
-        self.dh.copy_(self.hh, non_blocking=True)
+        self.cs.wait_stream(cur)  # after everything this step's buffers were used for
+        with torch.cuda.stream(self.cs):
+            self.dl.copy_(self.hl, non_blocking=True)
+            ev_l = torch.cuda.Event()
+            ev_l.record(self.cs)
+            self.dh.copy_(self.hh, non_blocking=True)
+            ev_h = torch.cuda.Event()
+            ev_h.record(self.cs)
         for layer in self.vlin:
             layer[0](self.dv)
             layer[1](self.dv)
             h1 = layer[2](self.dv, gelu=True)
             layer[3](h1)
+        cur.wait_event(ev_l)
         for l, layer in enumerate(self.llin):
             layer[0](self.dl)
             layer[1](self.dl)
             a = layer[2](self.dl, silu_gate=True)
             layer[3](a)
-        self.logits = self.head(self.dh, self.logits)
-        s0, cnt = self.out_slice
-        self.hout.copy_(self.logits[s0:s0 + cnt], non_blocking=True)
+        cur.wait_event(ev_h)
+        self.logits = self.head(self.dh, self.logits, on_chunk=self._d2h_chunk)
+        cur.wait_stream(self.cs)
 
 
 # ----------------------------------------------------------------------------------------------- GEMV sweep

@@ -59,7 +59,10 @@ class NSplitHead:
     of that chunk writes it, so no copy follows the collective. `as_rows(buf, M)` materialises [M, V] (tests and
     consumers that want row-major logits). Each chunk's all-gather is issued asynchronously right after its GEMM;
     NCCL runs it on its own stream while the next chunk's GEMM runs on the current stream. Every rank must call
-    with the same M (the collectives are matched in order).
+    with the same M (the collectives are matched in order). on_chunk(off, dst, work), if given, is called as each chunk
+    is enqueued: off = its offset in the flat buffer, dst = its [g * rows, V/g] block, work = its all-gather handle
+    (None on one rank: dst is then complete in stream order on the current stream), so a consumer can start on a chunk
+    (e.g. copy it to the host on another stream after work.wait() there) while later chunks compute.
     """
 
     def __init__(self, linear, V: int, group=None, chunks: int = 4):
@@ -74,7 +77,7 @@ class NSplitHead:
     def chunk_bounds(self, M: int):
         return [shard_rows(M, self.chunks, c) for c in range(self.chunks)]
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out: torch.Tensor = None, on_chunk=None) -> torch.Tensor:
         M = x.shape[0]
         if out is None:
             out = torch.empty(self.world * M * self.slab, device=x.device, dtype=torch.bfloat16)
@@ -85,11 +88,16 @@ class NSplitHead:
                 continue
             local = self.linear(x[start:start + cnt])  # [cnt, slab] on the current stream
             dst = out[off:off + self.world * cnt * self.slab].view(self.world * cnt, self.slab)
+            c_off = off
             off += self.world * cnt * self.slab
             if self.world == 1:
                 dst.copy_(local)
+                if on_chunk is not None:
+                    on_chunk(c_off, dst, None)
                 continue
             works.append(dist.all_gather_into_tensor(dst, local.contiguous(), group=self.group, async_op=True))
+            if on_chunk is not None:
+                on_chunk(c_off, dst, works[-1])
         for w in works:
             w.wait()
         return out

@@ -59,8 +59,20 @@ def _head_worker(rank, world, port, M, V, K, chunks, q):
         wq, sw = oracle.quantize_int8_ref(w)
         hs = head_shard(V, world, rank)
         head = NSplitHead(_oracle_linear(wq[hs.lo:hs.hi].contiguous(), sw[hs.lo:hs.hi].contiguous()), V, chunks=chunks)
-        buf = head(x)
+        seen = []
+
+        def on_chunk(off, dst, work):  # a consumer of finished chunks: copies each one as soon as it is gathered
+            if work is not None:
+                work.wait()
+            seen.append((off, dst.reshape(-1).clone()))
+
+        buf = head(x, on_chunk=on_chunk)
         full = head.as_rows(buf, M)
+        # the chunks reported tile the buffer in order and hold the final gathered values
+        offs = [o for o, _ in seen]
+        assert offs == sorted(offs) and offs[0] == 0
+        assert sum(v.numel() for _, v in seen) == buf.numel()
+        assert all(torch.equal(v, buf[o:o + v.numel()]) for o, v in seen)
         xq, sx = oracle.quant_rows_ref(x)
         ref = oracle.gemm_i8_ref(xq, sx, wq, sw)
         q.put((rank, bool(torch.equal(full, ref)), tuple(full.shape)))
