@@ -1053,10 +1053,13 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
   }
   int bn = ov;
   if (!bn) {
-    // enough 128 x 256 tiles to fill the GPU: 256 x 256 CTA-pair tiles (measured 3-10% faster than one CTA per
-    // 128 x 256 tile at K = 1152 .. 8192); otherwise one CTA per 128 x 128 tile for more parallelism
+    // 256 x 256 CTA-pair tiles when there are at least 1.5 per cluster (3-10% faster than one CTA per 128 x 256 tile
+    // at 65536 rows, K = 1152 .. 8192); fewer pair tiles leave too much of the last wave idle, so one CTA per
+    // 128 x 256 tile while those fill half the SMs (M = 1024: 5-10% faster than 128 x 128), else 128 x 128
+    const int sms = device_sm_count();
     const long tiles256 = (long)((M + TM - 1) / TM) * ((N + 255) / 256);
-    bn = tiles256 >= device_sm_count() ? -256 : 128;
+    const long pair_tiles = (long)((M + 2 * TM - 1) / (2 * TM)) * ((N + 255) / 256);
+    bn = 2 * pair_tiles >= 3 * (sms / 2) ? -256 : (2 * tiles256 >= sms ? 256 : 128);
   }
   GemmArgs a = base_args(sa, sb, bias, M, N, K, N, bn < 0 ? -bn : bn, bn < 0 ? 2 * TM : TM);
   a.Y = (bf16 *)Y;
