@@ -105,7 +105,10 @@ int lfm2q_selftest_wait_timeout(int limit_log2, void *stream) {
   return launched(launch_wait_timeout_selftest(limit_log2, (cudaStream_t)stream), "selftest_wait_timeout");
 }
 
-void lfm2q_set_pdl(int on) { g_pdl.store(on != 0); }
+void lfm2q_set_pdl(int on) {
+  g_pdl.store(on != 0);
+  gemm_set_pdl(on != 0);
+}
 void lfm2q_set_gemv_trigger(int early) { gemv_set_early_trigger(early != 0); }
 void lfm2q_set_gemv_impl(int) {}
 void lfm2q_set_gemv_path(int path) { gemv_set_impl(path == 1 ? 1 : 0); }

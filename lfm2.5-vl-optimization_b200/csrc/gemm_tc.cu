@@ -65,6 +65,7 @@ struct GemmArgs {
   int tiles_m, tiles_n;
   int m_fast;         // tile raster: 1 = consecutive tiles walk M (A stays in L2), 0 = walk N
   const int8_t *Wq;   // W8: int8 weights [N, K], staged as bf16 by the converter warps
+  int pdl;            // launched as a programmatic dependent: weights may load before the previous grid completes
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -395,30 +396,54 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
       tma_prefetch_desc(&tmB);
       int stage = 0;
       uint32_t phase = 0;
+      constexpr uint32_t STAGE_TX = CG * (L::A_BYTES + (W8 ? 0 : L::B_BYTES));  // bytes the leader expects per stage
+      auto load_b = [&](int st, int nt, int kb) {
+        const uint32_t sb = sbase + L::B_OFF + st * L::B_BYTES;
+        if constexpr (CG == 2) {
+          const int brow = (EPI == EPI_SILU) ? (rank ? args.Nout : 0) + nt * (BN / 2) : nt * BN + (int)rank * (BN / 2);
+          tma_load_2d_pair(sb, &tmB, lead(bar_full(st)), kb * TK, brow);
+        } else if (EPI == EPI_SILU) {
+          tma_load_2d(sb, &tmB, bar_full(st), kb * TK, nt * (BN / 2));
+          tma_load_2d(sb + (BN / 2) * TK, &tmB, bar_full(st), kb * TK, args.Nout + nt * (BN / 2));
+        } else {
+          tma_load_2d(sb, &tmB, bar_full(st), kb * TK, nt * BN);
+        }
+      };
+      auto load_a = [&](int st, int mt, int kb) {
+        const uint32_t sa = sbase + L::A_OFF + st * L::A_BYTES;
+        if constexpr (CG == 2)
+          tma_load_2d_pair(sa, &tmA, lead(bar_full(st)), kb * KPS, mt * TMU + (int)rank * TM);
+        else
+          tma_load_2d(sa, &tmA, bar_full(st), kb * KPS, mt * TM);
+      };
+      // Programmatic dependent launch: the weights of the first pipeline pass do not depend on the previous kernel,
+      // so they load before griddepcontrol.wait; the activations (its output) after it.
+      int pre = 0;
+      if (args.pdl) {
+        if (!W8) {
+          const int my_tiles = unit < tiles ? (tiles - 1 - unit) / units + 1 : 0;
+          pre = my_tiles * KB < STAGES ? my_tiles * KB : STAGES;
+          for (int j = 0; j < pre; ++j) {
+            int mt, nt;
+            tile_coord(unit + (j / KB) * units, args, mt, nt);
+            if (rank == 0) mbar_expect_tx(bar_full(j), STAGE_TX);
+            load_b(j, nt, j % KB);
+          }
+        }
+        pdl_wait();
+      }
+      int j = 0;
       for (int tile = unit; tile < tiles; tile += units) {
         int mt, nt;
         tile_coord(tile, args, mt, nt);
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(bar_empty(stage), phase ^ 1, abort_flag)) goto producer_done;
-          const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
-          const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
-          if constexpr (CG == 2) {
-            const uint32_t fb = lead(bar_full(stage));
-            if (rank == 0) mbar_expect_tx(bar_full(stage), 2 * (L::A_BYTES + (W8 ? 0 : L::B_BYTES)));
-            tma_load_2d_pair(sa, &tmA, fb, kb * KPS, mt * TMU + (int)rank * TM);
-            const int brow = (EPI == EPI_SILU) ? (rank ? args.Nout : 0) + nt * (BN / 2) : nt * BN + (int)rank * (BN / 2);
-            if (!W8) tma_load_2d_pair(sb, &tmB, fb, kb * TK, brow);
+        for (int kb = 0; kb < KB; ++kb, ++j) {
+          if (j < pre) {
+            load_a(stage, mt, kb);  // fresh stage, B already on its way, expect_tx posted
           } else {
-            mbar_expect_tx(bar_full(stage), L::A_BYTES + (W8 ? 0 : L::B_BYTES));
-            tma_load_2d(sa, &tmA, bar_full(stage), kb * KPS, mt * TM);
-            if (W8) {
-              // B: staged by the converter warps
-            } else if (EPI == EPI_SILU) {
-              tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * (BN / 2));
-              tma_load_2d(sb + (BN / 2) * TK, &tmB, bar_full(stage), kb * TK, args.Nout + nt * (BN / 2));
-            } else {
-              tma_load_2d(sb, &tmB, bar_full(stage), kb * TK, nt * BN);
-            }
+            if (!mbar_wait(bar_empty(stage), phase ^ 1, abort_flag)) goto producer_done;
+            if (rank == 0) mbar_expect_tx(bar_full(stage), STAGE_TX);
+            load_a(stage, mt, kb);
+            if (!W8) load_b(stage, nt, kb);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -426,6 +451,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
           }
         }
       }
+      if (args.pdl) pdl_trigger();  // every load is issued: the next kernel may start its own prologue
       // CTA pair: wait until every stage has been released once more, so no commit from the leader is still on its
       // way to this CTA's barriers when it exits
       if constexpr (CG == 2) {
@@ -600,6 +626,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
       }
     };
 
+    if (args.pdl) pdl_wait();  // the per-token scales come from the previous kernel
     prefetch(unit);
     for (int tile = unit; tile < tiles; tile += units) {
       int mt, nt;
@@ -677,18 +704,16 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
         if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) break;
         tc_fence_after();
         const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
-        uint32_t rg[2][32], ru[2][32];
-        tmem_ld32(tb, rg[0]);
-        tmem_ld32(tb + 32, rg[1]);
-        tmem_ld32(tb + BN / 2, ru[0]);
-        tmem_ld32(tb + BN / 2 + 32, ru[1]);
-        tmem_wait_tie(rg[0]);
-        tmem_wait_tie(rg[1]);
-        tmem_wait_tie(ru[0]);
-        tmem_wait_tie(ru[1]);
-        release_acc();
+        // one 32-column chunk at a time (gate and up): 64 registers of TMEM data live, not 128; the accumulator is
+        // released once the last chunk is in registers
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(tb + c * 32, rg);
+          tmem_ld32(tb + BN / 2 + c * 32, ru);
+          tmem_wait_tie(rg);
+          tmem_wait_tie(ru);
+          if (c == 1) release_acc();
           uint32_t o[16];
           const float4 *pgs = reinterpret_cast<const float4 *>(par_sw + c * 32);  // broadcast 16-byte reads
           const float4 *pgb = reinterpret_cast<const float4 *>(par_b + c * 32);
@@ -700,9 +725,9 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int j = 4 * j4 + 2 * h;
-              const float2 g = epi_pair(rg[c][j], rg[c][j + 1], sxm, h ? gs.z : gs.x, h ? gs.w : gs.y,
+              const float2 g = epi_pair(rg[j], rg[j + 1], sxm, h ? gs.z : gs.x, h ? gs.w : gs.y,
                                         h ? gb.z : gb.x, h ? gb.w : gb.y);
-              const float2 u = epi_pair(ru[c][j], ru[c][j + 1], sxm, h ? us.z : us.x, h ? us.w : us.y,
+              const float2 u = epi_pair(ru[j], ru[j + 1], sxm, h ? us.z : us.x, h ? us.w : us.y,
                                         h ? ub.z : ub.x, h ? ub.w : ub.y);
               const float g0 = rbf(g.x), g1 = rbf(g.y);
               const float2 sg = make_float2(rbf(__fdividef(g0, 1.f + __expf(-g0))), rbf(__fdividef(g1, 1.f + __expf(-g1))));
@@ -937,6 +962,7 @@ bool make_map_bf16(CUtensorMap *map, const void *ptr, int inner, int rows, int b
 }
 
 std::atomic<int> g_tile_override{0};
+std::atomic<bool> g_gemm_pdl{true};  // GEMMs launch as programmatic dependents (lfm2q_set_pdl)
 
 template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
 cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) {
@@ -947,17 +973,21 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CG;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int nattr = 0;
+  if (CG > 1) {
+    attr[nattr].id = cudaLaunchAttributeClusterDimension;
+    attr[nattr].val.clusterDim.x = CG;
+    attr[nattr].val.clusterDim.y = 1;
+    attr[nattr].val.clusterDim.z = 1;
+    ++nattr;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(cta_threads(EPI));
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = CG > 1 ? 1 : 0;
+  cfg.numAttrs = nattr;
   std::call_once(once[dev & 63], [&] {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
     int n = device_sm_count() / CG;
@@ -982,6 +1012,12 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
   const int tiles = a.tiles_m * a.tiles_n;
   const int units = tiles < max_units[dev & 63] ? tiles : max_units[dev & 63];
   cfg.gridDim = dim3(CG * units);
+  a.pdl = g_gemm_pdl.load() ? 1 : 0;
+  if (a.pdl) {
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = ++nattr;
+  }
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
 }
 
@@ -1033,6 +1069,8 @@ int gemm_device_error(bool clear) {
   }
   return v;
 }
+
+void gemm_set_pdl(bool on) { g_gemm_pdl.store(on); }
 
 void gemm_set_tile_override(int bn) {
   g_tile_override = (bn == 128 || bn == 256 || bn == -192 || bn == -256) ? bn : 0;

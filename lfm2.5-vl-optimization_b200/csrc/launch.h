@@ -45,7 +45,8 @@ cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *
                                 void *Y, int M, int I, int K, cudaStream_t st);
 int gemm_device_error(bool clear);
 cudaError_t launch_wait_timeout_selftest(int limit_log2, cudaStream_t st);  // sticky code written by a bounded wait that gave up (0 = none)
-void gemm_set_tile_override(int bn);  // 0 = heuristic, 128 / 256 = force the per-token tile width
+void gemm_set_tile_override(int bn);
+void gemm_set_pdl(bool on);  // 0 = heuristic, 128 / 256 = force the per-token tile width
 
 // gemm_w8.cu: tcgen05 W8A16 GEMM
 cudaError_t launch_gemm_w8(const void *A, const int8_t *B, const float *sb, const void *bias, void *Y, int M, int N,
