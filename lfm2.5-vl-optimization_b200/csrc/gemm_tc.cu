@@ -48,10 +48,13 @@ namespace {
 constexpr int TM = 128;        // output rows per tile (UMMA M, one TMEM lane per row)
 constexpr int TK = 128;        // K bytes per pipeline stage: one 128-byte swizzle row
 constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (2 per TMEM lane quarter)
-// threads per CTA: W8 adds 4 warps (warps 2-5 epilogue, 6-13 weight converters)
-__host__ __device__ constexpr int cta_threads(int epi) { return epi == EPI_W8 ? NTHREADS + 128 : NTHREADS; }
 constexpr int EPI_WARPS = 8;
+// epilogue warps: W8 4 (warps 6-13 convert the weights), else 8
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_W8 ? 4 : EPI_WARPS; }
+// threads per CTA: producer + MMA warps, the epilogue warps, W8 also 8 converter warps
+__host__ __device__ constexpr int cta_threads(int epi) { return epi == EPI_W8 ? NTHREADS + 128 : NTHREADS; }
 constexpr long long WAIT_LIMIT = 1ll << 31;
+constexpr uint32_t ACC_BIAS = 0x4B400000u;  // bit pattern of 1.5 * 2^23
 
 struct GemmArgs {
   const float *sa;    // sx [M] (per token) or sxT [K/64][M] (grouped)
@@ -228,7 +231,6 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Wait for this thread's TMEM loads with the destination registers tied to the wait, so no use of them can be
 // scheduled before it.
 __device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
@@ -266,9 +268,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr)
       : "memory");
 }
-
-// exact (float)v for |v| < 2^22: add into the mantissa of 1.5 * 2^23 and subtract it again
-__device__ __forceinline__ float i2f_small(int v) { return __int_as_float(v + 0x4B400000) - 12582912.f; }
 
 __device__ __forceinline__ void tile_coord(int tile, const GemmArgs &a, int &mt, int &nt) {
   if (a.m_fast) {
@@ -326,7 +325,8 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
   static_assert(CG == 1 || (CG == 2 && !GROUPED && BN % 32 == 0), "CTA pairs run the per-token epilogues");
   static_assert(EPI != EPI_SILU || BN == 256, "the SiLU tile holds 128 gate and 128 up rows");
   constexpr bool W8 = (EPI == EPI_W8);
-  constexpr int EW = W8 ? 4 : EPI_WARPS;  // epilogue warps (W8: warps 2-5; warps 6-13 convert the weights)
+  constexpr int EW = epi_warps(EPI);  // epilogue warps 2 .. 2 + EW - 1 (W8: warps 6-13 convert the weights)
+  constexpr int PARTS = EW / 4;       // column parts per TMEM lane quarter
   constexpr int KPS = W8 ? TK / 2 : TK;   // K elements per stage (128 bytes of a row: int8 or bf16)
   static_assert(!W8 || (BN / CG) % 64 == 0, "eight converter warps stage B in 8-row groups");
   constexpr int TMU = TM * CG;  // output rows per tile
@@ -546,7 +546,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
     constexpr int PF = PARW / 64;                         // parameters per lane
     const int ew = warp - 2;          // epilogue warp 0..EW-1
     const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const int half = ew >> 2;         // which half of the columns
+    const int half = ew >> 2;         // which part of the columns (PARTS per lane quarter)
     const int row = q * 32 + lane;    // tile row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF) + ew * PARW;  // [PARW / 2] weight scales
@@ -566,7 +566,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
       tile_coord(tile_i, args, pmt, pnt);
       const int pm = pmt * TMU + (int)rank * TM + row;
       pf_sx = (pm < M && !GROUPED && !W8) ? __ldg(args.sa + pm) : 0.f;
-      const int width = (EPI == EPI_SILU) ? BN / 4 : (W8 ? BN : BN / 2);
+      const int width = (EPI == EPI_SILU) ? BN / 4 : BN / PARTS;
       const int c0 = (EPI == EPI_SILU) ? pnt * (BN / 2) + half * width : pnt * BN + half * width;
       const int count = (EPI == EPI_SILU) ? 2 * width : width;
 #pragma unroll
@@ -628,6 +628,34 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
 
     if (args.pdl) pdl_wait();  // the per-token scales come from the previous kernel
     prefetch(unit);
+
+    // Grouped: the activation scale of (this lane's row, K group) is loaded three groups ahead of its fold, into a
+    // three-register queue that runs on into the next tile (a scale loaded one group ahead left every group waiting
+    // out a DRAM round trip). sl_*: the next (tile, group) to load and that tile's row for this lane.
+    auto tile_row = [&](int t) {
+      int tm_, tn_;
+      tile_coord(t, args, tm_, tn_);
+      return tm_ * TMU + (int)rank * TM + row;
+    };
+    int sl_tile = unit, sl_g = 0, sl_m = unit < tiles ? tile_row(unit) : M;
+    auto scale_next = [&]() {
+      float v = 0.f;
+      if (sl_tile < tiles) {
+        if (sl_m < M) v = __ldg(args.sa + (size_t)sl_g * M + sl_m);
+        if (++sl_g == G) {
+          sl_g = 0;
+          sl_tile += units;
+          sl_m = sl_tile < tiles ? tile_row(sl_tile) : M;
+        }
+      }
+      return v;
+    };
+    float sq0 = 0.f, sq1 = 0.f, sq2 = 0.f;
+    if constexpr (GROUPED) {
+      sq0 = scale_next();
+      sq1 = scale_next();
+      sq2 = scale_next();
+    }
     for (int tile = unit; tile < tiles; tile += units) {
       int mt, nt;
       tile_coord(tile, args, mt, nt);
@@ -738,33 +766,46 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
           store_chunk(o, c0 + c * 32, yrow);
         }
       } else {
-        // grouped: fold every 64-wide K group into fp32 running sums held in registers (64 columns per warp)
-        constexpr int CW = BN / 2;
+        // grouped: fold every 64-wide K group into fp32 running sums held in registers (CW = 64 columns per warp; QOUT's
+        // row-group scale needs a warp's 64 columns)
+        constexpr int CW = BN / PARTS, NLD = CW / 32;
         const int c0 = nt * BN + half * CW;
         float f[CW];
 #pragma unroll
         for (int j = 0; j < CW; ++j) f[j] = 0.f;
-        float s_next = (mrow && G > 0) ? __ldg(args.sa + m) : 0.f;
         bool ok = true;
         for (int g = 0; g < G; ++g) {
-          const float s = s_next;
+          const float s = sq0;
+          sq0 = sq1;
+          sq1 = sq2;
+          sq2 = scale_next();
           if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
-          uint32_t r0[32], r1[32];
-          tmem_ld32(tb, r0);
-          tmem_ld32(tb + 32, r1);
-          tmem_wait_tie(r0);
-          tmem_wait_tie(r1);
+          uint32_t r[NLD][32];
+#pragma unroll
+          for (int l = 0; l < NLD; ++l) tmem_ld32(tb + 32 * l, r[l]);
+#pragma unroll
+          for (int l = 0; l < NLD; ++l) tmem_wait_tie(r[l]);
           release_acc();
-          if (g + 1 < G) s_next = mrow ? __ldg(args.sa + (size_t)(g + 1) * M + m) : 0.f;
+          // f = fmaf((float)acc, s, f) per element, two at a time: the partial sums (|acc| < 2^22) become exact
+          // floats through the 1.5 * 2^23 mantissa trick (integer add, packed subtract), then one packed fused
+          // multiply-add: 2 instructions per element instead of 3, the same roundings
+          const float2 big2 = make_float2(12582912.f, 12582912.f), s2 = make_float2(s, s);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = __fmaf_rn(i2f_small((int)r0[j]), s, f[j]);
+          for (int l = 0; l < NLD; ++l) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) f[32 + j] = __fmaf_rn(i2f_small((int)r1[j]), s, f[32 + j]);
+            for (int jj = 0; jj < 32; jj += 2) {
+              const float2 a = fsub2(make_float2(__int_as_float((int)r[l][jj] + (int)ACC_BIAS),
+                                                 __int_as_float((int)r[l][jj + 1] + (int)ACC_BIAS)), big2);
+              const float2 q = ffma2(a, s2, make_float2(f[32 * l + jj], f[32 * l + jj + 1]));
+              f[32 * l + jj] = q.x;
+              f[32 * l + jj + 1] = q.y;
+            }
+          }
         }
         if (!ok) break;
         if (EPI == EPI_GROUP) {
