@@ -150,7 +150,8 @@ int lfm2q_selftest_wait_timeout(int limit_log2, void *stream);
 
 /* Forces the per-token GEMM tile: 128 or 256 = one CTA per 128-row tile of that many columns; -192 or -256 = a CTA
  * pair (cluster of two, tcgen05 cta_group::2) per 256-row tile of that many columns; 0 = automatic. The SiLU GEMM
- * follows the sign (one CTA or a pair, 128 output columns per tile). Tuning and testing only. */
+ * follows the sign (one CTA or a pair, 128 output columns per tile); 64 = one CTA per 128 x 64 tile (W8A16 only, its
+ * small-M choice; the int8 GEMMs treat it as automatic). Tuning and testing only. */
 void lfm2q_set_gemm_tile(int bn);
 
 #ifdef __cplusplus

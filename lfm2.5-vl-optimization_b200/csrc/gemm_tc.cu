@@ -67,7 +67,6 @@ struct GemmArgs {
   int Nout;           // output columns
   int tiles_m, tiles_n;
   int m_fast;         // tile raster: 1 = consecutive tiles walk M (A stays in L2), 0 = walk N
-  const int8_t *Wq;   // W8: int8 weights [N, K], staged as bf16 by the converter warps
   int pdl;            // launched as a programmatic dependent: weights may load before the previous grid completes
 };
 
@@ -247,9 +246,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 __device__ __forceinline__ void st_shared16(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-__device__ __forceinline__ uint4 ld_global16(const void *p) {
-  return __ldg(reinterpret_cast<const uint4 *>(p));
-}
 __device__ __forceinline__ uint4 ld_shared16(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
@@ -288,14 +284,17 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int *ab
   return ok;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int W_BYTES_ = 0>
 struct Smem {
   static constexpr int A_BYTES = TM * TK;
   static constexpr int B_BYTES = BN * TK;
   static constexpr int A_OFF = 0;
   static constexpr int B_OFF = STAGES * A_BYTES;
-  static constexpr int BAR_OFF = B_OFF + STAGES * B_BYTES;
-  static constexpr int NBARS = 2 * STAGES + 8;
+  // W8: the stage's int8 weight rows as loaded by TMA (rows of 64 bytes), the converter warps' source
+  static constexpr int W_BYTES = W_BYTES_;
+  static constexpr int W_OFF = B_OFF + STAGES * B_BYTES;
+  static constexpr int BAR_OFF = W_OFF + STAGES * W_BYTES;
+  static constexpr int NBARS = 3 * STAGES + 8;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   // epilogue: per-warp staging of its columns' weight scales and bias (2 x 128 fp32 per warp)
   static constexpr int PAR_OFF = ((MISC_OFF + 16 + 1023) / 1024) * 1024;
@@ -307,6 +306,9 @@ struct Smem {
   static constexpr int ALLOC = BYTES + 1024;  // room to align the base to 1024
   static_assert(ALLOC <= 232448, "shared memory per block");
 };
+// the layout of one instantiation: per CTA, A 128 rows and B BN / CG rows per stage (W8: plus the int8 weight rows)
+template <int BN, int STAGES, int EPI, int CG>
+using SmemOf = Smem<BN / CG, STAGES, EPI == EPI_W8 ? (BN / CG) * 64 : 0>;
 
 // ------------------------------------------------------------------ the kernel
 // CG = 1: one CTA per 128 x BN tile. CG = 2: a cluster of two CTAs (a CTA pair) per 256 x BN tile; CTA r loads A
@@ -317,7 +319,7 @@ template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
 __global__ void __launch_bounds__(cta_threads(EPI), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs args) {
-  using L = Smem<BN / CG, STAGES>;  // per CTA: A 128 rows, B BN / CG rows per stage
+  using L = SmemOf<BN, STAGES, EPI, CG>;
   constexpr bool GROUPED = (EPI == EPI_GROUP || EPI == EPI_GROUP_Q);
   static_assert(NACC * BN <= 512, "accumulators exceed TMEM");
   constexpr int TMEM_COLS = NACC * BN <= 256 ? 256 : 512;  // allocations are powers of two
@@ -342,6 +344,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
   auto bar_empty = [&](int s) { return smem_addr(bars + STAGES + s); };
   auto bar_tfull = [&](int a) { return smem_addr(bars + 2 * STAGES + a); };
   auto bar_tempty = [&](int a) { return smem_addr(bars + 2 * STAGES + 4 + a); };
+  auto bar_wfull = [&](int s) { return smem_addr(bars + 2 * STAGES + 8 + s); };  // W8: the stage's int8 weights
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = args.M, K = args.K;
@@ -360,6 +363,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
       // leader: its producer's arrive (expect_tx for both CTAs' TMA bytes), plus W8: one per converter warp of each CTA
       mbar_init(bar_full(s), W8 ? 1 + 8 * CG : 1);
       mbar_init(bar_empty(s), 1);  // every CTA: one commit from the (leader's) MMA thread
+      mbar_init(bar_wfull(s), 1);  // W8, every CTA: its producer's expect_tx for its own weight rows
     }
     for (int a = 0; a < 4; ++a) {
       mbar_init(bar_tfull(a), 1);
@@ -399,7 +403,10 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
       constexpr uint32_t STAGE_TX = CG * (L::A_BYTES + (W8 ? 0 : L::B_BYTES));  // bytes the leader expects per stage
       auto load_b = [&](int st, int nt, int kb) {
         const uint32_t sb = sbase + L::B_OFF + st * L::B_BYTES;
-        if constexpr (CG == 2) {
+        if constexpr (W8) {  // this CTA's int8 weight rows x 64 K, for its converter warps
+          mbar_expect_tx(bar_wfull(st), L::W_BYTES);
+          tma_load_2d(sbase + L::W_OFF + st * L::W_BYTES, &tmB, bar_wfull(st), kb * KPS, nt * BN + (int)rank * (BN / CG));
+        } else if constexpr (CG == 2) {
           const int brow = (EPI == EPI_SILU) ? (rank ? args.Nout : 0) + nt * (BN / 2) : nt * BN + (int)rank * (BN / 2);
           tma_load_2d_pair(sb, &tmB, lead(bar_full(st)), kb * TK, brow);
         } else if (EPI == EPI_SILU) {
@@ -420,15 +427,13 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
       // so they load before griddepcontrol.wait; the activations (its output) after it.
       int pre = 0;
       if (args.pdl) {
-        if (!W8) {
-          const int my_tiles = unit < tiles ? (tiles - 1 - unit) / units + 1 : 0;
-          pre = my_tiles * KB < STAGES ? my_tiles * KB : STAGES;
-          for (int j = 0; j < pre; ++j) {
-            int mt, nt;
-            tile_coord(unit + (j / KB) * units, args, mt, nt);
-            if (rank == 0) mbar_expect_tx(bar_full(j), STAGE_TX);
-            load_b(j, nt, j % KB);
-          }
+        const int my_tiles = unit < tiles ? (tiles - 1 - unit) / units + 1 : 0;
+        pre = my_tiles * KB < STAGES ? my_tiles * KB : STAGES;
+        for (int j = 0; j < pre; ++j) {
+          int mt, nt;
+          tile_coord(unit + (j / KB) * units, args, mt, nt);
+          if (rank == 0) mbar_expect_tx(bar_full(j), STAGE_TX);
+          load_b(j, nt, j % KB);
         }
         pdl_wait();
       }
@@ -443,7 +448,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
             if (!mbar_wait(bar_empty(stage), phase ^ 1, abort_flag)) goto producer_done;
             if (rank == 0) mbar_expect_tx(bar_full(stage), STAGE_TX);
             load_a(stage, mt, kb);
-            if (!W8) load_b(stage, nt, kb);
+            load_b(stage, nt, kb);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -860,12 +865,12 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
     }
   } else if constexpr (W8) {
     // ---------------------------------------------------------------- W8 weight converters, warps 6..13
-    // Each stage, this CTA's BN / CG weight rows x 64 K of int8 become bf16 in the B stage: converter warp cw owns the
-    // 8-row groups cw, cw + 8, ...; in a group, 4 lanes share a row (16 contiguous weights each: coalesced 64-byte
-    // row segments), convert exactly (exponent-bias trick) and write the two 16-byte units of their 32 bf16 bytes
-    // at the 128-byte-swizzled positions the MMA descriptor expects (unit u of row r at u ^ (r & 7)). The loads run
-    // two stages ahead (ping-pong registers); rows >= N and K >= K read as zero. Then: proxy fence (the tensor core
-    // reads through the async proxy), and one arrival per warp on the pair leader's full barrier.
+    // Each stage, this CTA's BN / CG weight rows x 64 K of int8 (brought into shared memory by the producer's TMA,
+    // STAGES stages ahead, zero-filled past N and K) become bf16 in the B stage: converter warp cw owns the 8-row
+    // groups cw, cw + 8, ...; in a group, 4 lanes share a row (16 contiguous weights each, one conflict-free 16-byte
+    // shared load), convert exactly (exponent-bias trick) and write the two 16-byte units of their 32 bf16 bytes at
+    // the 128-byte-swizzled positions the MMA descriptor expects (unit u of row r at u ^ (r & 7)). Then: proxy fence
+    // (the tensor core reads through the async proxy), and one arrival per warp on the pair leader's full barrier.
     constexpr int NCW = 8;                  // converter warps
     constexpr int BROWS = BN / CG;          // weight rows this CTA stages per tile
     constexpr int ITER = BROWS / (8 * NCW);  // 8-row groups per converter warp and stage
@@ -874,45 +879,23 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
     const int lr = lane >> 2, lc = lane & 3;
     const int my_tiles = unit < tiles ? (tiles - 1 - unit) / units + 1 : 0;
     const int total = my_tiles * KB;  // stages this CTA runs
-    // next stage to load: walked in order, tile coordinates recomputed once per tile
-    int ld_j = 0, ld_kb = 0, ld_tile = unit, ld_nt = 0;
-    if (ld_tile < tiles) {
-      int mt0;
-      tile_coord(ld_tile, args, mt0, ld_nt);
-    }
-    auto load_next = [&](uint4 (&buf)[ITER]) {
-      if (ld_j >= total) return;
-      const int k = ld_kb * KPS + lc * 16;
-      const int nbase = ld_nt * BN + (int)rank * BROWS + cw * 8 + lr;
-#pragma unroll
-      for (int it = 0; it < ITER; ++it) {
-        const int n = nbase + it * 8 * NCW;
-        buf[it] = (n < args.N && k < K) ? ld_global16(args.Wq + (size_t)n * K + k) : make_uint4(0u, 0u, 0u, 0u);
-      }
-      ++ld_j;
-      if (++ld_kb == KB) {
-        ld_kb = 0;
-        ld_tile += units;
-        if (ld_tile < tiles) {
-          int mt0;
-          tile_coord(ld_tile, args, mt0, ld_nt);
-        }
-      }
-    };
-    int c_stage = 0;
-    uint32_t c_phase = 0;
-    auto consume = [&](const uint4 (&buf)[ITER]) -> bool {
-      const int stage = c_stage;
-      if (!warp_wait(bar_empty(stage), c_phase ^ 1, abort_flag)) return false;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int j = 0; j < total; ++j) {
+      if (!warp_wait(bar_empty(stage), phase ^ 1, abort_flag)) break;  // the MMA has read this B stage
+      if (!warp_wait(bar_wfull(stage), phase, abort_flag)) break;      // the stage's int8 rows have landed
+      mbar_try_wait<false>(bar_wfull(stage), phase);  // every lane observes the completed phase (acquire)
+      const uint32_t sw8 = sbase + L::W_OFF + stage * L::W_BYTES;
       const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
 #pragma unroll
       for (int it = 0; it < ITER; ++it) {
         const int rr = (it * NCW + cw) * 8 + lr;
+        const uint4 v = ld_shared16(sw8 + rr * 64 + lc * 16);
         uint32_t o[8];
-        i8x4_to_bf16x2x2(buf[it].x, o[0], o[1]);
-        i8x4_to_bf16x2x2(buf[it].y, o[2], o[3]);
-        i8x4_to_bf16x2x2(buf[it].z, o[4], o[5]);
-        i8x4_to_bf16x2x2(buf[it].w, o[6], o[7]);
+        i8x4_to_bf16x2x2(v.x, o[0], o[1]);
+        i8x4_to_bf16x2x2(v.y, o[2], o[3]);
+        i8x4_to_bf16x2x2(v.z, o[4], o[5]);
+        i8x4_to_bf16x2x2(v.w, o[6], o[7]);
         const uint32_t rowa = sb + rr * 128;
         st_shared16(rowa + (((2 * lc) ^ (rr & 7)) << 4), o[0], o[1], o[2], o[3]);
         st_shared16(rowa + (((2 * lc + 1) ^ (rr & 7)) << 4), o[4], o[5], o[6], o[7]);
@@ -925,21 +908,10 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
         else
           mbar_arrive(bar_full(stage));
       }
-      if (++c_stage == STAGES) {
-        c_stage = 0;
-        c_phase ^= 1;
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
       }
-      return true;
-    };
-    uint4 ping[ITER], pong[ITER];
-    load_next(ping);
-    load_next(pong);
-    for (int j = 0; j < total; j += 2) {
-      if (!consume(ping)) break;
-      load_next(ping);
-      if (j + 1 >= total) break;
-      if (!consume(pong)) break;
-      load_next(pong);
     }
   }
 
@@ -1002,12 +974,26 @@ bool make_map_bf16(CUtensorMap *map, const void *ptr, int inner, int rows, int b
   return r == CUDA_SUCCESS;
 }
 
+// 2-D int8 matrix [rows, inner] row-major, box = 64 bytes x box_rows, unswizzled (rows 64 bytes apart), OOB reads zero
+bool make_map_w8(CUtensorMap *map, const void *ptr, int inner, int rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 std::atomic<int> g_tile_override{0};
 std::atomic<bool> g_gemm_pdl{true};  // GEMMs launch as programmatic dependents (lfm2q_set_pdl)
 
 template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
 cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) {
-  using L = Smem<BN / CG, STAGES>;
+  using L = SmemOf<BN, STAGES, EPI, CG>;
   auto kern = gemm_tc_kernel<BN, STAGES, NACC, EPI, GELU, CG>;
   static std::once_flag once[64];
   static int max_units[64];  // co-resident work units (CTAs, or CTA pairs) per device
@@ -1043,9 +1029,8 @@ cudaError_t run_tc(const void *A, const int8_t *B, GemmArgs a, cudaStream_t st) 
   });
   if (attr_err != cudaSuccess) return attr_err;
   CUtensorMap ta, tb;
-  if (EPI == EPI_W8) {  // bf16 activations by TMA; the int8 weights are read by the converter warps (a.Wq)
-    memset(&tb, 0, sizeof(tb));
-    if (!make_map_bf16(&ta, A, a.K, a.M, TM)) return cudaErrorInvalidValue;
+  if (EPI == EPI_W8) {  // bf16 activations; the int8 weights in 64-byte rows for the converter warps
+    if (!make_map_bf16(&ta, A, a.K, a.M, TM) || !make_map_w8(&tb, B, a.K, a.N, BN / CG)) return cudaErrorInvalidValue;
   } else {
     const int box_b = (EPI == EPI_SILU) ? BN / 2 : BN / CG;
     if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, box_b)) return cudaErrorInvalidValue;
@@ -1114,7 +1099,7 @@ int gemm_device_error(bool clear) {
 void gemm_set_pdl(bool on) { g_gemm_pdl.store(on); }
 
 void gemm_set_tile_override(int bn) {
-  g_tile_override = (bn == 128 || bn == 256 || bn == -192 || bn == -256) ? bn : 0;
+  g_tile_override = (bn == 64 || bn == 128 || bn == 256 || bn == -192 || bn == -256) ? bn : 0;
 }
 
 cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias, void *Y,
@@ -1125,7 +1110,7 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
     a.Y = (bf16 *)Y;
     return gelu ? run_tc<128, 6, 4, EPI_GROUP, true, 1>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false, 1>(A, B, a, st);
   }
-  const int ov = g_tile_override.load();
+  const int ov = g_tile_override.load() == 64 ? 0 : g_tile_override.load();  // 64: a W8A16-only choice
   if (M <= 16 && K % 64 == 0 && !ov) {
     // skinny: the A8 GEMV streams W once with int8 MMAs (same exact int32 sums and the same epilogue)
     return launch_gemv_a8(B, sb, A, sa, bias, Y, N, K, M, gelu, false, st);
@@ -1183,8 +1168,9 @@ cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *
 namespace lfm2q {
 // W8A16: y = bf16(act(((bf16 x) . (int8 W -> bf16)^T) * sw + b)), fp32 accumulation in TMEM (tcgen05 kind::f16).
 // Reference: gemm_w8_kernel / launch_gemm_w8 (kernels/int8_gemm.cu:306-388, :765-780), op gemm_w8
-// (kernels/int8_gemm.cpp:72-79). CTA pairs on 256 x 256 tiles when one-CTA 128 x 256 tiles fill the GPU, else one
-// CTA per 128 x 128 tile; a forced tile width (lfm2q_set_gemm_tile) picks the same way by sign.
+// (kernels/int8_gemm.cpp:72-79). CTA pairs on 256 x 256 tiles when one-CTA 128 x 256 tiles fill the GPU, one CTA per
+// 128 x 128 tile while those fill it, else one CTA per 128 x 64 tile; a forced tile width (lfm2q_set_gemm_tile) picks
+// the same way by sign (64: the narrow tile).
 cudaError_t launch_gemm_w8(const void *x, const int8_t *w, const float *sw, const void *bias, void *y, int M, int N,
                            int K, bool gelu, cudaStream_t st) {
   if (M <= 0 || N <= 0) return cudaSuccess;
@@ -1193,13 +1179,19 @@ cudaError_t launch_gemm_w8(const void *x, const int8_t *w, const float *sw, cons
     // a few tokens, no bias / activation: y = bf16(acc * sw) is the weight-only decode GEMV, which streams W once
     return launch_gemv(w, true, sw, x, y, N, K, 0, M, false, st);
   }
-  const long tiles256 = (long)((M + TM - 1) / TM) * ((N + 255) / 256);
-  const bool pair = ov < 0 || (ov == 0 && tiles256 >= device_sm_count());
-  GemmArgs a = base_args(nullptr, sw, bias, M, N, K, N, pair ? 256 : 128, pair ? 2 * TM : TM);
+  const int sms = device_sm_count();
+  const long tiles_m = (M + TM - 1) / TM;
+  const bool pair = ov < 0 || (ov == 0 && tiles_m * ((N + 255) / 256) >= sms);
+  // Few 128-column tiles (decode batches, small M): 64-column tiles put twice as many SMs on the weight stream; each
+  // CTA's MMA and conversion work per stage halves, which is what bounds a one-tile-per-CTA launch.
+  const bool narrow = ov == 64 || (ov == 0 && !pair && tiles_m * ((N + 127) / 128) < sms);
+  const int bn = pair ? 256 : (narrow ? 64 : 128);
+  GemmArgs a = base_args(nullptr, sw, bias, M, N, K, N, bn, pair ? 2 * TM : TM);
   a.Y = (bf16 *)y;
-  a.Wq = w;
   if (pair)
-    return gelu ? run_tc<256, 6, 2, EPI_W8, true, 2>(x, w, a, st) : run_tc<256, 6, 2, EPI_W8, false, 2>(x, w, a, st);
-  return gelu ? run_tc<128, 6, 2, EPI_W8, true, 1>(x, w, a, st) : run_tc<128, 6, 2, EPI_W8, false, 1>(x, w, a, st);
+    return gelu ? run_tc<256, 5, 2, EPI_W8, true, 2>(x, w, a, st) : run_tc<256, 5, 2, EPI_W8, false, 2>(x, w, a, st);
+  if (narrow)
+    return gelu ? run_tc<64, 7, 4, EPI_W8, true, 1>(x, w, a, st) : run_tc<64, 7, 4, EPI_W8, false, 1>(x, w, a, st);
+  return gelu ? run_tc<128, 5, 2, EPI_W8, true, 1>(x, w, a, st) : run_tc<128, 5, 2, EPI_W8, false, 1>(x, w, a, st);
 }
 }  // namespace lfm2q

@@ -194,7 +194,7 @@ W8_CASES = [(9216, 4304, 1152, True, False), (2327, 8192, 2048, False, False), (
             (4096, 2048, 8192, False, False), (300, 1152, 264, True, False), (517, 16, 40, True, True)]
 
 
-@pytest.fixture(params=[0, 128, -256], ids=["auto", "one_cta", "pair"])
+@pytest.fixture(params=[0, 128, 64, -256], ids=["auto", "one_cta", "narrow", "pair"])
 def w8_tile(request):
     _capi.lib().lfm2q_set_gemm_tile(request.param)
     yield request.param
