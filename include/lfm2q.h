@@ -104,10 +104,11 @@ int lfm2q_gemv(const void *W, int w_is_int8, const float *scale, const uint16_t 
 
 /* A8 decode GEMV, bit-exact at int32: the W8A8 path of gemm_i8 for few tokens (no single counterpart in the
  * reference, whose decode GEMV is weight-only; the result equals gemm_i8 (kernels/int8_gemm.cpp:39-50) on the same
- * int8 inputs, and lfm2q_gemm_i8 itself routes M <= 16 per-token calls here).
+ * int8 inputs, and lfm2q_gemm_i8 itself routes per-token calls here at M <= 16, at M <= 64 when K >= 4096, and at
+ * M <= 32 when N * K <= 8 M).
  * y bf16 [B, N] = bf16(act(((float)(xq . W^T)[b, n] * sx[b]) * sw[n] + bias[n])), xq int8 [B, K] quantized per token
  * (lfm2q_quant_rows), sx fp32 [B], W int8 [N, K], sw fp32 [N], bias bf16 [N] or NULL, act = GELU(tanh) if gelu.
- * Needs K % 64 == 0, B >= 1 (any B: chunks of 16 tokens per launch). */
+ * Needs K % 64 == 0, B >= 1 (any B: up to 64 tokens per pass over W). */
 int lfm2q_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const uint16_t *bias,
                   uint16_t *y, int N, int K, int B, int gelu, void *stream);
 

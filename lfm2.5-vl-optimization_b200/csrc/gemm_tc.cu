@@ -989,6 +989,17 @@ bool make_map_w8(CUtensorMap *map, const void *ptr, int inner, int rows, int box
 }
 
 std::atomic<int> g_tile_override{0};
+// Per-token GEMMs with few rows: the A8 GEMV (one pass over W, int8 mma.sync, tokens on the MMA's N side) against
+// one 128-row tcgen05 tile per CTA, whose time is set by its pipeline depth per K stage (~7.9 us at K = 2048,
+// ~21 us at K = 8192 for M = 16..128, measured). The GEMV wins at M <= 16 always, and up to 64 rows when K is long
+// (K = 8192: 9-14 us) or, up to 32 rows, when the weights are small (<= 8 M) — its 32- and 64-token variants hold
+// more registers and fewer blocks per SM, so at K = 2048 with large N the tiles are faster.
+bool a8_rows(int M, int N, int K) {
+  if (K % 64 != 0) return false;
+  if (M <= 16) return true;
+  if (M <= 32) return K >= 4096 || (long)N * K <= 8L * 1024 * 1024;
+  return M <= A8_MAX_TOKENS && K >= 4096;
+}
 std::atomic<bool> g_gemm_pdl{true};  // GEMMs launch as programmatic dependents (lfm2q_set_pdl)
 
 template <int BN, int STAGES, int NACC, int EPI, bool GELU, int CG>
@@ -1111,7 +1122,7 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
     return gelu ? run_tc<128, 6, 4, EPI_GROUP, true, 1>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false, 1>(A, B, a, st);
   }
   const int ov = g_tile_override.load() == 64 ? 0 : g_tile_override.load();  // 64: a W8A16-only choice
-  if (M <= 16 && K % 64 == 0 && !ov) {
+  if (!ov && a8_rows(M, N, K)) {
     // skinny: the A8 GEMV streams W once with int8 MMAs (same exact int32 sums and the same epilogue)
     return launch_gemv_a8(B, sb, A, sa, bias, Y, N, K, M, gelu, false, st);
   }

@@ -838,7 +838,8 @@ cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const
                        const bf16 *bias, bf16 *y, int N, int K, int B, int ks, bool pdl, cudaStream_t st) {
   const int groups = (N + 15) / 16, rg = 8 / ks;
   const int sets = (groups + rg - 1) / rg;
-  const int resident = 4 * device_sm_count();
+  // resident blocks per SM: 4 (48 KB of weight rings each); 32 and 64 tokens: 2 and 1 (registers: 128 / ~170 per thread)
+  const int resident = (NT >= 8 ? 1 : (NT >= 4 ? 2 : 4)) * device_sm_count();
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
   const size_t extra = FUSEQ ? (size_t)B * (K + 64) : 0;
@@ -917,14 +918,21 @@ cudaError_t launch_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, c
                            int N, int K, int B, bool gelu, bool pdl, cudaStream_t st) {
   if (N <= 0 || B <= 0) return cudaSuccess;
   const int ks = pick_ks(N, K, 64, 0);
-  for (int b0 = 0; b0 < B; b0 += 16) {
-    const int bs = min(16, B - b0);
+  // up to 64 tokens per pass over W (8 token groups of 8 per MMA row block); more tokens take more passes
+  for (int b0 = 0; b0 < B; b0 += A8_MAX_TOKENS) {
+    const int bs = min(A8_MAX_TOKENS, B - b0);
     const int8_t *xb = xq + (size_t)b0 * K;
     const float *sb = sx + b0;
     bf16 *yb = (bf16 *)y + (size_t)b0 * N;
     const bf16 *bi = (const bf16 *)bias;
     cudaError_t e;
-    if (bs > 8)
+    if (bs > 32)
+      e = gelu ? gemv_a8_ks<8, true, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<8, false, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st);
+    else if (bs > 16)
+      e = gelu ? gemv_a8_ks<4, true, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st)
+               : gemv_a8_ks<4, false, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st);
+    else if (bs > 8)
       e = gelu ? gemv_a8_ks<2, true, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st)
                : gemv_a8_ks<2, false, false>(W, sw, xb, sb, nullptr, bi, yb, N, K, bs, ks, pdl, st);
     else

@@ -24,14 +24,17 @@ cudaError_t launch_silu_mul_q(const void *g, int8_t *q, float *s, int rows, int 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st);
 int gemv_device_error(bool clear);
+// tuning: let dependents launch at kernel start (default: after the K loop)
 void gemv_set_early_trigger(bool early);
 void gemv_set_impl(int impl);
 // per-token W8A8 linear for few tokens in one launch: quant_rows(x) fused into the A8 GEMV
 cudaError_t launch_linear_a8(const void *x, const int8_t *W, const float *sw, const void *bias, void *y, int N, int K,
-                             int B, bool gelu, bool pdl, cudaStream_t st);  // tuning: let dependents launch at kernel start (default: after the K loop)
-// A8 decode GEMV: int8 tokens (per-token scales) x int8 W, exact int32, the per-token W8A8 epilogue (gemm_i8's)
+                             int B, bool gelu, bool pdl, cudaStream_t st);
+// A8 decode GEMV: int8 tokens (per-token scales) x int8 W, exact int32, the per-token W8A8 epilogue (gemm_i8's);
+// up to A8_MAX_TOKENS tokens per pass over W
+constexpr int A8_MAX_TOKENS = 64;
 cudaError_t launch_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const float *sx, const void *bias, void *y,
-                           int N, int K, int B, bool gelu, bool pdl, cudaStream_t st);  // sticky code written by a bounded wait of the bulk-copy GEMV (0 = none)
+                           int N, int K, int B, bool gelu, bool pdl, cudaStream_t st);
 cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,
                             void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st);
 

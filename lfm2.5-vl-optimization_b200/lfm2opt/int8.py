@@ -5,8 +5,8 @@ act_group :27-36, a16_kinds :22-24): same names, arguments, environment variable
 
   a8  (W8A8):  activations quantized on the fly (quantize_rows) with one scale per token (LFM2_INT8_GROUP=0) or per
                token and group of 64 input channels (LFM2_INT8_GROUP=64, the default), int8 x int8 tcgen05 GEMM with
-               the scales, bias and GELU in the epilogue (per-token calls of <= 16 tokens run the A8 GEMV inside
-               gemm_i8: same exact int32 sums, same epilogue).
+               the scales, bias and GELU in the epilogue (per-token calls of <= 16 tokens, and of up to 64 with
+               long K, run the A8 GEMV inside gemm_i8: same exact int32 sums, same epilogue).
   a16 (W8A16): bf16 activations, int8 weights (LFM2_INT8_A16 lists the layer kinds).
 
 Additions over the reference (all optional, defaults keep the reference's behaviour):

@@ -58,7 +58,8 @@ TOKEN_CASES = [(9216, 1152, 3456, True, False), (9216, 1152, 4304, True, True), 
                (272, 2048, 3072, False, False), (17, 2048, 2048, False, False), (1, 1152, 1152, True, False),
                (300, 1152, 1152, True, True), (16, 2048, 8192, False, False), (130, 4304, 1152, False, False),
                (129, 144, 264, True, False), (5, 16, 8, False, False), (4096, 8192, 2048, False, False),
-               (383, 1152, 200, True, True), (640, 2048, 1152, True, False)]
+               (383, 1152, 200, True, True), (640, 2048, 1152, True, False), (48, 2048, 6144, True, True),
+               (64, 8192, 2048, False, False), (24, 2048, 3072, False, False), (65, 2048, 2048, True, False)]
 
 
 @pytest.mark.parametrize("M,K,N,bias,gelu", TOKEN_CASES)
