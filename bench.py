@@ -589,7 +589,8 @@ def run_case(a):
         one = lambda w_: E.gemm_i8_q(xq, sx, w_, sw, b, yq, ys, False)  # noqa: E731
     else:
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-        one = lambda w_: E.gemm_i8(xq, sx, w_, sw, b, y, epi == "gelu")  # noqa: E731
+        bb = None if epi == "nobias" else b
+        one = lambda w_: E.gemm_i8(xq, sx, w_, sw, bb, y, epi == "gelu")  # noqa: E731
     for i in range(max(3, a.warmup)):
         one(wqs[i % copies])
     st = torch.cuda.Stream(dev)
@@ -677,7 +678,7 @@ def main():
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--case", default=None,
-                    help="M,K,N[,epi] — time one GEMM shape (epi: none|gelu|silu|group|groupq|w8|w8gelu); tuning "
+                    help="M,K,N[,epi] — time one GEMM shape (epi: none|nobias|gelu|silu|group|groupq|w8|w8gelu); tuning "
                          "and ncu target")
     ap.add_argument("--tile", type=int, default=0, help="force the per-token GEMM tile width (128 or 256)")
     ap.add_argument("--gemv-case", default=None, help="N,K,B[,rows] — time one decode GEMV shape (tuning, ncu target)")
