@@ -19,9 +19,12 @@
 //   warp 1      allocates TMEM and issues tcgen05.mma.kind::i8 (K = 32 per instruction) from one thread;
 //               tcgen05.commit releases a smem stage when its MMAs retire and hands a finished accumulator over
 //   warps 2-9   epilogue, two warps per TMEM lane quarter (one per half of the tile's columns): tcgen05.ld
-//               (32 lanes x 32 columns per load) -> fp32 math -> a per-warp shared-memory transpose -> coalesced
-//               16-byte global stores; each thread owns one output row, so per-row scales and the QOUT row-group
-//               maxima stay in registers
+//               (32 lanes x 32 columns per load) -> fp32 math -> 32 x 32 bf16 blocks written to a per-warp shared
+//               buffer and stored by TMA (QOUT: int8 rows stored directly); each thread owns one output row, so
+//               per-row scales and the QOUT row-group maxima stay in registers
+//   W8A16       (EPI_W8, tcgen05.mma.kind::f16, 448 threads): the int8 weight rows arrive by TMA into a staging
+//               area and eight converter warps write them as bf16 into the swizzled B stage; four epilogue warps
+//               take all of the tile's columns
 //   TMEM        2 accumulators of BN columns (TOKEN / SILU) or 4 of 128 (GROUP: one per 64-wide K group, so the
 //               int32 partial sums of group g are folded while the MMAs of groups g+1.. run)
 //   CTA pairs   (CG = 2, per-token and SiLU epilogues at large M x N): a cluster of two CTAs computes a 256-row tile
@@ -311,7 +314,7 @@ struct Smem {
   // epilogue: per-warp staging of its columns' weight scales and bias (2 x 128 fp32 per warp)
   static constexpr int PAR_OFF = ((MISC_OFF + 16 + 1023) / 1024) * 1024;
   static constexpr int PAR_FLOATS = 256;
-  // epilogue: per-warp 32 x 32 bf16 output block (64-byte rows), the transpose buffer for coalesced stores
+  // epilogue: per-warp 32 x 32 bf16 output block (64-byte rows, 64-byte TMA swizzle), the source of its TMA store
   static constexpr int OUT_OFF = PAR_OFF + EPI_WARPS * PAR_FLOATS * 4;
   static constexpr int OUT_BLOCK = 32 * 64;
   static constexpr int BYTES = OUT_OFF + EPI_WARPS * OUT_BLOCK;
