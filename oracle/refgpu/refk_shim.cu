@@ -1,0 +1,41 @@
+// TEST INFRASTRUCTURE ONLY (not part of the product library): a C-ABI shim over the reference's own CUDA launchers,
+// compiled together with the reference's kernel sources (kernels/int8_gemm.cu, kernels/lfm2_decode.cu, built for
+// sm_100a from where they lie) into oracle/_ref/librefk.so by oracle/Makefile. The GPU parity tests call the
+// reference kernels through it on the same device buffers as lfm2q's, and time both.
+//
+// The prototypes below restate the reference launchers' signatures (kernels/int8_gemm.cu:741-742, :765-766, :822,
+// kernels/lfm2_decode.cu:708); they must match for the link to resolve.
+#include <cuda_runtime.h>
+
+void launch_gemm_i8(const void *A, const float *sa, const void *B, const float *sb, const void *bias, void *Y, int M,
+                    int N, int K, bool gelu, bool grouped, cudaStream_t st);
+void launch_gemm_w8(const void *A, const void *B, const float *sb, const void *bias, void *Y, int M, int N, int K,
+                    bool gelu, cudaStream_t st);
+void launch_quant_rows(const void *x, void *q, float *s, int rows, int K, cudaStream_t st);
+void launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows, int B,
+                 cudaStream_t st);
+void set_pdl(bool on);
+
+// Each wrapper launches on `stream` and returns the launch status (cudaError_t as int; 0 = success).
+extern "C" {
+int refk_gemm_i8(const void *xq, const float *sx, const void *w, const float *sw, const void *bias, void *y, int M,
+                 int N, int K, int gelu, int grouped, void *stream) {
+  launch_gemm_i8(xq, sx, w, sw, bias, y, M, N, K, gelu != 0, grouped != 0, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+int refk_gemm_w8(const void *x, const void *w, const float *sw, const void *bias, void *y, int M, int N, int K,
+                 int gelu, void *stream) {
+  launch_gemm_w8(x, w, sw, bias, y, M, N, K, gelu != 0, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+int refk_quant_rows(const void *x, void *q, float *s, int rows, int K, void *stream) {
+  launch_quant_rows(x, q, s, rows, K, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+int refk_gemv(const void *w, int w_is_int8, const float *scale, const void *x, void *y, int N, int K, int B,
+              void *stream) {
+  launch_gemv(w, w_is_int8 != 0, scale, x, y, N, K, 0, B, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+void refk_set_pdl(int on) { set_pdl(on != 0); }
+}
