@@ -179,9 +179,8 @@ def test_gemm_i8_silu(cuda_dev, silu_tile, M, K, I, bias):
     y = torch.empty(M, I, device=cuda_dev, dtype=BF)
     int8_ext().gemm_i8_silu(xq, sx, wq.to(cuda_dev), sw.to(cuda_dev), None if b is None else b.to(cuda_dev), y)
     r = oracle.gemm_i8_silu_ref(xq.cpu(), sx.cpu(), wq, sw, b)
-    assert oracle.bf16_ulps(y.cpu(), r) <= 1
-    frac = (y.cpu() != r).float().mean().item()
-    assert frac < 1e-3, frac
+    ok, detail = oracle.silu_chain_close(y.cpu(), r)
+    assert ok, detail
 
 
 def test_device_error_word_clear(cuda_dev):

@@ -158,8 +158,8 @@ def test_gemv_epi_swiglu(cuda_dev, int8):
     out = torch.empty(1, I, device=cuda_dev, dtype=BF)
     ext().gemv_epi(0, W, s, x, out)
     ref = oracle.gemm.silu_mul_ref(gout.cpu())
-    assert oracle.bf16_ulps(out.cpu(), ref) <= 1
-    assert (out.cpu() != ref).float().mean().item() < 1e-3
+    ok, detail = oracle.silu_chain_close(out.cpu(), ref)
+    assert ok, detail
 
 
 @pytest.mark.parametrize("int8", [True, False])

@@ -61,4 +61,5 @@ def test_int8linear_silu_gate(cuda_dev):
     assert y.shape == (512, 8192)
     xq, sx = oracle.quant_rows_ref(x)
     r = oracle.gemm_i8_silu_ref(xq, sx, lin.q.cpu(), lin.s.cpu())
-    assert oracle.bf16_ulps(y.cpu(), r) <= 1
+    ok, detail = oracle.silu_chain_close(y.cpu(), r)
+    assert ok, detail
