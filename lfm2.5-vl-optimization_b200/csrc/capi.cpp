@@ -203,7 +203,8 @@ int lfm2q_add_layernorm_q(uint16_t *h, const uint16_t *y, const uint16_t *w, con
   REQUIRE(D % 8 == 0 && D <= 16384, "D must be a multiple of 8, <= 16384");
   if (grouped) REQUIRE(D % 64 == 0, "s shape: grouped scales need D % 64 == 0");
   REQUIRE(h && w && b && q && s, "h, w, b, q and s must be non-null");
-  REQUIRE(aligned16(h) && aligned16(y), "h and y must be 16-byte aligned");
+  REQUIRE(aligned16(h) && aligned16(y) && aligned16(w) && aligned16(b) && aligned16(q),
+          "h, y, w, b and q must be 16-byte aligned");
   if (rows == 0) return LFM2Q_OK;
   if (int e = device_gate()) return e;
   return launched(launch_add_layernorm_q(h, y, w, b, q, s, rows, D, eps, grouped != 0, (cudaStream_t)stream),

@@ -11,7 +11,7 @@
 //   EPI_GROUP_Q as EPI_GROUP, then the bf16-rounded row segment of every 64 output columns is requantized:
 //               yq int8 [M, N], ysT[n / 64][m] = max(|.|, 1e-8) / 127
 //   EPI_SILU    weight rows [0, I) = gate, [I, 2I) = up; g, u = bf16 of the per-token epilogue;
-//               y[m, n] = bf16( bf16(silu(g)) * u ),  silu(g) = g / (1 + __expf(-g)),  y is [M, I]
+//               y[m, n] = bf16( bf16(silu(g)) * u ),  silu(g) = g / (1 + __expf(-g)) (IEEE quotient),  y is [M, I]
 //
 // B200 structure (one persistent CTA per SM, 320 threads, warp-specialised):
 //   warp 0      TMA producer: 128 x 128-byte A tile and BN x 128-byte B tile per stage, 128-byte swizzle,
@@ -773,7 +773,9 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
               const float2 u = epi_pair(ru[j], ru[j + 1], sxm, h ? us.z : us.x, h ? us.w : us.y,
                                         h ? ub.z : ub.x, h ? ub.w : ub.y);
               const float g0 = rbf(g.x), g1 = rbf(g.y);
-              const float2 sg = make_float2(rbf(__fdividef(g0, 1.f + __expf(-g0))), rbf(__fdividef(g1, 1.f + __expf(-g1))));
+              // IEEE quotient, as the reference's silu_mul: __fdividef flushes to 0 once the divisor passes 2^126
+              // (g < -87.3), where the reference's value is still a normal float
+              const float2 sg = make_float2(rbf(__fdiv_rn(g0, 1.f + __expf(-g0))), rbf(__fdiv_rn(g1, 1.f + __expf(-g1))));
               const float2 y = fmul2(sg, make_float2(rbf(u.x), rbf(u.y)));
               o[j / 2] = pack_bf16x2(y.x, y.y);
             }

@@ -107,6 +107,18 @@ def silu_chain_close(y: torch.Tensor, r: torch.Tensor, frac: float = 1e-3):
     return u <= 2 and f < frac, f"max {u} ulps, {f:.2e} of the elements differ"
 
 
+def gelu_close(y: torch.Tensor, r: torch.Tensor):
+    """Acceptance check for the GELU epilogue against gemm_i8_ref(..., gelu=True): <= 1 bf16 ulp, except in the fp32
+    cancellation region of 0.5 v (1 + tanh(u)) near tanh = -1 (v < ~ -4.5), where the outputs are below 2e-7 in
+    magnitude and the GPU's and the CPU's tanh may round 1 + tanh differently: there <= 4e-7 absolute.
+    Returns (ok, detail)."""
+    ia, ib = y.view(torch.int16).int(), r.view(torch.int16).int()
+    ia = torch.where(ia < 0, -32768 - ia, ia)
+    ib = torch.where(ib < 0, -32768 - ib, ib)
+    bad = ((ia - ib).abs() > 1) & ((y.float() - r.float()).abs() > 4e-7)
+    return (not bool(bad.any())), f"{int(bad.sum())} outside the GELU bar, max {bf16_ulps(y, r)} ulps"
+
+
 @torch.no_grad()
 def gemm_i8_silu_ref(xq, sx, w13, sw13, bias=None):
     """The fused SiLU-gate GEMM's parity target: gemm_i8 (bf16 out, per token) over [w1 | w3], then silu_mul."""

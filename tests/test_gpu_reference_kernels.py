@@ -33,12 +33,21 @@ def refk(cuda_dev):
     if not LIB.exists():
         pytest.skip("oracle/_ref/librefk.so not built (the reference's source tree was absent at build time)")
     L = ctypes.CDLL(str(LIB))
+    if not hasattr(L, "refk_silu_mul"):
+        pytest.skip("oracle/_ref/librefk.so predates the producer wrappers: rebuild it (oracle/Makefile, target ref)")
     L.refk_gemm_i8.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]
     L.refk_gemm_w8.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _i, _p]
     L.refk_quant_rows.argtypes = [_p, _p, _p, _i, _i, _p]
     L.refk_gemv.argtypes = [_p, _i, _p, _p, _p, _i, _i, _i, _p]
     L.refk_set_pdl.argtypes = [_i]
-    for f in (L.refk_gemm_i8, L.refk_gemm_w8, L.refk_quant_rows, L.refk_gemv):
+    L.refk_gemm_i8_q.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]
+    L.refk_quant_groups.argtypes = [_p, _p, _p, _i, _i, _p]
+    L.refk_add_layernorm_q.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, ctypes.c_float, _i, _p]
+    L.refk_add_rmsnorm_q.argtypes = [_p, _p, _p, _p, _p, _i, _i, ctypes.c_float, _i, _p]
+    L.refk_silu_mul_q.argtypes = [_p, _p, _p, _i, _i, _i, _p]
+    L.refk_silu_mul.argtypes = [_p, _p, _i, _i, _p]
+    for f in (L.refk_gemm_i8, L.refk_gemm_w8, L.refk_quant_rows, L.refk_gemv, L.refk_gemm_i8_q, L.refk_quant_groups,
+              L.refk_add_layernorm_q, L.refk_add_rmsnorm_q, L.refk_silu_mul_q, L.refk_silu_mul):
         f.restype = _i
     L.refk_set_pdl.restype = None
     return L
@@ -131,6 +140,122 @@ def test_gemv_matches_reference(cuda_dev, refk, N, K, B):
     tol = 2e-2 * max(ref.float().abs().max().item(), 1.0)  # the reference's own bound (tests/test_kernels.py:32)
     for out in (y, ry):
         assert (out.cpu().float() - ref.float()).abs().max().item() <= tol
+
+
+# ------------------------------------------------------------------ fused producers and the SiLU gate, bit for bit
+# The reference's own acceptance test for these is torch.equal (tests/test_int8_gemm.py:123-155); here the equality is
+# with the reference's kernels themselves, run on the same GPU on the same inputs.
+
+PRODUCER_ROWS = [(300, 1152), (257, 2048), (1, 1152), (4099, 1152), (64, 768)]
+
+
+@pytest.mark.parametrize("grouped", [0, 1], ids=["per_row", "grouped"])
+@pytest.mark.parametrize("with_y", [True, False], ids=["add", "noadd"])
+@pytest.mark.parametrize("rows,D", PRODUCER_ROWS)
+def test_add_layernorm_q_equals_reference(cuda_dev, refk, grouped, with_y, rows, D):
+    g = torch.Generator().manual_seed(rows + D + grouped)
+    h0 = (torch.randn(rows, D, generator=g) + 0.2).to(BF).to(cuda_dev)
+    y = torch.randn(rows, D, generator=g).to(BF).to(cuda_dev) if with_y else None
+    w = (torch.rand(D, generator=g) + 0.5).to(BF).to(cuda_dev)
+    b = torch.randn(D, generator=g).to(BF).to(cuda_dev)
+    h, rh = h0.clone(), h0.clone()
+    from lfm2opt.int8 import qbuf
+    q, s = qbuf(rows, D, 64 if grouped else 0, cuda_dev)
+    rq, rs = torch.full_like(q, 99), torch.full_like(s, -1.0)
+    int8_ext().add_layernorm_q(h, y, w, b, q, s, 1e-6)
+    call(refk.refk_add_layernorm_q(ptr(rh), ptr(y), ptr(w), ptr(b), ptr(rq), ptr(rs), rows, D, 1e-6, grouped,
+                                   stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(h, rh)
+    assert torch.equal(q, rq), f"{(q != rq).sum().item()} codes differ"
+    assert torch.equal(s, rs), f"{(s != rs).sum().item()} scales differ"
+
+
+@pytest.mark.parametrize("grouped", [0, 1], ids=["per_row", "grouped"])
+@pytest.mark.parametrize("with_y", [True, False], ids=["add", "noadd"])
+@pytest.mark.parametrize("rows,H", [(257, 2048), (1, 2048), (1000, 2048), (33, 1024), (5, 8192)])
+def test_add_rmsnorm_q_equals_reference(cuda_dev, refk, grouped, with_y, rows, H):
+    g = torch.Generator().manual_seed(rows + H + grouped + 7)
+    h0 = torch.randn(rows, H, generator=g).to(BF).to(cuda_dev)
+    y = torch.randn(rows, H, generator=g).to(BF).to(cuda_dev) if with_y else None
+    w = (torch.rand(H, generator=g) + 0.5).to(BF).to(cuda_dev)
+    h, rh = h0.clone(), h0.clone()
+    from lfm2opt.int8 import qbuf
+    q, s = qbuf(rows, H, 64 if grouped else 0, cuda_dev)
+    rq, rs = torch.full_like(q, 99), torch.full_like(s, -1.0)
+    int8_ext().add_rmsnorm_q(h, y, w, q, s, 1e-5)
+    call(refk.refk_add_rmsnorm_q(ptr(rh), ptr(y), ptr(w), ptr(rq), ptr(rs), rows, H, 1e-5, grouped, stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(h, rh)
+    assert torch.equal(q, rq), f"{(q != rq).sum().item()} codes differ"
+    assert torch.equal(s, rs), f"{(s != rs).sum().item()} scales differ"
+
+
+@pytest.mark.parametrize("grouped", [0, 1], ids=["per_row", "grouped"])
+@pytest.mark.parametrize("rows,I", [(257, 8192), (1, 8192), (64, 4096)])
+def test_silu_mul_q_equals_reference(cuda_dev, refk, grouped, rows, I):
+    g = torch.Generator().manual_seed(rows + I + grouped + 3)
+    gg = (torch.randn(rows, 2 * I, generator=g) * 2).to(BF).to(cuda_dev)
+    from lfm2opt.int8 import qbuf
+    q, s = qbuf(rows, I, 64 if grouped else 0, cuda_dev)
+    rq, rs = torch.full_like(q, 99), torch.full_like(s, -1.0)
+    int8_ext().silu_mul_q(gg, q, s)
+    call(refk.refk_silu_mul_q(ptr(gg), ptr(rq), ptr(rs), rows, I, grouped, stream()))
+    # the reference's unfused chain: its silu_mul kernel (bf16 out), then the oracle's quantizer
+    a = torch.empty(rows, I, device=cuda_dev, dtype=BF)
+    call(refk.refk_silu_mul(ptr(gg), ptr(a), rows, I, stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(q, rq) and torch.equal(s, rs)
+    uq, us = (oracle.quant_groups_ref if grouped else oracle.quant_rows_ref)(a.cpu())
+    assert torch.equal(q.cpu(), uq) and torch.equal(s.cpu(), us)
+
+
+@pytest.mark.parametrize("M,K,N,bias,gelu", [(300, 1152, 4352, True, True), (1024, 2048, 2048, False, False),
+                                             (77, 4352, 1152, True, False)])
+def test_gemm_i8_q_equals_reference(cuda_dev, refk, M, K, N, bias, gelu):
+    x, wq, sw, b = inputs(M, K, N, bias, M + 2 * K + N, cuda_dev)
+    xq, sxT = quantize_rows(x, 64)
+    q = torch.empty(M, N, device=cuda_dev, dtype=torch.int8)
+    s = torch.empty(N // 64, M, device=cuda_dev)
+    rq, rs = torch.full_like(q, 99), torch.full_like(s, -1.0)
+    int8_ext().gemm_i8_q(xq, sxT, wq, sw, b, q, s, gelu)
+    call(refk.refk_gemm_i8_q(ptr(xq), ptr(sxT), ptr(wq), ptr(sw), ptr(b), ptr(rq), ptr(rs), M, N, K, int(gelu),
+                             stream()))
+    torch.cuda.synchronize()
+    if gelu:  # the two sides evaluate tanh differently: codes within one, scales within 2^-7 relative
+        assert (q.int() - rq.int()).abs().max().item() <= 1
+        assert ((s - rs).abs() <= rs.abs() * 2 ** -7).all()
+    else:
+        assert torch.equal(q, rq) and torch.equal(s, rs)
+
+
+@pytest.mark.parametrize("M,K,I,gate_bias", [(300, 2048, 8192, None), (1024, 1152, 2048, None),
+                                             (256, 2048, 1024, -88.0), (130, 2048, 512, -87.5)])
+def test_silu_gate_equals_reference_composition(cuda_dev, refk, M, K, I, gate_bias):
+    """gemm_i8_silu equals the reference's gemm_i8 (bf16 [M, 2I]) followed by its silu_mul, bit for bit. With a gate
+    bias near -88 the gate values land in [-89, -87], where 1 + exp(-g) passes 2^126: the IEEE quotient the reference
+    takes is still a normal float there (a fast reciprocal-based division would return 0)."""
+    x, wq, sw, _ = inputs(M, K, 2 * I, False, M + K + I, cuda_dev)
+    b = None
+    if gate_bias is not None:
+        b = torch.zeros(2 * I, dtype=BF)
+        b[:I] = gate_bias
+        b[I:] = 1.0
+        b = b.to(cuda_dev)
+        sw = sw * 0.05  # gate = bias + a small product: every gate value lies within one unit of the bias
+    xq, sx = quantize_rows(x)
+    y = torch.empty(M, I, device=cuda_dev, dtype=BF)
+    int8_ext().gemm_i8_silu(xq, sx, wq, sw, b, y)
+    gu = torch.empty(M, 2 * I, device=cuda_dev, dtype=BF)
+    call(refk.refk_gemm_i8(ptr(xq), ptr(sx), ptr(wq), ptr(sw), ptr(b), ptr(gu), M, 2 * I, K, 0, 0, stream()))
+    ry = torch.empty_like(y)
+    call(refk.refk_silu_mul(ptr(gu), ptr(ry), M, I, stream()))
+    torch.cuda.synchronize()
+    if gate_bias is not None:
+        gate = gu[:, :I].float()
+        assert gate.min().item() >= -89.0 and gate.max().item() <= -87.0
+        assert (ry != 0).float().mean().item() > 0.5  # the reference's values there are not flushed to zero
+    assert torch.equal(y, ry), f"{(y != ry).sum().item()} of {y.numel()} outputs differ"
 
 
 def _time(fn, reps=10):

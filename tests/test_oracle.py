@@ -84,3 +84,65 @@ def test_quant_edge_cases():
     assert q[0].abs().max().item() == 0
     assert q[1, :3].tolist() == [127, 0, 2]
     assert (q[2] == -127).all()
+
+
+def _f32(v):
+    return np.float32(v)
+
+
+def _butterfly_scalar(lanes):
+    v = [_f32(x) for x in lanes]
+    for o in (16, 8, 4, 2, 1):
+        v = [_f32(v[l] + v[l ^ o]) for l in range(32)]
+    assert all(x == v[0] for x in v)  # every lane ends with the same total
+    return v[0]
+
+
+def _fmaf(a, b, c):
+    from oracle import _c
+    return _c.fmaf(np.array([a], np.float32), np.array([b], np.float32), np.array([c], np.float32))[0]
+
+
+def test_layernorm_order_matches_lane_loop():
+    """The vectorised layernorm statistics equal a literal per-lane loop over the reference's warp layout
+    (kernels/int8_gemm.cu:541-570): chunk c*32+l belongs to lane l, ((v0+v1)+v2)+v3 per chunk, xor butterfly."""
+    from oracle.producers import layernorm_stats
+
+    g = torch.Generator().manual_seed(11)
+    for D in (1152, 200, 2048):
+        X = (torch.randn(3, D, generator=g) * 3 + 0.5).to(torch.bfloat16).float().numpy()
+        mean, rstd = layernorm_stats(X, 1e-6)
+        for r in range(3):
+            x = X[r]
+            lanes = [_f32(0)] * 32
+            for ci in range(D // 4):
+                v = x[4 * ci:4 * ci + 4]
+                lanes[ci % 32] = _f32(lanes[ci % 32] + _f32(_f32(_f32(v[0] + v[1]) + v[2]) + v[3]))
+            m = _f32(_butterfly_scalar(lanes) / _f32(D))
+            assert m == mean[r], (D, r)
+            lanes = [_f32(0)] * 32
+            for ci in range(D // 4):
+                for j in range(4):
+                    d = _f32(x[4 * ci + j] - m)
+                    lanes[ci % 32] = _fmaf(d, d, lanes[ci % 32])
+            var = _f32(_butterfly_scalar(lanes) / _f32(D))
+            assert _f32(1.0 / np.sqrt(np.float64(_f32(var + _f32(1e-6))))) == rstd[r], (D, r)
+
+
+def test_rmsnorm_order_matches_thread_loop():
+    """The vectorised RMSNorm statistic equals a literal loop over the reference's block layout
+    (kernels/int8_gemm.cu:600-614 with block_sum, kernels/lfm2_decode.cu:79-90)."""
+    from oracle.producers import rmsnorm_rs
+
+    g = torch.Generator().manual_seed(12)
+    for H in (2048, 1024, 320):
+        X = (torch.randn(2, H, generator=g) * 2).to(torch.bfloat16).float().numpy()
+        rs = rmsnorm_rs(X, 1e-5)
+        for r in range(2):
+            part = [_f32(0)] * 256
+            for i in range(H):
+                part[i % 256] = _fmaf(X[r, i], X[r, i], part[i % 256])
+            warps = [_butterfly_scalar(part[32 * w:32 * w + 32]) for w in range(8)]
+            ss = _butterfly_scalar(warps + [_f32(0)] * 24)
+            v = _f32(_f32(ss / _f32(H)) + _f32(1e-5))
+            assert _f32(1.0 / np.sqrt(np.float64(v))) == rs[r], (H, r)
