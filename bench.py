@@ -102,6 +102,7 @@ class ClockSampler:
         self.rows = []
         self.proc = None
         self.thread = None
+        self.i0, self.i1 = 0, None
 
     def start(self):
         try:
@@ -114,6 +115,21 @@ class ClockSampler:
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        t0 = time.time()
+        while not self.rows and time.time() - t0 < 10:  # nvidia-smi is up before the timed region starts
+            time.sleep(0.05)
+
+    def mark_start(self):
+        self.i0 = len(self.rows)
+
+    def mark_end(self):
+        # keep the sample that follows the timed region too: a short region (many GPUs, few steps) may hold fewer
+        # than one 200 ms interval
+        t0 = time.time()
+        n = len(self.rows)
+        while len(self.rows) == n and time.time() - t0 < 0.5:
+            time.sleep(0.02)
+        self.i1 = len(self.rows)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -130,7 +146,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.thread.join(timeout=5)
-        rows = [r for r in self.rows if r[0].isdigit()]
+        rows = [r for r in self.rows[self.i0:self.i1] if r[0].isdigit()]
         sm = [float(r[1]) for r in rows if r[1].replace(".", "", 1).isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "", 1).isdigit()]
         pw = [float(r[3]) for r in rows if r[3].replace(".", "", 1).isdigit()]
@@ -232,7 +248,10 @@ class Job:
         self.q = {}
         self.y = {}
         self.stream = torch.cuda.current_stream(dev).cuda_stream
-        self.calls = []  # (is_gemm, ops, fn, args)
+        self.calls = []  # (kind "quant" | "gemm", ops, fn, args, tag)
+        # tag -> (x, wq, sw, bias, N, epi, y) of the last launch that writes y: after a step, y holds that launch's
+        # result on inputs that stay resident, which the verification leg recomputes on the CPU
+        self.last_of = {}
         self._plan()
 
     def _buf(self, key, shape, dtype):
@@ -248,17 +267,20 @@ class Job:
         out_n = N // 2 if epi == "silu" else N
         y = self._buf(("y", tag, rows, out_n), (rows, out_n), torch.bfloat16)
         st = self.stream
-        self.calls.append((False, 0, self.L.lfm2q_quant_rows, (x.data_ptr(), xq.data_ptr(), sx.data_ptr(), rows, K, st)))
+        shape = tag[:4] if tag.startswith("head") else tag
+        self.calls.append(("quant", 0, self.L.lfm2q_quant_rows, (x.data_ptr(), xq.data_ptr(), sx.data_ptr(), rows, K, st),
+                           shape))
         ops = 2 * rows * N * K
         bp = bias.data_ptr() if bias is not None else None
         if epi == "silu":
-            self.calls.append((True, ops, self.L.lfm2q_gemm_i8_silu,
+            self.calls.append(("gemm", ops, self.L.lfm2q_gemm_i8_silu,
                                (xq.data_ptr(), sx.data_ptr(), wq.data_ptr(), sw.data_ptr(), bp, y.data_ptr(), rows,
-                                N // 2, K, st)))
+                                N // 2, K, st), shape))
         else:
-            self.calls.append((True, ops, self.L.lfm2q_gemm_i8,
+            self.calls.append(("gemm", ops, self.L.lfm2q_gemm_i8,
                                (xq.data_ptr(), sx.data_ptr(), 0, wq.data_ptr(), sw.data_ptr(), bp, y.data_ptr(), rows,
-                                N, K, int(epi == "gelu"), st)))
+                                N, K, int(epi == "gelu"), st), shape))
+        self.last_of[tag] = (x, wq, sw, bias, N, epi, y)
         return y
 
     def _plan(self):
@@ -281,25 +303,28 @@ class Job:
             y = self._linear(self.xh[s0:s0 + cnt], self.hq, self.hsc, None, self.hq.shape[0], "none", f"head{c}")
             self.head_local.append((len(self.calls), s0, cnt, y))
 
-    def run(self, gemm_events=None):
-        """Enqueue one step. gemm_events: list to receive (start, end, ops) CUDA events around every GEMM launch."""
+    def run(self, rec=None):
+        """Enqueue one step. rec: a StepRecorder that receives CUDA events around every launch and at the step's end."""
         launches = 0
         works = []
         head_at = {idx: (s0, cnt, y) for idx, s0, cnt, y in self.head_local}
         off = 0
         slab = self.hq.shape[0]
-        for i, (is_gemm, ops, fn, args) in enumerate(self.calls):
-            if is_gemm and gemm_events is not None:
+        last_gemm_end = None
+        for i, (kind, ops, fn, args, tag) in enumerate(self.calls):
+            if rec is not None:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e0.record()
             st = fn(*args)
             if st != 0:
                 raise RuntimeError(self.L.lfm2q_last_error().decode())
             launches += 1
-            if is_gemm and gemm_events is not None:
+            if rec is not None:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()
-                gemm_events.append((e0, e1, ops))
+                rec.items.append((kind, tag, ops, e0, e1))
+                if kind == "gemm":
+                    last_gemm_end = e1
             if (i + 1) in head_at and self.world > 1:
                 s0, cnt, y = head_at[i + 1]
                 dst = self.logits[off:off + self.world * cnt * slab].view(self.world * cnt, slab)
@@ -307,21 +332,74 @@ class Job:
                 works.append(dist.all_gather_into_tensor(dst, y, async_op=True))
         for w in works:
             w.wait()
+        if rec is not None:
+            e_end = torch.cuda.Event(enable_timing=True)
+            e_end.record()  # after the current stream has waited for the last all-gather
+            rec.tails.append((last_gemm_end, e_end))
         return launches
 
+    def gathered_rows(self, rows):
+        """Logits [len(rows), V] of the given head rows from the step's output (N > 1: the chunk-major all-gather
+        buffer; N = 1: the head chunks' outputs)."""
+        from lfm2opt.parallel import shard_rows
+        slab = self.hq.shape[0]
+        out = []
+        for m in rows:
+            off = 0
+            for c in range(self.head_chunks):
+                s0, cnt = shard_rows(HEAD_M, self.head_chunks, c)
+                if s0 <= m < s0 + cnt:
+                    if self.world == 1:
+                        out.append(self.head_local[c][3][m - s0])
+                    else:
+                        blk = self.logits[off:off + self.world * cnt * slab].view(self.world, cnt, slab)
+                        out.append(blk[:, m - s0, :].reshape(-1))
+                    break
+                off += self.world * cnt * slab
+        return torch.stack(out)
 
-def time_steps(fn, steps, warmup, world):
+
+class StepRecorder:
+    """CUDA events of the timed steps: (kind, shape tag, ops, start, end) per launch, and per step (end of its last
+    GEMM, end of the step after the all-gathers)."""
+
+    def __init__(self):
+        self.items = []
+        self.tails = []
+
+    def summary(self, steps):
+        per_kind, per_shape = {}, {}
+        for kind, tag, ops, e0, e1 in self.items:
+            ms = e0.elapsed_time(e1)
+            per_kind[kind] = per_kind.get(kind, 0.0) + ms
+            if kind == "gemm":
+                d = per_shape.setdefault(tag, [0, 0.0, 0])
+                d[0] += ops
+                d[1] += ms
+                d[2] += 1
+        exposed = sum(a.elapsed_time(b) for a, b in self.tails if a is not None)
+        shapes = {t: {"tops": round(o / (ms * 1e-3) / 1e12, 1), "us_per_launch": round(ms * 1e3 / n, 1),
+                      "launches_per_step": n // steps} for t, (o, ms, n) in per_shape.items()}
+        return ({"gemm": per_kind.get("gemm", 0.0) / steps, "quant": per_kind.get("quant", 0.0) / steps,
+                 "gather_exposed": exposed / steps}, shapes)
+
+
+def time_steps(fn, steps, warmup, world, on_start=None, on_end=None):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
+    if on_start:
+        on_start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
         fn()
     e1.record()
     torch.cuda.synchronize()
+    if on_end:
+        on_end()
     barrier(world)
     torch.cuda.synchronize()
     return max_over_ranks(e0.elapsed_time(e1), world)
@@ -407,6 +485,76 @@ class E2E:
         cur.wait_stream(self.cs)
 
 
+# ----------------------------------------------------------------------------------------------- verification
+# After the timed loops (outside every timed region) the outputs of the last step are checked against the CPU oracle
+# (the checker only: nothing timed runs through it) on a fixed sample of rows of every distinct GEMM shape at its real
+# size (65536 / N rows, the tile choice of the run), and, at N > 1, the NCCL-gathered logits against the full head
+# weights recomputed on rank 0.
+VERIFY_ROWS = 256
+
+
+def _check(y, r, epi):
+    import oracle
+    if epi == "silu":
+        return oracle.silu_chain_close(y, r)
+    if epi == "gelu":
+        return oracle.gelu_close(y, r)
+    u = oracle.bf16_ulps(y, r)
+    return u == 0, f"max {u} ulps"
+
+
+def verify_job(job):
+    """Every distinct shape's last output on VERIFY_ROWS sampled rows against the oracle; returns (ok, details)."""
+    import oracle
+
+    g = torch.Generator().manual_seed(4242 + job.rank)
+    details, ok_all = {}, True
+    for tag, (x, wq, sw, bias, N, epi, y) in job.last_of.items():
+        M = x.shape[0]
+        idx = torch.randperm(M, generator=g)[:min(VERIFY_ROWS, M)].sort().values
+        idx_d = idx.to(job.dev)
+        xq, sx = oracle.quant_rows_ref(x.index_select(0, idx_d).cpu())
+        wqc, swc = wq.cpu(), sw.cpu()
+        bc = bias.cpu() if bias is not None else None
+        if epi == "silu":
+            r = oracle.gemm_i8_silu_ref(xq, sx, wqc, swc, bc)
+        else:
+            r = oracle.gemm_i8_ref(xq, sx, wqc, swc, bc, epi == "gelu")
+        ok, detail = _check(y.index_select(0, idx_d).cpu(), r, epi)
+        ok_all &= ok
+        details[tag] = f"{M}x{wq.shape[1]}x{N}: " + ("ok" if ok else "MISMATCH") + f" ({detail})"
+    if job.world > 1 and job.rank == 0:
+        # the gathered logits: 64 rows of the full [4096, 65536] result against the full head weights
+        from lfm2opt.quant import quantize_int8
+        gw = torch.Generator(device=job.dev).manual_seed(99_999)
+        w = (torch.randn(HEAD[2], HEAD[1], generator=gw, device=job.dev) * 0.02).to(torch.bfloat16)
+        hq, hs = quantize_int8(w)
+        del w
+        rows = torch.randperm(HEAD_M, generator=g)[:64].sort().values.tolist()
+        got = job.gathered_rows(rows).cpu()
+        xq, sx = oracle.quant_rows_ref(job.xh[rows].cpu())
+        r = oracle.gemm_i8_ref(xq, sx, hq.cpu(), hs.cpu())
+        ok, detail = _check(got, r, "none")
+        ok_all &= ok
+        details["gathered_logits"] = f"64 rows x {HEAD[2]}: " + ("ok" if ok else "MISMATCH") + f" ({detail})"
+        del hq, hs
+    return ok_all, details
+
+
+def verify_e2e(job, ee):
+    """The public-API step's outputs: its gathered logits equal the C-ABI job's, and the host copy equals the device
+    buffer it was read from."""
+    from lfm2opt.parallel import NSplitHead
+    V = HEAD[2]
+    if job.world > 1:
+        ok = torch.equal(ee.logits, job.logits)
+    else:
+        ok = torch.equal(ee.logits.view(HEAD_M, V), torch.cat([y for _, _, _, y in job.head_local], 0))
+    s0, cnt = ee.out_slice
+    ok_h = torch.equal(ee.hout, ee.logits[s0:s0 + cnt].cpu())
+    return ok and ok_h, {"e2e_logits_equal_job": ok, "e2e_host_copy_equal": ok_h}
+
+
 # ----------------------------------------------------------------------------------------------- GEMV sweep
 def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
     """Decode GEMV stack (16 layers + lm_head, distinct weights: 1.17 GB > L2) replayed from a CUDA graph, for both
@@ -473,9 +621,92 @@ def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
     return res
 
 
+GEMV_SHAPES = [("qkv", 3072, 2048), ("o_proj", 2048, 2048), ("conv_in", 6144, 2048), ("conv_out", 2048, 2048),
+               ("w1w3", 16384, 2048), ("w2", 2048, 8192), ("lm_head", 65536, 2048)]
+
+
+def gemv_shape_sweep(dev, world, batches=(1, 2, 4, 8, 16), per=20, replays=5):
+    """BASELINE config 2 shape by shape: the weight-only GEMV (lfm2q_gemv, the reference's gemv semantics) at every
+    decode shape and batch, each timed as a CUDA graph of `per` launches cycling through enough distinct weight copies
+    (>= 400 MB, more than 3x L2) that every launch streams its weights from HBM, as the reference's
+    profiling/bench_gemv.py:40 does. Replicas on every rank; GB/s = (N*K + 4N + 2BK + 2BN) / per-launch time."""
+    from lfm2opt.kernels import ext
+
+    E = ext()
+    hbm = load_peaks().get("hbm_gbs")
+    g = torch.Generator(device=dev).manual_seed(31)
+    out = {}
+    for name, N, K in GEMV_SHAPES:
+        copies = max(2, -(-400 * 10 ** 6 // (N * K)))
+        Ws = [torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8) for _ in range(copies)]
+        s = torch.rand(N, generator=g, device=dev) * 1e-3 + 1e-4
+        out[name] = {}
+        for B in batches:
+            x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty(B, N, device=dev, dtype=torch.bfloat16)
+
+            def burst():
+                for i in range(per):
+                    E.gemv(Ws[i % copies], s, x, y)
+
+            st = torch.cuda.Stream(dev)
+            st.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(st):
+                burst()
+            torch.cuda.current_stream(dev).wait_stream(st)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                burst()
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(replays):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (replays * per), world)
+            nbytes = N * K + 4 * N + 2 * B * K + 2 * B * N
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out[name][str(B)] = {"us": round(us, 2), "gbs_per_gpu": round(gbs, 1),
+                                 "frac_hbm": round(gbs / hbm, 4) if hbm else None}
+            del graph
+        del Ws
+        torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------------------------------------------- CPU baseline
+def shape_job_ops():
+    """2*M*N*K of the whole job per distinct shape (the config-5 mix), keyed by the names of distinct_shapes()."""
+    conv = sum(1 for l in range(LM_LAYERS) if l not in ATTN_LAYERS)
+    ops = {n: VISION_ROWS * VISION_LAYERS * 2 * K * N for n, K, N, _, _ in VISION}
+    ops.update({n: LM_ROWS * conv * 2 * K * N for n, K, N in LM_CONV})
+    ops.update({n: LM_ROWS * (LM_LAYERS - conv) * 2 * K * N for n, K, N in LM_ATTN})
+    ops.update({n: LM_ROWS * LM_LAYERS * 2 * K * N for n, K, N in LM_MLP})
+    ops["head"] = HEAD_M * 2 * HEAD[1] * HEAD[2]
+    assert sum(ops.values()) == job_ops()
+    return ops
+
+
+def host_cpu():
+    """The host's CPU as lscpu reports it (model, sockets, cores), and the threads torch uses."""
+    info = {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            k, _, v = line.partition(":")
+            if k.strip() in ("Model name", "CPU(s)", "Socket(s)", "Core(s) per socket", "Thread(s) per core"):
+                info[k.strip()] = v.strip()
+    except (OSError, subprocess.SubprocessError):
+        info["lscpu"] = "unavailable"
+    return info
+
+
 def cpu_sample(rows=2048):
-    """The reference's CPU path on one `rows`-row instance of every distinct GEMM shape of the job."""
+    """The reference's CPU path (per-token quantizer, exact int32 GEMM, fp32 epilogue, bf16; restated in oracle/) on
+    one `rows`-row instance of every distinct GEMM shape of the job. run() returns the seconds per shape."""
     import oracle
 
     torch.set_num_threads(os.cpu_count())
@@ -486,35 +717,52 @@ def cpu_sample(rows=2048):
         wq = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
         sw = torch.rand(N, generator=g) * 1e-3
         b = torch.randn(N, generator=g).to(torch.bfloat16) if bias else None
-        work.append((x, wq, sw, b, epi, 2 * rows * N * K))
+        work.append((name, x, wq, sw, b, epi, 2 * rows * N * K))
 
     def run():
-        for x, wq, sw, b, epi, _ in work:
+        sec = {}
+        for name, x, wq, sw, b, epi, _ in work:
+            t0 = time.perf_counter()
             xq, sx = oracle.quant_rows_ref(x)
             if epi == "silu":
                 oracle.gemm_i8_silu_ref(xq, sx, wq, sw)
             else:
                 oracle.gemm_i8_ref(xq, sx, wq, sw, b, epi == "gelu")
+            sec[name] = time.perf_counter() - t0
+        return sec
 
-    ops = sum(w[-1] for w in work)
-    return run, ops, f"one {rows}-row instance of each of the {len(work)} distinct GEMM shapes of the job " \
-                     f"(quant_rows + exact int32 GEMM + fp32 epilogue + bf16), {ops / 1e12:.2f} TOP"
+    sample_ops = {w[0]: w[-1] for w in work}
+    desc = (f"one {rows}-row instance of each of the {len(work)} distinct GEMM shapes of the job (quant_rows + exact "
+            f"int32 GEMM + fp32 epilogue + bf16, {sum(sample_ops.values()) / 1e12:.2f} TOP per pass); each shape's "
+            f"time scaled by its share of the config-5 job (its count per request x rows), so the TOPS are the job "
+            f"mix's")
+    return run, sample_ops, desc
+
+
+def weighted_tops(sec_tot, sample_ops, passes):
+    """Config-5 job throughput from per-shape CPU times: job seconds = sum over shapes of job ops / shape rate."""
+    jops = shape_job_ops()
+    job_sec = sum(jops[n] * (sec_tot[n] / passes) / sample_ops[n] for n in jops)
+    return sum(jops.values()) / job_sec / 1e12, job_sec
 
 
 def cpu_baseline(rows=2048, min_seconds=10.0):
     """The CPU path timed over whole passes of the sample until at least `min_seconds` of work (after one untimed
-    pass)."""
-    run, ops, sample = cpu_sample(rows)
+    pass); TOPS of the config-5 mix."""
+    run, sample_ops, sample = cpu_sample(rows)
     run()
-    n, t0 = 0, time.perf_counter()
+    n, tot, t0 = 0, {}, time.perf_counter()
     while True:
-        run()
+        for k, v in run().items():
+            tot[k] = tot.get(k, 0.0) + v
         n += 1
         sec = time.perf_counter() - t0
         if sec >= min_seconds:
             break
-    return {"value": round(ops * n / sec / 1e12, 3), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n} passes over " + sample, "seconds": round(sec, 2)}
+    tops, job_sec = weighted_tops(tot, sample_ops, n)
+    return {"value": round(tops, 3), "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} passes over " + sample, "seconds": round(sec, 2),
+            "job_seconds_extrapolated": round(job_sec, 1), "host": host_cpu()}
 
 
 def job_config(world, rows_per_gpu):
@@ -526,12 +774,6 @@ def job_config(world, rows_per_gpu):
 
 
 # ----------------------------------------------------------------------------------------------- main
-def roofline_from(gemm_events):
-    tot_ms = sum(a.elapsed_time(b) for a, b, _ in gemm_events)
-    ops = sum(o for _, _, o in gemm_events)
-    return ops, tot_ms
-
-
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -693,22 +935,26 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
-        run, ops, sample = cpu_sample()
+        run, sample_ops, sample = cpu_sample()
         for _ in range(warmup):
             run()
+        tot = {}
         t0 = time.perf_counter()
         for _ in range(a.steps):
-            run()
+            for k, v in run().items():
+                tot[k] = tot.get(k, 0.0) + v
         sec = (time.perf_counter() - t0) / a.steps
-        v = round(ops / sec / 1e12, 3)
+        tops, job_sec = weighted_tops(tot, sample_ops, a.steps)
+        v = round(tops, 3)
+        cfg = job_config(a.gpus, VISION_ROWS // a.gpus)
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": v, "unit": "TOPS", "n_gpus": a.gpus, "steps": a.steps,
             "warmup": warmup, "ms_per_step": round(sec * 1e3, 2), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": job_config(a.gpus, VISION_ROWS // a.gpus),
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": cfg,
             "cpu_baseline": {"value": v, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": "each step: " + sample + "; the reference's CPU path restated in oracle/ "
-                                       "(the reference itself is a CUDA torch extension, not runnable on the host)"},
+                                       "(the reference itself is a CUDA torch extension, not runnable on the host)",
+                             "job_seconds_extrapolated": round(job_sec, 1), "host": host_cpu()},
             "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
 
@@ -724,12 +970,12 @@ def main():
     total_ops = job_ops()
     log(f"job: {total_ops / 1e12:.2f} TOP per step over {world} GPU(s); {len(job.calls)} launches per rank")
 
-    # value: device-resident, C-ABI launches, per-GEMM events
-    gemm_events = []
+    # value: device-resident, C-ABI launches, CUDA events around every launch (phases, per-shape TOPS, roofline)
+    rec = StepRecorder()
     launches = [0]
 
     def step():
-        launches[0] += job.run(gemm_events)
+        launches[0] += job.run(rec)
 
     for _ in range(warmup):
         job.run()
@@ -743,17 +989,26 @@ def main():
     clocks = ClockSampler(uuids)
     if rank == 0:
         clocks.start()
-    ms = time_steps(step, a.steps, 0, world)
+    ms = time_steps(step, a.steps, 0, world, on_start=clocks.mark_start if rank == 0 else None,
+                    on_end=clocks.mark_end if rank == 0 else None)
     clk = clocks.stop() if rank == 0 else None
     ms_step = ms / a.steps
     value = total_ops / (ms_step * 1e-3) / 1e12
-    g_ops, g_ms = roofline_from(gemm_events)
-    g_ms = max_over_ranks(g_ms, world)
-    achieved = sum_over_ranks(g_ops, world) / world / (g_ms * 1e-3) / 1e12  # per-GPU GEMM TOPS
-    n_gemm = len(gemm_events)  # this rank's timed GEMM launches
+    phases, shapes = rec.summary(a.steps)
+    gemm_ops = sum(o for k, _, o, _, _ in rec.items if k == "gemm")
+    g_ms = max_over_ranks(phases["gemm"] * a.steps, world)
+    achieved = sum_over_ranks(gemm_ops, world) / world / (g_ms * 1e-3) / 1e12  # per-GPU GEMM TOPS
+    n_gemm = sum(1 for k, _, _, _, _ in rec.items if k == "gemm")  # this rank's timed GEMM launches
+    phases = {k: round(max_over_ranks(v, world), 3) for k, v in phases.items()}
+    phases["other"] = round(ms_step - sum(phases.values()), 3)
     total_launches = int(sum_over_ranks(launches[0], world))
+    dev_err = _capi.lib().lfm2q_check_device(0)  # a bounded pipeline wait that gave up would void the outputs
+    ok_job, vdetail = verify_job(job)
+    ok_job = ok_job and dev_err == 0
+    del rec
 
     e2e = None
+    ok_e2e = True
     if not a.no_e2e:
         ee = E2E(job)
         ms_e = time_steps(ee.step, a.steps, warmup, world)
@@ -762,25 +1017,34 @@ def main():
                "h2d_bytes_per_step": int(sum_over_ranks(ee.h2d_bytes, world)),
                "d2h_bytes_per_step": int(sum_over_ranks(ee.d2h_bytes, world)),
                "api": "lfm2opt.int8.Int8Linear + lfm2opt.parallel.NSplitHead"}
+        ok_e2e, edetail = verify_e2e(job, ee)
+        vdetail.update(edetail)
         del ee
+    verified = max_over_ranks(0.0 if (ok_job and ok_e2e) else 1.0, world) == 0.0
+    if dev_err:
+        vdetail["device_error_word"] = "set: a bounded pipeline wait gave up"
 
-    gemv = None
+    gemv = gemv_shapes = None
     if not a.no_gemv:
         gemv = gemv_sweep(dev, world, rank)
+        gemv_shapes = gemv_shape_sweep(dev, world)
 
     peaks = load_peaks()
     hbm = peaks.get("hbm_gbs")
     out = None
     if rank == 0:
         cpu = None if (a.no_cpu or world > 1) else cpu_baseline()
-        traffic = load_traffic()
+        traffic = load_traffic() if world == 1 else None
         roof = {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 kind::i8)", "achieved": round(achieved, 1),
                 "peak": INT8_PEAK_NOMINAL, "unit": "TOPS", "frac": round(achieved / INT8_PEAK_NOMINAL, 4),
                 "peak_source": "B200 dense INT8 datasheet (MEASURED_PEAKS.json has no INT8 entry)",
                 "frac_of_2x_measured_bf16": (round(achieved / (2 * peaks["bf16_tflops"]), 4)
                                              if peaks.get("bf16_tflops") else None),
                 "launches_timed_per_gpu": n_gemm, "avg_launch_us": round(g_ms * 1e3 / max(1, n_gemm), 1),
-                "traffic": traffic.get("dram_bytes_per_launch") if traffic else None}
+                "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                "traffic_source": (traffic.get("source") if traffic else
+                                   "not measured at N > 1 (the committed ncu capture is of the N = 1 job)"),
+                "per_shape": shapes}
         if gemv:
             w1 = gemv["w16"][1]["gbs"] / world
             a1 = gemv["a8"][1]["gbs"] / world
@@ -790,7 +1054,8 @@ def main():
                         "b1_gbs_per_gpu": {"w16": round(w1, 1), "a8": round(a1, 1)},
                         "hbm_peak_gbs": hbm,
                         "frac_b1": {"w16": round(w1 / hbm, 4), "a8": round(a1 / hbm, 4)} if hbm else None,
-                        "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy bandwidth)"}
+                        "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy bandwidth)",
+                        "per_shape_w16": gemv_shapes}
         else:
             gemv_out = None
         out = {
@@ -799,6 +1064,8 @@ def main():
             "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,1) activations with 0.1% x20 "
                                                            "outlier channels in the LM; N(0,0.02) weights, int8 per-channel)",
             "config": job_config(world, job.vrows),
+            "verified": verified, "verify": vdetail,
+            "phases_ms_per_step": phases,
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": total_launches, "clocks": clk,
             "gemv": gemv_out,
         }
