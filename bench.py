@@ -574,26 +574,37 @@ def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
                            torch.rand(N, generator=g, device=dev) * 1e-3 + 1e-4))
     layers.append((torch.randint(-127, 128, (65536, 2048), generator=g, device=dev, dtype=torch.int8),
                    torch.rand(65536, generator=g, device=dev) * 1e-3 + 1e-4))
-    res = {"w16": {}, "a8": {}}
-    for mode in ("w16", "a8"):
+    res = {"w16": {}, "a8": {}, "w16_chain": {}}
+    for mode in ("w16", "a8", "w16_chain"):
         for B in batches:
+            if mode == "w16_chain" and B > 4:
+                continue
             xs = {K: torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16) for K in (2048, 8192)}
             xq = {K: torch.empty(B, K, device=dev, dtype=torch.int8) for K in (2048, 8192)}
             sx = {K: torch.empty(B, device=dev, dtype=torch.float32) for K in (2048, 8192)}
             ys = [torch.empty(B, W.shape[0], device=dev, dtype=torch.bfloat16) for W, _ in layers]
             nbytes = sum(W.shape[0] * W.shape[1] + 4 * W.shape[0] + 2 * B * W.shape[1] + 2 * B * W.shape[0]
                          for W, _ in layers)
+            if mode == "w16_chain":
+                # the 65 GEMVs through lfm2q_gemv_chain (one launch each, in order, L2 window ahead), replayed from
+                # a CUDA graph like the other modes
+                from lfm2opt.kernels import GemvChain
+                chain = GemvChain([(W, s, xs[W.shape[1]], y) for (W, s), y in zip(layers, ys)])
 
-            def sweep():
-                stream = torch.cuda.current_stream(dev).cuda_stream
-                for (W, s), y in zip(layers, ys):
-                    K = W.shape[1]
-                    if mode == "w16":
-                        E.gemv(W, s, xs[K], y)
-                    else:  # Int8Linear's a8 flow: quant_rows, then gemm_i8 (routed to the A8 GEMV), both under PDL
-                        L.lfm2q_quant_rows(xs[K].data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), B, K, stream)
-                        L.lfm2q_gemv_a8(W.data_ptr(), s.data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), None,
-                                        y.data_ptr(), W.shape[0], K, B, 0, stream)
+                def sweep():
+                    chain()
+            else:
+
+                def sweep():
+                    stream = torch.cuda.current_stream(dev).cuda_stream
+                    for (W, s), y in zip(layers, ys):
+                        K = W.shape[1]
+                        if mode == "w16":
+                            E.gemv(W, s, xs[K], y)
+                        else:  # Int8Linear's a8 flow: quant_rows, then gemm_i8 (routed to the A8 GEMV), under PDL
+                            L.lfm2q_quant_rows(xs[K].data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), B, K, stream)
+                            L.lfm2q_gemv_a8(W.data_ptr(), s.data_ptr(), xq[K].data_ptr(), sx[K].data_ptr(), None,
+                                            y.data_ptr(), W.shape[0], K, B, 0, stream)
 
             st = torch.cuda.Stream(dev)
             st.wait_stream(torch.cuda.current_stream(dev))
@@ -616,7 +627,7 @@ def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
             ms = max_over_ranks(e0.elapsed_time(e1) / replays, world)
             res[mode][B] = {"us_per_sweep": round(ms * 1e3, 2), "gbs": round(world * nbytes / (ms * 1e-3) / 1e9, 1),
                             "bytes_per_sweep": nbytes,
-                            "launches": len(layers) * (1 if mode == "w16" else 2)}
+                            "launches": len(layers) * (2 if mode == "a8" else 1)}
             del graph
     return res
 
@@ -1046,14 +1057,17 @@ def main():
                                    "not measured at N > 1 (the committed ncu capture is of the N = 1 job)"),
                 "per_shape": shapes}
         if gemv:
-            w1 = gemv["w16"][1]["gbs"] / world
-            a1 = gemv["a8"][1]["gbs"] / world
-            gemv_out = {"metric": "decode GEMV HBM GB/s (16-layer LFM2 stack + lm_head, CUDA graph)",
+            b1 = {m: gemv[m][1]["gbs"] / world for m in ("w16", "w16_chain", "a8")}
+            gemv_out = {"metric": "decode GEMV HBM GB/s (16-layer LFM2 stack + lm_head: 65 GEMVs, each after the one "
+                                  "before, replayed from a CUDA graph; w16: lfm2q_gemv per layer; w16_chain: "
+                                  "lfm2q_gemv_chain (same GEMVs, weights of the layers ahead streamed into L2); "
+                                  "a8: quant_rows + A8 GEMV per layer)",
                         "w16_weight_only": {str(k): v for k, v in gemv["w16"].items()},
+                        "w16_chain": {str(k): v for k, v in gemv["w16_chain"].items()},
                         "a8_int8_tokens": {str(k): v for k, v in gemv["a8"].items()},
-                        "b1_gbs_per_gpu": {"w16": round(w1, 1), "a8": round(a1, 1)},
+                        "b1_gbs_per_gpu": {m: round(v, 1) for m, v in b1.items()},
                         "hbm_peak_gbs": hbm,
-                        "frac_b1": {"w16": round(w1 / hbm, 4), "a8": round(a1 / hbm, 4)} if hbm else None,
+                        "frac_b1": {m: round(v / hbm, 4) for m, v in b1.items()} if hbm else None,
                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy bandwidth)",
                         "per_shape_w16": gemv_shapes}
         else:

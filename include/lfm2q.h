@@ -38,8 +38,9 @@ const char *lfm2q_version(void);
 /* 1 if the current device is an sm_100 part this library can launch on, else 0. */
 int lfm2q_device_supported(void);
 
-/* Reads (and with clear != 0 resets) the sticky device error word the GEMM kernels set when a bounded wait
- * expires. Returns LFM2Q_OK or LFM2Q_ETIMEOUT. Synchronous (copies one int from the device). */
+/* Reads (and with clear != 0 resets) the sticky device error word that the tcgen05 GEMMs set when one of their
+ * bounded pipeline waits gives up (no other kernel of this library waits on anything). Returns LFM2Q_OK or
+ * LFM2Q_ETIMEOUT. Synchronous (copies one int from the device). Poll it after a batch of work whose outputs matter. */
 int lfm2q_check_device(int clear);
 
 /* ------------------------------------------------------------------ activation quantizers
@@ -118,6 +119,31 @@ int lfm2q_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const floa
  * lfm2q_quant_rows + lfm2q_gemm_i8 on the same inputs. Needs K % 64 == 0 (any B: chunks of up to 16 tokens). */
 int lfm2q_linear_a8(const uint16_t *x, const int8_t *W, const float *sw, const uint16_t *bias, uint16_t *y, int N,
                     int K, int B, int gelu, void *stream);
+
+/* ------------------------------------------------------------------ chained decode GEMV
+ * No single counterpart in the reference: it replaces a run of gemv launches (kernels/lfm2_decode.cu:708-714 behind
+ * gemv, kernels/lfm2_decode.cpp:73-85) that the reference's decode step issues back to back inside its captured
+ * graph (src/lfm2opt/runtime.py:223-244, :247-294). The layers run in list order, each after the previous one has
+ * completed (so a layer may read an earlier layer's y as its x); each is lfm2q_gemv with int8 weights, y = bf16((x .
+ * W^T) * scale), computed on the int8 tensor path with the tokens sliced into exact fixed-point bytes where the
+ * slices fit in shared memory (B * (B <= 2 ? 3 : 2) * (K + 64) <= 65536 and B * K <= 16384; else the bf16 path).
+ * While a layer runs, the weights of the next layers of the list stream into L2, so small layers do not wait for
+ * HBM. One kernel launch per layer, capturable in a CUDA graph; nothing is allocated. */
+typedef struct {
+  const int8_t *W;    /* int8 [N, K], 16-byte aligned */
+  const float *scale; /* fp32 [N] */
+  const uint16_t *x;  /* bf16 [B, K], 16-byte aligned; may be an earlier layer's y */
+  uint16_t *y;        /* bf16 [B, N]; must not overlap this layer's x */
+  int N;
+  int K;              /* a multiple of 512 */
+} lfm2q_gemv_layer;
+
+#define LFM2Q_CHAIN_MAX_LAYERS 96
+#define LFM2Q_CHAIN_MAX_TOKENS 4
+
+/* Runs layers[0 .. n_layers) (a host array, read during the call) for B tokens, 1 <= B <= 4, 1 <= n_layers <= 96,
+ * on `stream`. */
+int lfm2q_gemv_chain(const lfm2q_gemv_layer *layers, int n_layers, int B, void *stream);
 
 /* Replaces launch_gemv_epi (kernels/lfm2_decode.cu:818-827) behind gemv_epi (kernels/lfm2_decode.cpp:130-150).
  * Batch 1. epi 0: W = w1|w3 [2S, K] -> y [S] = bf16(bf16(silu(g)) * u).

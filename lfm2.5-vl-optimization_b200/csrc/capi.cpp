@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/lfm2q.h"
 #include "launch.h"
@@ -26,34 +27,31 @@ static int fail(int code, const std::string &msg) {
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Device facts, filled once per device (std::call_once: concurrent first calls from several threads see the
+// complete record).
 struct DevInfo {
   int sms = 0;
-  int supported = -1;  // -1 unknown
+  int supported = 0;
 };
 static DevInfo g_dev[64];
-static std::mutex g_dev_mu;
+static std::once_flag g_dev_once[64];
 
-static DevInfo &dev_info() {
+static const DevInfo &dev_info() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     cudaGetLastError();
-    static DevInfo none;
-    none.supported = 0;
+    static const DevInfo none;
     return none;
   }
-  DevInfo &d = g_dev[dev & 63];
-  if (d.supported < 0) {
-    std::lock_guard<std::mutex> lk(g_dev_mu);
-    if (d.supported < 0) {
-      int major = 0, minor = 0, sms = 0;
-      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      d.sms = sms;
-      d.supported = (major == 10 && minor == 0) ? 1 : 0;
-    }
-  }
-  return d;
+  std::call_once(g_dev_once[dev], [dev] {
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    g_dev[dev].sms = sms;
+    g_dev[dev].supported = (major == 10 && minor == 0) ? 1 : 0;
+  });
+  return g_dev[dev];
 }
 
 int device_sm_count() {
@@ -93,9 +91,7 @@ int lfm2q_device_supported(void) { return device_is_sm100() ? 1 : 0; }
 int lfm2q_check_device(int clear) {
   if (int e = device_gate()) return e;
   const int v = gemm_device_error(clear != 0);
-  const int u = gemv_device_error(clear != 0);
   if (v) return fail(LFM2Q_ETIMEOUT, "lfm2q: a GEMM pipeline wait timed out on the device");
-  if (u) return fail(LFM2Q_ETIMEOUT, "lfm2q: a GEMV pipeline wait timed out on the device");
   return LFM2Q_OK;
 }
 
@@ -268,6 +264,26 @@ int lfm2q_linear_a8(const uint16_t *x, const int8_t *W, const float *sw, const u
   if (int e = device_gate()) return e;
   return launched(launch_linear_a8(x, W, sw, bias, y, N, K, B, gelu != 0, g_pdl.load(), (cudaStream_t)stream),
                   "linear_a8");
+}
+
+int lfm2q_gemv_chain(const lfm2q_gemv_layer *layers, int n_layers, int B, void *stream) {
+  REQUIRE(n_layers >= 1 && n_layers <= LFM2Q_CHAIN_MAX_LAYERS, "n_layers must be in [1, 96]");
+  REQUIRE(B >= 1 && B <= LFM2Q_CHAIN_MAX_TOKENS, "x [B, K]: the chained GEMV takes 1 <= B <= 4 tokens");
+  REQUIRE(layers != nullptr, "layers must be non-null");
+  std::vector<ChainLayer> L((size_t)n_layers);
+  for (int l = 0; l < n_layers; ++l) {
+    const lfm2q_gemv_layer &g = layers[l];
+    const std::string at = "layer " + std::to_string(l) + ": ";
+    REQUIRE(g.W && g.scale && g.x && g.y, at + "W, scale, x and y must be non-null");
+    REQUIRE(aligned16(g.W) && aligned16(g.x), at + "W and x must be 16-byte aligned");
+    REQUIRE(g.N > 0 && g.K >= 512 && g.K % 512 == 0, at + "need N > 0 and K a positive multiple of 512");
+    const uintptr_t x0 = reinterpret_cast<uintptr_t>(g.x), x1 = x0 + (size_t)B * g.K * 2;
+    const uintptr_t y0 = reinterpret_cast<uintptr_t>(g.y), y1 = y0 + (size_t)B * g.N * 2;
+    REQUIRE(x1 <= y0 || y1 <= x0, at + "y must not overlap x");
+    L[(size_t)l] = ChainLayer{g.W, g.scale, g.x, g.y, g.N, g.K};
+  }
+  if (int e = device_gate()) return e;
+  return launched(launch_gemv_chain(L.data(), n_layers, B, g_pdl.load(), (cudaStream_t)stream), "gemv_chain");
 }
 
 int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int S,

@@ -118,13 +118,13 @@ __device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// ------------------------------------------------------------------ streaming loads
-// 16-byte read-only load that does not allocate in L1: weights are read exactly once per launch.
-__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+// 16-byte load through L2 (ld.global.cg), for data the previous kernel in the stream wrote. A kernel launched with
+// programmatic dependent launch starts before its predecessor has finished; after griddepcontrol.wait the
+// predecessor's stores are in L2, but a line of the same address cached in this SM's L1 or read-only path could be
+// stale, so activations and their scales are never read through those caches.
+__device__ __forceinline__ uint4 ld_cg16(const void *p) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
 

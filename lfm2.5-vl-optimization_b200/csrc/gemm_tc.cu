@@ -586,7 +586,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
       int pmt, pnt;
       tile_coord(tile_i, args, pmt, pnt);
       const int pm = pmt * TMU + (int)rank * TM + row;
-      pf_sx = (pm < M && !GROUPED && !W8) ? __ldg(args.sa + pm) : 0.f;
+      pf_sx = (pm < M && !GROUPED && !W8) ? __ldcg(args.sa + pm) : 0.f;  // the previous kernel wrote sa
       const int width = (EPI == EPI_SILU) ? BN / 4 : BN / PARTS;
       const int c0 = (EPI == EPI_SILU) ? pnt * (BN / 2) + half * width : pnt * BN + half * width;
       const int count = (EPI == EPI_SILU) ? 2 * width : width;
@@ -656,7 +656,7 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
     auto scale_next = [&]() {
       float v = 0.f;
       if (sl_tile < tiles) {
-        if (sl_m < M) v = __ldg(args.sa + (size_t)sl_g * M + sl_m);
+        if (sl_m < M) v = __ldcg(args.sa + (size_t)sl_g * M + sl_m);
         if (++sl_g == G) {
           sl_g = 0;
           sl_tile += units;

@@ -22,249 +22,38 @@
 #include <utility>
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "launch.h"
 
 namespace lfm2q {
 namespace {
 
-constexpr int GV_THREADS = 256;  // 8 warps
-constexpr int GV_RING = 6;       // K steps (1 KB each) a warp keeps in flight
-
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-template <typename WT>
-struct WFmt;
-// int8: one 16-byte chunk = 16 codes = 4 MMA k-steps of one row; a 64-wide K step is one chunk per lane-row
-template <>
-struct WFmt<int8_t> {
-  static constexpr int KSTEP = 64;  // K covered per lane chunk pair
-  static constexpr int STEPS = 4;   // MMA k16 steps per chunk
-  __device__ static void frag(const uint4 &r0, const uint4 &r1, int s, uint32_t (&a)[4]) {
-    const uint32_t w0 = (&r0.x)[s], w1 = (&r1.x)[s];
-    i8x4_to_bf16x2x2(w0, a[0], a[2]);  // row g: k slots 2t,2t+1 | 2t+8,2t+9
-    i8x4_to_bf16x2x2(w1, a[1], a[3]);  // row g + 8
-  }
-};
-// bf16: one 16-byte chunk = 8 weights = 2 MMA k-steps of one row
-template <>
-struct WFmt<bf16> {
-  static constexpr int KSTEP = 32;
-  static constexpr int STEPS = 2;
-  __device__ static void frag(const uint4 &r0, const uint4 &r1, int s, uint32_t (&a)[4]) {
-    a[0] = (&r0.x)[2 * s];
-    a[2] = (&r0.x)[2 * s + 1];
-    a[1] = (&r1.x)[2 * s];
-    a[3] = (&r1.x)[2 * s + 1];
-  }
-};
-
-// x fragment words for lane (g, t) at K position k0 of token `tok`: the lane's chunk of x covers the same
-// physical k as its weight chunk: int8 -> 16 bf16 (two 16-byte loads), bf16 -> 8 bf16 (one load)
-template <typename WT>
-__device__ __forceinline__ void load_x(const bf16 *__restrict__ x, int K, int tok, int B, int kphys, uint32_t (&xw)[8]) {
-  constexpr int NW = WFmt<WT>::KSTEP / 8;  // 32-bit words per lane chunk: 8 (int8) or 4 (bf16)
-  if (tok < B) {
-    const uint4 *p = reinterpret_cast<const uint4 *>(x + (size_t)tok * K + kphys);
-    const uint4 v0 = __ldg(p);
-    xw[0] = v0.x; xw[1] = v0.y; xw[2] = v0.z; xw[3] = v0.w;
-    if (NW == 8) {
-      const uint4 v1 = __ldg(p + 1);
-      xw[4] = v1.x; xw[5] = v1.y; xw[6] = v1.z; xw[7] = v1.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) xw[i] = 0u;
-  }
-}
-
-// Core: one warp accumulates rows [r0, r0 + 16) x K-slice [kb, ke) for tokens 0..8*NT-1 into acc[NT][4].
-// Weights travel global -> shared memory with cp.async (16 bytes per lane per row and step), GV_RING steps ahead, in
-// a ring private to the warp (ring: GV_RING x 1 KB; each lane writes and later reads only its own 16-byte slots,
-// at row * 64 + t * 16, which is bank-conflict-free), so no registers are tied up by loads in flight and a warp
-// keeps ~5 KB of weights outstanding. A slot is refilled only after its data has been read and used.
-template <typename WT, int NT>
-__device__ __forceinline__ void warp_gemv(const WT *__restrict__ W, const bf16 *__restrict__ x, int N, int K, int B,
-                                          int r0, int kb, int ke, float (&acc)[NT][4], uint8_t *ring, bool pdl) {
-  constexpr int KSTEP = WFmt<WT>::KSTEP, STEPS = WFmt<WT>::STEPS;
-  constexpr int CH = 16 / sizeof(WT);  // elements per 16-byte chunk
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const WT *row0 = W + (size_t)min(r0 + g, N - 1) * K + kb + t * CH;
-  const WT *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K + kb + t * CH;
-  const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(ring) + g * 64 + t * 16;
-  const int nsteps = (ke - kb) / KSTEP;
-
-  auto issue = [&](int st) {
-    if (st < nsteps) {
-      const uint32_t d = slot0 + (st % GV_RING) * 1024;
-      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + st * KSTEP) : "memory");
-      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(row1 + st * KSTEP)
-                   : "memory");
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  auto lds = [&](int st, uint4 &w0, uint4 &w1) {
-    const uint32_t d = slot0 + (st % GV_RING) * 1024;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
-                 : "memory");
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
-                 : "r"(d + 512)
-                 : "memory");
-  };
-
-  // two independent accumulator chains (even / odd MMA k-steps), summed at the end
-  float acc2[NT][4];
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = acc2[j][e] = 0.f;
-
-#pragma unroll
-  for (int st = 0; st < GV_RING; ++st) issue(st);  // weights are immutable: stream before the dependency wait
-  if (pdl) pdl_wait();
-  // software pipeline: the weights (shared memory) and x fragments (L1 / L2) of step st + 1 are loaded while
-  // step st is converted and multiplied
-  uint4 wc0, wc1, wn0, wn1;
-  uint32_t xc[NT][8], xn[NT][8];
-  asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 1) : "memory");
-  if (nsteps > 0) {
-    lds(0, wc0, wc1);
-#pragma unroll
-    for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kb + t * CH, xc[j]);
-  }
-  for (int st = 0; st < nsteps; ++st) {
-    if (st + 1 < nsteps) {
-      asm volatile("cp.async.wait_group %0;" ::"n"(GV_RING - 2) : "memory");
-      lds(st + 1, wn0, wn1);
-#pragma unroll
-      for (int j = 0; j < NT; ++j) load_x<WT>(x, K, g + 8 * j, B, kb + (st + 1) * KSTEP + t * CH, xn[j]);
-    }
-#pragma unroll
-    for (int s = 0; s < STEPS; ++s) {
-      uint32_t a[4];
-      WFmt<WT>::frag(wc0, wc1, s, a);
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        if (s & 1) mma_bf16_16816(acc2[j], a, xc[j][2 * s], xc[j][2 * s + 1]);
-        else mma_bf16_16816(acc[j], a, xc[j][2 * s], xc[j][2 * s + 1]);
-      }
-    }
-    issue(st + GV_RING);  // slot of step st: its data is already in registers
-    wc0 = wn0;
-    wc1 = wn1;
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) xc[j][i] = xn[j][i];
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] += acc2[j][e];
-}
-
-__device__ __forceinline__ void mma_s8_16832(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// A8 core: int8 weights x int8 tokens (quantized per token) -> exact int32 sums, rows [r0, r0 + 16) x K-slice
-// [kb, ke). Same cp.async ring and software pipeline as warp_gemv; no conversion at all: the 16 bytes a lane holds
-// of rows g and g + 8 feed two m16n8k32 s8 MMAs directly. Lane (g, t), MMA s of a 64-byte step: logical k slots
-// 4t..4t+3 / 16+4t..16+4t+3 take physical bytes 16t+8s..+3 / 16t+8s+4..+7, for W and x alike.
-// phase 0: prefetch + compute; 1: only issue the first RING steps (weights, immutable); 2: compute after phase 1.
-template <int NT, int RING = GV_RING>
-__device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const int8_t *xq, int xstride, int N, int K,
-                                             int B, int r0, int kb, int ke, int (&acc)[NT][4], uint8_t *ring, bool pdl,
-                                             int phase = 0) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int8_t *row0 = W + (size_t)min(r0 + g, N - 1) * K + kb + t * 16;
-  const int8_t *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K + kb + t * 16;
-  const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(ring) + g * 64 + t * 16;
-  const int nsteps = (ke - kb) / 64;
-  auto issue = [&](int st) {
-    if (st < nsteps) {
-      const uint32_t d = slot0 + (st % RING) * 1024;
-      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + st * 64) : "memory");
-      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(row1 + st * 64) : "memory");
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  auto lds = [&](int st, uint4 &w0, uint4 &w1) {
-    const uint32_t d = slot0 + (st % RING) * 1024;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
-                 : "memory");
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
-                 : "r"(d + 512)
-                 : "memory");
-  };
-  auto ldx = [&](int st, uint4 (&xw)[NT]) {
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const int tok = g + 8 * j;
-      xw[j] = tok < B ? *reinterpret_cast<const uint4 *>(xq + (size_t)tok * xstride + kb + st * 64 + t * 16)
-                      : make_uint4(0, 0, 0, 0);
-    }
-  };
-  if (phase != 2) {
-#pragma unroll
-    for (int st = 0; st < RING; ++st) issue(st);
-  }
-  if (phase == 1) return;
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = 0;
-  if (pdl) pdl_wait();
-  uint4 wc0, wc1, wn0, wn1, xc[NT], xn[NT];
-  asm volatile("cp.async.wait_group %0;" ::"n"(RING - 1) : "memory");
-  if (nsteps > 0) {
-    lds(0, wc0, wc1);
-    ldx(0, xc);
-  }
-  for (int st = 0; st < nsteps; ++st) {
-    if (st + 1 < nsteps) {
-      asm volatile("cp.async.wait_group %0;" ::"n"(RING - 2) : "memory");
-      lds(st + 1, wn0, wn1);
-      ldx(st + 1, xn);
-    }
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const uint32_t a[4] = {(&wc0.x)[2 * s], (&wc1.x)[2 * s], (&wc0.x)[2 * s + 1], (&wc1.x)[2 * s + 1]};
-#pragma unroll
-      for (int j = 0; j < NT; ++j) mma_s8_16832(acc[j], a, (&xc[j].x)[2 * s], (&xc[j].x)[2 * s + 1]);
-    }
-    issue(st + RING);
-    wc0 = wn0;
-    wc1 = wn1;
-#pragma unroll
-    for (int j = 0; j < NT; ++j) xc[j] = xn[j];
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
-// Fragment accumulator element e of token group j -> (row in group, token)
-__device__ __forceinline__ int frag_row(int lane, int e) { return (lane >> 2) + ((e & 2) ? 8 : 0); }
-__device__ __forceinline__ int frag_tok(int lane, int j, int e) { return 8 * j + 2 * (lane & 3) + (e & 1); }
-
 // Plain GEMV. Block = RG row groups x KS K-slices (RG * KS == 8 warps); blocks walk the row-group sets in a grid
 // stride (grid = min(sets, resident blocks)), so large N runs in one wave with balanced work.
+// This block's share of every range of pf requested into L2 (one bulk prefetch per range, thread 0).
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch &pf) {
+  if (threadIdx.x != 0) return;
+  for (int i = 0; i < pf.cnt; ++i) {
+    const unsigned long long chunk = ((pf.n[i] + gridDim.x - 1) / gridDim.x + 255) / 256 * 256;
+    const unsigned long long lo = chunk * blockIdx.x;
+    if (lo < pf.n[i]) {
+      const unsigned long long len = pf.n[i] - lo < chunk ? pf.n[i] - lo : chunk;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char *>(pf.p[i]) + lo),
+                   "r"((uint32_t)len)
+                   : "memory");
+    }
+  }
+}
+
 template <typename WT, int NT, int KS>
 __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__ W, const float *__restrict__ scale,
                                                           const bf16 *__restrict__ x, bf16 *__restrict__ y, int N, int K,
-                                                          int B, int pdl) {
+                                                          int B, int pdl, const L2Prefetch pf) {
   constexpr int RG = 8 / KS;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x GV_RING x 1 KB
   __shared__ float red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
   if (pdl == 2) pdl_trigger();
+  l2_prefetch_share(pf);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
@@ -345,7 +134,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
       const uint4 *xr = reinterpret_cast<const uint4 *>(xbf + (size_t)b * K);
       uint32_t m2 = 0;
       for (int c = lane; c < K / 8; c += 32) {
-        const uint4 v = __ldg(xr + c);
+        const uint4 v = ld_cg16(xr + c);
         m2 = __vmaxu2(m2, __vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu));
         m2 = __vmaxu2(m2, __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
       }
@@ -353,7 +142,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
       const float rinv = __frcp_rn(sc);
       if (lane == 0) sx_s[b] = sc;
       for (int c = lane; c < K / 8; c += 32) {
-        const uint4 v = __ldg(xr + c);
+        const uint4 v = ld_cg16(xr + c);
         const uint32_t o0 = pack_sums4(q8r2(make_float2(bf_lo(v.x), bf_hi(v.x)), sc, rinv),
                                        q8r2(make_float2(bf_lo(v.y), bf_hi(v.y)), sc, rinv));
         const uint32_t o1 = pack_sums4(q8r2(make_float2(bf_lo(v.z), bf_hi(v.z)), sc, rinv),
@@ -377,7 +166,8 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
         for (int e = 0; e < 4; ++e) {
           const int n = r0 + frag_row(lane, e), b = frag_tok(lane, j, e);
           if (n < N && b < B)
-            y[(size_t)b * N + n] = f2bf(epi_token<GELU>(acc[j][e], sx[b], sw[n], bias ? bf2f(bias[n]) : 0.f));
+            y[(size_t)b * N + n] =
+                f2bf(epi_token<GELU>(acc[j][e], FUSEQ ? sx[b] : __ldcg(sx + b), sw[n], bias ? bf2f(bias[n]) : 0.f));
         }
       continue;
     }
@@ -394,112 +184,11 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
       int v = 0;
 #pragma unroll
       for (int s2 = 0; s2 < KS; ++s2) v += red[((g2 * KS + s2) * 16 + rr) * 8 * NT + b];
-      y[(size_t)b * N + n] = f2bf(epi_token<GELU>(v, sx[b], sw[n], bias ? bf2f(bias[n]) : 0.f));
+      y[(size_t)b * N + n] = f2bf(epi_token<GELU>(v, FUSEQ ? sx[b] : __ldcg(sx + b), sw[n], bias ? bf2f(bias[n]) : 0.f));
     }
     __syncthreads();
   }
 }
-
-// Writes tokens 0..B-1 of x (bf16 [B, K]) as NSL-byte fixed point into shared memory, row b * NSL + s holding byte s
-// of every element (q = sum_s q_s 256^s, balanced bytes), and the token's exponent E (x = q * 2^E) into e_s[b].
-// All threads of the block take part (16-byte chunks c = tid, tid + 256, ..., held in registers across the absmax
-// reduction, XS_CH chunks per thread and token at most: K <= 8 * 256 * XS_CH / B); the block is synchronised inside
-// and the caller synchronises again before reading the slices.
-constexpr int XS_CH = 8;
-template <int NSL>
-__device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride, int *e_s,
-                                             float (&red_max)[4][8]) {
-  constexpr int QBITS = 8 * NSL - 2;  // |q| < 2^QBITS
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int K8 = K / 8, total = B * K8;
-  // this thread's chunks over all tokens: index i = tid + j * 256 -> token i / K8, chunk i % K8
-  uint4 v[XS_CH];
-#pragma unroll
-  for (int j = 0; j < XS_CH; ++j) {
-    const int i = threadIdx.x + j * GV_THREADS;
-    v[j] = i < total ? __ldg(reinterpret_cast<const uint4 *>(x) + i) : make_uint4(0u, 0u, 0u, 0u);
-  }
-  {
-    float m[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < XS_CH; ++j) {
-      if (threadIdx.x + j * GV_THREADS < total) {
-        const int b = (threadIdx.x + j * GV_THREADS) / K8;
-        const uint32_t m2 = __vmaxu2(__vmaxu2(v[j].x & 0x7FFF7FFFu, v[j].y & 0x7FFF7FFFu),
-                                     __vmaxu2(v[j].z & 0x7FFF7FFFu, v[j].w & 0x7FFF7FFFu));
-        const float mm = fmaxf(bf_lo(m2), bf_hi(m2));
-#pragma unroll
-        for (int bb = 0; bb < 4; ++bb)
-          if (bb == b) m[bb] = fmaxf(m[bb], mm);
-      }
-    }
-#pragma unroll
-    for (int bb = 0; bb < 4; ++bb) {
-      const float w = warp_max(m[bb]);
-      if (lane == 0 && bb < B) red_max[bb][warp] = w;
-    }
-  }
-  __syncthreads();
-  int E[4], f1b[4], f2b[4];
-#pragma unroll
-  for (int bb = 0; bb < 4; ++bb) {
-    float amax = 0.f;
-    if (bb < B) {
-#pragma unroll
-      for (int w = 0; w < 8; ++w) amax = fmaxf(amax, red_max[bb][w]);
-    }
-    // amax < 2^(ex + 1) with ex its binary exponent (bf16 subnormals: below the smallest normal, ex = -126 bounds
-    // them); E = ex + 1 - QBITS. The scale 2^-E is applied as two exact power-of-two factors (it can exceed 2^127).
-    const int ex = amax > 0.f ? max(((__float_as_int(amax) >> 23) & 255) - 127, -126) : 0;
-    E[bb] = ex + 1 - QBITS;
-    const int ne1 = min(max(-E[bb], -126), 127), ne2 = -E[bb] - ne1;
-    f1b[bb] = (ne1 + 127) << 23;
-    f2b[bb] = (ne2 + 127) << 23;
-  }
-  if (threadIdx.x < B)
-    e_s[threadIdx.x] = threadIdx.x == 0 ? E[0] : (threadIdx.x == 1 ? E[1] : (threadIdx.x == 2 ? E[2] : E[3]));
-#pragma unroll
-  for (int j = 0; j < XS_CH; ++j) {
-    const int i = threadIdx.x + j * GV_THREADS;
-    if (i >= total) break;
-    const int b = i / K8, c = i - b * K8;
-    int fb1 = f1b[0], fb2 = f2b[0];
-#pragma unroll
-    for (int bb = 1; bb < 4; ++bb)
-      if (bb == b) {
-        fb1 = f1b[bb];
-        fb2 = f2b[bb];
-      }
-    const float f1 = __int_as_float(fb1), f2 = __int_as_float(fb2);
-    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-    uint32_t o[NSL][2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t acc[NSL];
-#pragma unroll
-      for (int sl = 0; sl < NSL; ++sl) acc[sl] = 0u;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float xv = (e & 1) ? bf_hi(w[2 * h + (e >> 1)]) : bf_lo(w[2 * h + (e >> 1)]);
-        int q = __float2int_rn(__fmul_rn(__fmul_rn(xv, f1), f2));  // exact scaling, one rounding
-#pragma unroll
-        for (int sl = 0; sl < NSL; ++sl) {
-          const int qs = ((q + 128) & 255) - 128;  // balanced byte: q = qs + 256 * q'
-          acc[sl] |= (uint32_t)(qs & 255) << (8 * e);
-          q = (q - qs) >> 8;
-        }
-      }
-#pragma unroll
-      for (int sl = 0; sl < NSL; ++sl) o[sl][h] = acc[sl];
-    }
-#pragma unroll
-    for (int sl = 0; sl < NSL; ++sl)
-      *reinterpret_cast<uint2 *>(xs + (size_t)(b * NSL + sl) * xstride + c * 8) = make_uint2(o[sl][0], o[sl][1]);
-  }
-}
-
-// Largest K the sliced path handles for B tokens (chunks held in registers by the 256 threads of a block)
-__host__ __device__ constexpr int xs_max_k(int B) { return 8 * GV_THREADS * XS_CH / (B > 0 ? B : 1); }
 
 // Weight-only GEMV on the int8 tensor path ("x-sliced"), for 1..8/NSL tokens. Each token's bf16 activations are
 // written exactly as NSL-byte fixed point, q = x * 2^-E with E from the token's absmax so that |q| < 2^(8 NSL - 2),
@@ -513,13 +202,14 @@ __host__ __device__ constexpr int xs_max_k(int B) { return 8 * GV_THREADS * XS_C
 template <int KS, int NSL, int RING>
 __global__ void __launch_bounds__(GV_THREADS) gemv_xs_kernel(const int8_t *__restrict__ W, const float *__restrict__ scale,
                                                              const bf16 *__restrict__ x, bf16 *__restrict__ y, int N,
-                                                             int K, int B, int pdl) {
+                                                             int K, int B, int pdl, const L2Prefetch pf) {
   constexpr int RG = 8 / KS;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x RING x 1 KB, then the sliced tokens
   __shared__ int red[RG * KS * 16 * 8];
   __shared__ int e_s[4];
   __shared__ float red_max[4][8];
   if (pdl == 2) pdl_trigger();
+  l2_prefetch_share(pf);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
@@ -770,19 +460,21 @@ cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStrea
   return launch_dyn(kernel, grid, block, pdl, st, GV_DYN_SMEM + extra_smem, args...);
 }
 
+const L2Prefetch kNoPrefetch = {};
+
 template <typename WT, int NT>
 cudaError_t gemv_ks(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
-                    cudaStream_t st) {
+                    cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
   const int groups = (N + 15) / 16, rg = 8 / ks;
   const int sets = (groups + rg - 1) / rg;
   const int resident = 4 * device_sm_count();  // 48 KB of rings per block: 4 blocks per SM
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
   switch (ks) {
-    case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
-    case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
-    case 4: return launch_ex(gemv_kernel<WT, NT, 4>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
-    default: return launch_ex(gemv_kernel<WT, NT, 8>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
+    case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
+    case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
+    case 4: return launch_ex(gemv_kernel<WT, NT, 4>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
+    default: return launch_ex(gemv_kernel<WT, NT, 8>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
   }
 }
 
@@ -798,14 +490,14 @@ int pick_ks(int N, int K, int kstep, int rows_override) {
 
 template <typename WT>
 cudaError_t gemv_dispatch(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int rows, int B,
-                          bool pdl, cudaStream_t st) {
+                          bool pdl, cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
   const int ks = pick_ks(N, K, WFmt<WT>::KSTEP, rows);
   for (int b0 = 0; b0 < B; b0 += 16) {
     const int bs = min(16, B - b0);
     const bf16 *xb = x + (size_t)b0 * K;
     bf16 *yb = y + (size_t)b0 * N;
-    const cudaError_t e = bs > 8 ? gemv_ks<WT, 2>(W, scale, xb, yb, N, K, bs, ks, pdl, st)
-                                 : gemv_ks<WT, 1>(W, scale, xb, yb, N, K, bs, ks, pdl, st);
+    const cudaError_t e = bs > 8 ? gemv_ks<WT, 2>(W, scale, xb, yb, N, K, bs, ks, pdl, st, b0 ? kNoPrefetch : pf)
+                                 : gemv_ks<WT, 1>(W, scale, xb, yb, N, K, bs, ks, pdl, st, b0 ? kNoPrefetch : pf);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -853,7 +545,7 @@ cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const
 
 template <int KS, int NSL>
 cudaError_t gemv_xs_launch(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
-                           cudaStream_t st) {
+                           cudaStream_t st, const L2Prefetch &pf) {
   auto kern = gemv_xs_kernel<KS, NSL, XS_RING>;
   const int groups = (N + 15) / 16, rg = 8 / KS;
   const int sets = (groups + rg - 1) / rg;
@@ -861,17 +553,17 @@ cudaError_t gemv_xs_launch(const int8_t *W, const float *scale, const bf16 *x, b
   const int resident = resident_blocks(kern, dyn);  // one wave: the grid strides over the sets
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
-  return launch_dyn(kern, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p);
+  return launch_dyn(kern, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
 }
 
 template <int NSL>
 cudaError_t gemv_xs_ks(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
-                       cudaStream_t st) {
+                       cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
   switch (ks) {
-    case 1: return gemv_xs_launch<1, NSL>(W, scale, x, y, N, K, B, pdl, st);
-    case 2: return gemv_xs_launch<2, NSL>(W, scale, x, y, N, K, B, pdl, st);
-    case 4: return gemv_xs_launch<4, NSL>(W, scale, x, y, N, K, B, pdl, st);
-    default: return gemv_xs_launch<8, NSL>(W, scale, x, y, N, K, B, pdl, st);
+    case 1: return gemv_xs_launch<1, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
+    case 2: return gemv_xs_launch<2, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
+    case 4: return gemv_xs_launch<4, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
+    default: return gemv_xs_launch<8, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
   }
 }
 
@@ -883,7 +575,6 @@ int gemv_xs_slices(int K, int B) {
   return nsl;
 }
 
-int gemv_device_error(bool) { return 0; }
 void gemv_set_early_trigger(bool early) { g_early_trigger = early; }
 void gemv_set_impl(int impl) { g_gemv_impl = impl; }
 
@@ -902,6 +593,19 @@ cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void
   if (int8)
     return gemv_dispatch<int8_t>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
   return gemv_dispatch<bf16>((const bf16 *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
+}
+
+// One GEMV of a chain: the x-sliced int8 path wherever its token buffer fits (the chain's contract: every layer gives
+// the sliced path's exact-product values), else the bf16 path; both issue the prefetch list first.
+cudaError_t launch_gemv_pf(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
+                           const L2Prefetch &pf, bool pdl, cudaStream_t st) {
+  if (N <= 0 || B <= 0) return cudaSuccess;
+  if (const int nsl = gemv_xs_slices(K, B)) {
+    const int ks = pick_ks(N, K, 64, 0);
+    return nsl == 3 ? gemv_xs_ks<3>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st, pf)
+                    : gemv_xs_ks<2>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st, pf);
+  }
+  return gemv_dispatch<int8_t>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, 0, B, pdl, st, pf);
 }
 
 cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,

@@ -23,7 +23,6 @@ cudaError_t launch_silu_mul_q(const void *g, int8_t *q, float *s, int rows, int 
 // gemv.cu
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st);
-int gemv_device_error(bool clear);
 // tuning: let dependents launch at kernel start (default: after the K loop)
 void gemv_set_early_trigger(bool early);
 void gemv_set_impl(int impl);
@@ -38,6 +37,29 @@ cudaError_t launch_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, c
 cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,
                             void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st);
 
+// Bulk L2 prefetch ranges a GEMV launch issues when it starts (before its dependency wait): every block requests its
+// share of each range into L2. Used by the chained GEMV to stream the weights of the layers ahead.
+struct L2Prefetch {
+  const void *p[8];
+  unsigned long long n[8];  // bytes, multiples of 16; p 16-byte aligned
+  int cnt;
+};
+
+// gemv_chain.cu: a list of weight-only int8 GEMVs, one PDL launch each, with an L2 prefetch window ahead of them
+constexpr int CHAIN_MAX = 96;
+constexpr int CHAIN_MAX_TOKENS = 4;
+struct ChainLayer {
+  const int8_t *W;      // int8 [N, K]
+  const float *scale;   // fp32 [N]
+  const uint16_t *x;    // bf16 [B, K]
+  uint16_t *y;          // bf16 [B, N]
+  int N, K;
+};
+cudaError_t launch_gemv_chain(const ChainLayer *layers, int n, int B, bool pdl, cudaStream_t st);
+// gemv.cu: one weight-only int8 GEMV of a chain (the x-sliced path where it applies, else the bf16 path)
+cudaError_t launch_gemv_pf(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
+                           const L2Prefetch &pf, bool pdl, cudaStream_t st);
+
 // gemm_tc.cu: tcgen05 W8A8 GEMMs
 enum GemmEpi { EPI_TOKEN = 0, EPI_GROUP = 1, EPI_GROUP_Q = 2, EPI_SILU = 3, EPI_W8 = 4 };
 cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias, void *Y,
@@ -48,10 +70,10 @@ cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *
                                 void *Y, int M, int I, int K, cudaStream_t st);
 int gemm_device_error(bool clear);
 cudaError_t launch_wait_timeout_selftest(int limit_log2, cudaStream_t st);  // sticky code written by a bounded wait that gave up (0 = none)
-void gemm_set_tile_override(int bn);
-void gemm_set_pdl(bool on);  // 0 = heuristic, 128 / 256 = force the per-token tile width
+void gemm_set_tile_override(int bn);  // 0 = heuristic, 128 / 256 = force the per-token tile width (< 0: CTA pairs)
+void gemm_set_pdl(bool on);            // GEMMs launch as programmatic dependents
 
-// gemm_w8.cu: tcgen05 W8A16 GEMM
+// gemm_tc.cu: tcgen05 W8A16 GEMM
 cudaError_t launch_gemm_w8(const void *A, const int8_t *B, const float *sb, const void *bias, void *Y, int M, int N,
                            int K, bool gelu, cudaStream_t st);
 

@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(QT) quant_kernel(const bf16 *__restrict__ x, i
   for (int i = 0; i < QC; ++i) {
     const int c = sub * 32 + lane + i * 32 * RW;
     if (live && c < K8) {
-      v[i] = ld_stream16(xr + c);
+      v[i] = ld_cg16(xr + c);
     } else {
       v[i] = make_uint4(0, 0, 0, 0);
     }

@@ -40,10 +40,17 @@ SIGNATURES = {
     "lfm2q_set_gemv_trigger": [_i],
     "lfm2q_set_gemv_path": [_i],
     "lfm2q_selftest_wait_timeout": [_i, _p],
+    "lfm2q_gemv_chain": [_p, _i, _i, _p],
 }
 _VOID = {"lfm2q_set_pdl", "lfm2q_set_gemv_impl", "lfm2q_set_gemm_tile", "lfm2q_set_gemv_trigger",
          "lfm2q_set_gemv_path"}
 _STR = {"lfm2q_last_error", "lfm2q_version"}
+
+
+class GemvLayer(ctypes.Structure):
+    """lfm2q_gemv_layer (include/lfm2q.h)."""
+
+    _fields_ = [("W", _p), ("scale", _p), ("x", _p), ("y", _p), ("N", _i), ("K", _i)]
 
 _LIB = None
 

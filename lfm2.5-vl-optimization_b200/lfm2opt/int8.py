@@ -26,14 +26,16 @@ from .quant import quantize_int8
 
 
 def a16_kinds():
-    """Layer kinds that keep BF16 activations (W8A16); the rest run W8A8."""
+    """The set of layer kinds named in LFM2_INT8_A16 (comma-separated): those layers take bf16 activations and int8
+    weights (W8A16); every other kind runs W8A8."""
     return set(filter(None, os.environ.get("LFM2_INT8_A16", "").split(",")))
 
 
 def act_group(kind=None, K=0):
-    """Activation scale granularity of a W8A8 layer: 64 = per token and group of 64 channels, 0 = per token.
-    LFM2_INT8_GROUP=64 / 0 sets it for every kind; LFM2_INT8_GROUP_KINDS="fc2,w2" limits the groups to those kinds
-    (the rest per token). Inputs wider than 2048 (fc2, w2) are grouped, as in the reference."""
+    """How finely a W8A8 layer's activations are scaled: 0 = one scale per token, 64 = one per token and 64-channel
+    slice of the input. LFM2_INT8_GROUP (0 or 64, default 64) chooses it; LFM2_INT8_GROUP_KINDS, a comma-separated
+    list of kinds, restricts the 64-wide scales to those kinds. Layers with K > 2048 always get 64-wide scales,
+    which is the reference's rule (its per-token quantizer stops at K = 2048)."""
     g = int(os.environ.get("LFM2_INT8_GROUP", "64"))
     if g not in (0, 64):
         raise ValueError("LFM2_INT8_GROUP must be 0 or 64: the kernel folds one scale per 64-wide K group")
@@ -44,13 +46,15 @@ def act_group(kind=None, K=0):
 
 
 def qbuf(rows, K, group, device):
-    """Empty (int8 [rows, K], scales) for a producer kernel that writes a W8A8 layer's input directly."""
+    """Uninitialised output buffers for a kernel that writes a W8A8 layer's quantized input itself: int8 [rows, K]
+    codes and fp32 scales, [rows] for group 0 or [K / 64, rows] for group 64."""
     return (torch.empty(rows, K, device=device, dtype=torch.int8),
             torch.empty((K // 64, rows) if group else (rows,), device=device, dtype=torch.float32))
 
 
 def quantize_rows(x2, group=0):
-    """[M, K] bf16 -> (int8 [M, K], fp32 scales): [M] (absmax / 127 per row) or, group=64, [K / 64, M]."""
+    """Quantize bf16 activations x2 [M, K] to int8 on the GPU. Returns (codes int8 [M, K], fp32 scales): with
+    group 0 one scale per row, [M] (row absmax / 127); with group 64 one per row and 64 columns, laid out [K / 64, M]."""
     M, K = x2.shape
     q = torch.empty(x2.shape, device=x2.device, dtype=torch.int8)
     s = torch.empty((K // 64, M) if group else (M,), device=x2.device, dtype=torch.float32)
@@ -60,9 +64,11 @@ def quantize_rows(x2, group=0):
 
 class Int8Linear:
     def __init__(self, weight=None, bias=None, a8=True, q=None, scale=None, pad_n=0, pad_k=0, kind=None, group=None):
-        """From a BF16 weight [N, K] (quantized here), or from an already quantized (q, scale) pair. pad_n / pad_k
-        append zero output rows (and zero bias) / zero input columns, e.g. to make K a multiple of 128 for the
-        grouped activation scales (SigLIP2's 4304-wide MLP -> 4352: fc1 pad_n=48, fc2 pad_k=48)."""
+        """Build the layer either from a bf16 weight [N, K], which is quantized per output row here, or from an
+        already quantized pair (q int8 [N, K], scale fp32 [N]). pad_n adds zero weight rows (and zero bias) at the
+        end, pad_k zero input columns, before quantizing; the grouped activation scales need K % 128 == 0, so a
+        4304-wide layer is padded to 4352 (pad_n=48 on the layer that produces it, pad_k=48 on the one that reads
+        it). kind names the layer for LFM2_INT8_A16 / LFM2_INT8_GROUP_KINDS; group overrides act_group."""
         if q is None:
             weight = torch.nn.functional.pad(weight, (0, pad_k, 0, pad_n))
             if bias is not None and pad_n:
@@ -76,10 +82,12 @@ class Int8Linear:
         self.ext = int8_ext()
 
     def __call__(self, x, gelu=False, quant_out=False, silu_gate=False):
-        """x: bf16 [..., K], or an already quantized (int8 [..., K], scales) pair from a fused producer kernel.
-        quant_out: return the output as the next W8A8 GEMM's input (int8 [M, N], scales [N/64, M]), quantized inside
-        this GEMM's epilogue (grouped W8A8 only, N % 128 == 0).
-        silu_gate: the weight is [w1 | w3]; return bf16(bf16(silu(g)) * u) [..., N/2] (per-token W8A8 only)."""
+        """Apply the layer. x is bf16 [..., K] or, when a producer kernel already quantized it, the pair
+        (int8 [..., K], scales) that kernel wrote. Returns bf16 [..., N] with GELU applied when gelu is set.
+        quant_out: return the result already quantized for the next W8A8 layer, (int8 [M, N], scales [N/64, M]),
+        from this GEMM's epilogue (grouped W8A8 only, N % 128 == 0).
+        silu_gate: the weight rows are [w1 | w3]; returns bf16(bf16(silu(g)) * u) [..., N/2] from one GEMM (per-token
+        W8A8 only: a layer built with a8=False or with 64-wide activation scales raises ValueError)."""
         if quant_out:
             xq, sx = x if isinstance(x, tuple) else quantize_rows(x.reshape(-1, self.K).contiguous(), 64)
             M = xq.numel() // self.K
@@ -89,6 +97,9 @@ class Int8Linear:
         if silu_gate:
             if gelu:
                 raise ValueError("silu_gate and gelu are exclusive epilogues")
+            if not self.a8 or self.group != 0:
+                raise ValueError("silu_gate runs the per-token W8A8 epilogue: build the layer with a8=True and "
+                                 "group=0 (it has " + ("a8=False" if not self.a8 else f"group={self.group}") + ")")
             if isinstance(x, tuple):
                 xq, sx = x
                 lead = xq.shape[:-1]

@@ -1,4 +1,4 @@
-"""The two extension objects the reference loads (src/lfm2opt/kernels.py:178-230 of the reference), backed by the
+"""The two extension objects the reference loads (src/lfm2opt/kernels.py:16-68 of the reference), backed by the
 prebuilt sm_100a library liblfm2q.so instead of a JIT build.
 
     int8_ext()  ops of the reference's lfm2_int8_gemm extension (kernels/int8_gemm.cpp:143-151):
@@ -13,6 +13,7 @@ stream of the tensors' device and returns None. The decode extension's non-GEMV 
 norms) are not part of this library; reaching for them raises AttributeError.
 """
 
+import ctypes
 import os
 
 import torch
@@ -305,6 +306,50 @@ class DecodeGemvExt:
     def set_gemv_impl(self, impl):
         """Accepted for compatibility with the reference (0 = staged x, 1 = direct x); this build has one GEMV."""
         _capi.lib().lfm2q_set_gemv_impl(int(impl))
+
+
+class GemvChain:
+    """A fixed list of int8 weight-only decode GEMVs run in order (lfm2q_gemv_chain, include/lfm2q.h): the run of gemv
+    calls a decode step makes back to back, with the weights of the layers ahead streamed into L2 meanwhile.
+
+    layers: sequence of (W int8 [N, K], scale fp32 [N], x bf16 [B, K], y bf16 [B, N]) with one B (1..4) for all; a
+    layer's x may be an earlier layer's y. The tensors are referenced, not copied: calling the chain reads the current
+    contents of every x and writes every y, on the current stream (capturable in a CUDA graph)."""
+
+    def __init__(self, layers):
+        layers = list(layers)
+        _req(1 <= len(layers) <= 96, "a chain holds 1 to 96 layers")
+        B = layers[0][2].shape[0]
+        _req(1 <= B <= 4, "x [B, K]: the chained GEMV takes 1 <= B <= 4 tokens")
+        arr = (_capi.GemvLayer * len(layers))()
+        for i, (W, scale, x, y) in enumerate(layers):
+            _check(W, _I8, "W")
+            _check(scale, _F32, "scale")
+            _check(x, _BF, "x")
+            _check(y, _BF, "y")
+            _req(W.dim() == 2, "W must be [N, K]")
+            N, K = W.shape
+            _req(K % 512 == 0, f"layer {i}: K must be a multiple of 512")
+            _req(x.dim() == 2 and x.shape == (B, K), f"layer {i}: x must be [B, K] with the chain's B")
+            _req(y.numel() == B * N and scale.numel() == N, f"layer {i}: y / scale shape")
+            _req(W.device == x.device == y.device == scale.device == layers[0][0].device, "one device for all")
+            arr[i] = _capi.GemvLayer(W.data_ptr(), scale.data_ptr(), x.data_ptr(), y.data_ptr(), N, K)
+        self.B, self.n, self.arr = B, len(layers), arr
+        self.device = layers[0][0].device
+        self._keep = layers  # the launches read these pointers
+
+    def __call__(self):
+        with _DeviceOf(self._keep[0][0]):
+            _capi.call("lfm2q_gemv_chain", ctypes.cast(self.arr, ctypes.c_void_p), self.n, self.B,
+                       torch.cuda.current_stream(self.device).cuda_stream)
+
+
+def check_device(clear=False):
+    """Raise RuntimeError if a bounded pipeline wait inside a tcgen05 GEMM gave up since the last clear (the outputs of
+    that work are then invalid). Synchronises with the current device. clear: reset the word."""
+    st = _capi.lib().lfm2q_check_device(int(bool(clear)))
+    if st != _capi.OK:
+        raise RuntimeError(_capi.lib().lfm2q_last_error().decode() or f"lfm2q_check_device: status {st}")
 
 
 _INT8 = None

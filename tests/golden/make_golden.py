@@ -14,6 +14,7 @@ stand-in captures the reference tensors the test computes (its locals), which be
 """
 
 import argparse
+import os
 import ast
 import sys
 from pathlib import Path
@@ -86,8 +87,11 @@ def t2np(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("LFM2_REFERENCE"),
+                    help="the reference project's source tree (or set LFM2_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("name the reference's source tree with --reference or LFM2_REFERENCE")
     ref = Path(a.reference)
     sys.path.insert(0, str(ref / "src"))
     import lfm2opt.quant as rq  # the reference's own module

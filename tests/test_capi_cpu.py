@@ -96,3 +96,23 @@ def test_selftest_rejects_bad_limits():
     L = _capi.lib()
     assert L.lfm2q_selftest_wait_timeout(5, None) == _capi.EINVAL
     assert L.lfm2q_selftest_wait_timeout(40, None) == _capi.EINVAL
+
+
+def test_gemv_chain_rejects_bad_layers_without_a_gpu():
+    """lfm2q_gemv_chain validates every layer on the host before touching a device."""
+    L = _capi.lib()
+    fake = ctypes.c_void_p(1 << 20)
+    ok = _capi.GemvLayer(1 << 20, 1 << 20, 2 << 20, 3 << 20, 256, 2048)
+    arr = (_capi.GemvLayer * 2)(ok, ok)
+    assert L.lfm2q_gemv_chain(arr, 0, 1, None) == _capi.EINVAL  # no layers
+    assert L.lfm2q_gemv_chain(arr, 97, 1, None) == _capi.EINVAL  # too many
+    assert L.lfm2q_gemv_chain(arr, 2, 5, None) == _capi.EINVAL  # B > 4
+    assert L.lfm2q_gemv_chain(None, 1, 1, None) == _capi.EINVAL
+    arr[1] = _capi.GemvLayer(1 << 20, 1 << 20, 2 << 20, 3 << 20, 256, 2000)  # K % 512
+    assert L.lfm2q_gemv_chain(arr, 2, 1, None) == _capi.EINVAL
+    assert b"layer 1" in L.lfm2q_last_error()
+    arr[1] = _capi.GemvLayer(1 << 20, 1 << 20, 2 << 20, (2 << 20) + 64, 256, 2048)  # y overlaps x
+    assert L.lfm2q_gemv_chain(arr, 2, 1, None) == _capi.EINVAL
+    arr[1] = _capi.GemvLayer(1 << 20, 1 << 20, (2 << 20) + 8, 3 << 20, 256, 2048)  # x not 16-byte aligned
+    assert L.lfm2q_gemv_chain(arr, 2, 1, None) == _capi.EINVAL
+    del fake
