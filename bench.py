@@ -5,7 +5,7 @@ Metric: INT8 GEMM TOPS (% of B200 peak); decode GEMV HBM GB/s (%
 
 One step = the BASELINE config-5 job ("large-M batched throughput"), total work fixed, split over the ranks:
   vision  65536 tokens x 27 SigLIP2 layers x {qkv 1152->3456 +bias, o 1152->1152 +bias, fc1 1152->4304 +bias +GELU,
-          fc2 4304->1152 +bias}
+          fc2 4304->1152 +bias} (the MLP laid out 4352 wide with zero padding, as the reference does)
   LM      65536 tokens x 16 LFM2 layers (10 conv: in 2048->6144, out 2048->2048; 6 attention: qkv 2048->3072,
           o 2048->2048; every layer: w1|w3 2048->16384 with the SiLU gate fused (-> 8192), w2 8192->2048)
   head    lm_head 2048->65536 at M = 4096, N-split over the ranks, chunked NCCL all-gather of the bf16 logits
@@ -52,6 +52,11 @@ VISION_LAYERS, LM_LAYERS = 27, 16
 ATTN_LAYERS = {2, 5, 8, 10, 12, 14}  # 6 GQA blocks among the 16; the other 10 are gated short-conv blocks
 VISION = [("v.qkv", 1152, 3456, True, "none"), ("v.o", 1152, 1152, True, "none"),
           ("v.fc1", 1152, 4304, True, "gelu"), ("v.fc2", 4304, 1152, True, "none")]
+# SigLIP2's 4304-wide MLP is laid out 4352 wide, as the reference does for it (Int8Linear pad_n / pad_k,
+# src/lfm2opt/vision.py:69-73): fc1 gets 48 zero weight rows (zero outputs), fc2 48 zero input columns. The results
+# are those of the 4304-wide layers; rows of 4352 bytes keep every TMA row on 128-byte boundaries (4304-byte rows ran
+# 18 % slower, measured). The job's operation count uses the unpadded shapes.
+VISION_PAD = {"v.fc1": (48, 0), "v.fc2": (0, 48)}  # name -> (pad_n, pad_k)
 LM_CONV = [("l.in", 2048, 6144), ("l.out", 2048, 2048)]
 LM_ATTN = [("l.qkv", 2048, 3072), ("l.o", 2048, 2048)]
 LM_MLP = [("l.w13", 2048, 16384), ("l.w2", 8192, 2048)]
@@ -215,9 +220,11 @@ class Job:
         self.hs = head_shard(HEAD[2], world, rank)
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
 
-        def weight(N, K, seed):
+        def weight(N, K, seed, pad_n=0, pad_k=0):
             gw = torch.Generator(device=dev).manual_seed(seed)
             w = (torch.randn(N, K, generator=gw, device=dev) * 0.02).to(torch.bfloat16)
+            if pad_n or pad_k:
+                w = torch.nn.functional.pad(w, (0, pad_k, 0, pad_n))
             q, s = quantize_int8(w)
             del w
             return q, s
@@ -230,8 +237,11 @@ class Job:
             return x
 
         # weights: distinct per layer (the step streams ~1.5 GB of weights, far more than L2)
-        self.vw = [[weight(N, K, 100 * l + j) for j, (_, K, N, _, _) in enumerate(VISION)] for l in range(VISION_LAYERS)]
-        self.vb = [(torch.randn(N, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _, K, N, _, _ in VISION]
+        self.vw = [[weight(N, K, 100 * l + j, *VISION_PAD.get(n, (0, 0))) for j, (n, K, N, _, _) in enumerate(VISION)]
+                   for l in range(VISION_LAYERS)]
+        self.vb = [torch.nn.functional.pad((torch.randn(N, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+                                           (0, VISION_PAD.get(n, (0, 0))[0]))
+                   for n, K, N, _, _ in VISION]
         self.lw = []
         for l in range(LM_LAYERS):
             mix = LM_ATTN if l in ATTN_LAYERS else LM_CONV
@@ -241,7 +251,7 @@ class Job:
         del hq, hsc
         # activations: one input per distinct K (all > L2: 151 MB .. 1 GB at N = 1), outputs per shape
         self.xv = act(self.vrows, 1152, False)
-        self.xv2 = act(self.vrows, 4304, False)
+        self.xv2 = torch.nn.functional.pad(act(self.vrows, 4304, False), (0, VISION_PAD["v.fc2"][1]))
         self.xl = act(self.lrows, 2048, True)
         self.xl2 = act(self.lrows, 8192, True)
         self.xh = act(HEAD_M, 2048, True)
@@ -259,8 +269,8 @@ class Job:
             self.q[key] = torch.empty(*shape, device=self.dev, dtype=dtype)
         return self.q[key]
 
-    def _linear(self, x, wq, sw, bias, N, epi, tag):
-        """quant_rows + gemm launches for y = linear(x) (per token)."""
+    def _linear(self, x, wq, sw, bias, N, epi, tag, ops=None):
+        """quant_rows + gemm launches for y = linear(x) (per token). ops: the algorithmic 2*M*N*K (unpadded)."""
         rows, K = x.shape
         xq = self._buf(("xq", rows, K), (rows, K), torch.int8)
         sx = self._buf(("sx", rows, K), (rows,), torch.float32)
@@ -270,7 +280,7 @@ class Job:
         shape = tag[:4] if tag.startswith("head") else tag
         self.calls.append(("quant", 0, self.L.lfm2q_quant_rows, (x.data_ptr(), xq.data_ptr(), sx.data_ptr(), rows, K, st),
                            shape))
-        ops = 2 * rows * N * K
+        ops = 2 * rows * N * K if ops is None else ops
         bp = bias.data_ptr() if bias is not None else None
         if epi == "silu":
             self.calls.append(("gemm", ops, self.L.lfm2q_gemm_i8_silu,
@@ -287,7 +297,8 @@ class Job:
         for l in range(VISION_LAYERS):
             for j, (name, K, N, _, epi) in enumerate(VISION):
                 x = self.xv if K == 1152 else self.xv2
-                self._linear(x, *self.vw[l][j], self.vb[j], N, epi, name)
+                wq, sw = self.vw[l][j]
+                self._linear(x, wq, sw, self.vb[j], wq.shape[0], epi, name, ops=2 * self.vrows * N * K)
         for l in range(LM_LAYERS):
             mix = LM_ATTN if l in ATTN_LAYERS else LM_CONV
             for j, (name, K, N) in enumerate(mix + LM_MLP):

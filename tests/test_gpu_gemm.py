@@ -228,3 +228,32 @@ def test_gemm_w8(cuda_dev, w8_tile, M, K, N, bias, gelu):
             rc = torch.nn.functional.gelu(rc, approximate="tanh")
         e_cub = ((rc.to(BF).double() - r64).norm() / r64.norm()).item()
         assert e_ours <= 1.5 * e_cub + 1e-4, (e_ours, e_cub)
+
+
+@pytest.mark.parametrize("epi", ["none", "gelu", "silu"])
+def test_gemm_i8_accumulators_beyond_2p22(cuda_dev, epi):
+    """Rows whose int32 sums reach 127 * 127 * K (all codes +-127), far beyond 2^24: (float)acc must round to nearest
+    even exactly as the oracle's float(acc) does, in every epilogue."""
+    M, K, N = 300, 2048, 1024
+    g = torch.Generator().manual_seed(77)
+    x = torch.randn(M, K, generator=g)
+    x[::3] = 1.0          # every third row quantizes to 127 everywhere
+    x[1::3] = torch.sign(torch.randn(K, generator=g))  # +-1 rows: +-127
+    x = x.to(BF)
+    w = (torch.randn(N, K, generator=g) * 0.02)
+    w[: N // 4] = 0.02    # a quarter of the weight rows quantize to 127 everywhere
+    w = w.to(BF)
+    wq, sw = quantize_int8(w)
+    b = (torch.randn(N, generator=g) * 0.1).to(BF)
+    xq, sx = oracle.quant_rows_ref(x)
+    assert int(oracle.int_mm_exact(xq, wq).abs().max()) >= 1 << 22
+    dev = cuda_dev
+    if epi == "silu":
+        y = torch.empty(M, N // 2, device=dev, dtype=BF)
+        int8_ext().gemm_i8_silu(xq.to(dev), sx.to(dev), wq.to(dev), sw.to(dev), b.to(dev), y)
+        ok, detail = oracle.silu_chain_close(y.cpu(), oracle.gemm_i8_silu_ref(xq, sx, wq, sw, b))
+        assert ok, detail
+    else:
+        y = torch.empty(M, N, device=dev, dtype=BF)
+        int8_ext().gemm_i8(xq.to(dev), sx.to(dev), wq.to(dev), sw.to(dev), b.to(dev), y, epi == "gelu")
+        assert_close_bf16(y.cpu(), oracle.gemm_i8_ref(xq, sx, wq, sw, b, epi == "gelu"), epi == "gelu")

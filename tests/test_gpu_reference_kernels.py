@@ -258,6 +258,39 @@ def test_silu_gate_equals_reference_composition(cuda_dev, refk, M, K, I, gate_bi
     assert torch.equal(y, ry), f"{(y != ry).sum().item()} of {y.numel()} outputs differ"
 
 
+def test_silu_gate_every_table_value_equals_reference(cuda_dev, refk):
+    """The fused SiLU epilogue evaluates bf16(silu(g)) from a table for 2^-8 <= |g| < 2^8 and directly elsewhere. With
+    all-zero activations every gate equals its bias, so the bias enumerates every bf16 value the table holds (both
+    signs, 16 binades x 128 mantissas) and a spread outside it (zero, subnormal, tiny, large, around -88); the result
+    must equal the reference's gemm_i8 -> silu_mul composition bit for bit. The up half is 1, so y = bf16(silu(g))."""
+    table = [((s << 15) | (e << 7) | m) for s in (0, 1) for e in range(119, 135) for m in range(128)]
+    extra = [0x0000, 0x8000, 0x0001, 0x8001, 0x0080, 0x3B00, 0xBB00, 0x3BFF, 0xBBFF, 0x4380, 0xC380, 0x43FF, 0xC3FF,
+             0x4700, 0xC2B0, 0xC2B1, 0xC2AF, 0xC2B2, 0xC2C0, 0x7F7F, 0xFF7F]
+    g = torch.Generator().manual_seed(13)
+    rand = torch.randint(0, 0x7F80, (8192 - len(table) - len(extra),), generator=g)
+    rand = rand | (torch.randint(0, 2, rand.shape, generator=g) << 15)
+    bits = torch.tensor(table + extra, dtype=torch.int32)
+    bits = torch.cat([bits, rand.to(torch.int32)])
+    I, K, M = bits.numel(), 64, 3
+    gate_bias = bits.to(torch.int16).view(BF)
+    b = torch.cat([gate_bias, torch.ones(I, dtype=BF)]).to(cuda_dev)
+    x = torch.zeros(M, K, dtype=BF, device=cuda_dev)
+    w = (torch.randn(2 * I, K, generator=g) * 0.02).to(BF)
+    wq, sw = quantize_int8(w)
+    wq, sw = wq.to(cuda_dev), sw.to(cuda_dev)
+    xq, sx = quantize_rows(x)
+    y = torch.empty(M, I, device=cuda_dev, dtype=BF)
+    int8_ext().gemm_i8_silu(xq, sx, wq, sw, b, y)
+    gu = torch.empty(M, 2 * I, device=cuda_dev, dtype=BF)
+    call(refk.refk_gemm_i8(ptr(xq), ptr(sx), ptr(wq), ptr(sw), ptr(b), ptr(gu), M, 2 * I, K, 0, 0, stream()))
+    ry = torch.empty_like(y)
+    call(refk.refk_silu_mul(ptr(gu), ptr(ry), M, I, stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(gu[:, :I].cpu(), gate_bias.expand(M, I)), "gates are the biases"
+    bad = (y != ry).any(0).nonzero().flatten()
+    assert bad.numel() == 0, [hex(int(bits[i]) & 0xFFFF) for i in bad[:10]]
+
+
 def _time(fn, reps=10):
     for _ in range(3):
         fn()
