@@ -647,29 +647,44 @@ GEMV_SHAPES = [("qkv", 3072, 2048), ("o_proj", 2048, 2048), ("conv_in", 6144, 20
                ("w1w3", 16384, 2048), ("w2", 2048, 8192), ("lm_head", 65536, 2048)]
 
 
-def gemv_shape_sweep(dev, world, batches=(1, 2, 4, 8, 16), per=20, replays=5):
-    """BASELINE config 2 shape by shape: the weight-only GEMV (lfm2q_gemv, the reference's gemv semantics) at every
-    decode shape and batch, each timed as a CUDA graph of `per` launches cycling through enough distinct weight copies
-    (>= 400 MB, more than 3x L2) that every launch streams its weights from HBM, as the reference's
-    profiling/bench_gemv.py:40 does. Replicas on every rank; GB/s = (N*K + 4N + 2BK + 2BN) / per-launch time."""
+def gemv_shape_sweep(dev, world, batches=(1, 2, 4, 8, 16), per=20, replays=5, int4=False):
+    """BASELINE config 2 shape by shape: the weight-only GEMV (lfm2q_gemv, the reference's gemv semantics; with int4,
+    lfm2q_gemv_w4 on group-128 INT4 weights, B <= 4) at every decode shape and batch, each timed as a CUDA graph of
+    `per` launches cycling through enough distinct weight copies (>= 400 MB, more than 3x L2) that every launch streams
+    its weights from HBM, as the reference's profiling/bench_gemv.py:40 does. Replicas on every rank; GB/s = bytes
+    per launch / time, bytes = weights (N*K, INT4: N*K/2 + 4*N*K/128 of scales) + 4N + 2BK + 2BN."""
+    from lfm2opt import _capi
     from lfm2opt.kernels import ext
 
     E = ext()
+    L = _capi.lib()
     hbm = load_peaks().get("hbm_gbs")
     g = torch.Generator(device=dev).manual_seed(31)
     out = {}
     for name, N, K in GEMV_SHAPES:
-        copies = max(2, -(-400 * 10 ** 6 // (N * K)))
-        Ws = [torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8) for _ in range(copies)]
-        s = torch.rand(N, generator=g, device=dev) * 1e-3 + 1e-4
+        wbytes = N * K // 2 + 4 * N * (K // 128) if int4 else N * K
+        copies = max(2, -(-400 * 10 ** 6 // wbytes))
+        if int4:
+            Ws = [(torch.randint(0, 256, (N, K // 2), generator=g, device=dev, dtype=torch.uint8),
+                   torch.rand(N, K // 128, generator=g, device=dev) * 1e-2 + 1e-3) for _ in range(copies)]
+        else:
+            Ws = [(torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8),
+                   torch.rand(N, generator=g, device=dev) * 1e-3 + 1e-4) for _ in range(copies)]
         out[name] = {}
         for B in batches:
+            if int4 and B * K > 16384:
+                continue
             x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
             y = torch.empty(B, N, device=dev, dtype=torch.bfloat16)
 
             def burst():
+                st = torch.cuda.current_stream(dev).cuda_stream
                 for i in range(per):
-                    E.gemv(Ws[i % copies], s, x, y)
+                    W, s = Ws[i % copies]
+                    if int4:
+                        L.lfm2q_gemv_w4(W.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 128, B, st)
+                    else:
+                        E.gemv(W, s, x, y)
 
             st = torch.cuda.Stream(dev)
             st.wait_stream(torch.cuda.current_stream(dev))
@@ -689,7 +704,7 @@ def gemv_shape_sweep(dev, world, batches=(1, 2, 4, 8, 16), per=20, replays=5):
             e1.record()
             torch.cuda.synchronize()
             us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (replays * per), world)
-            nbytes = N * K + 4 * N + 2 * B * K + 2 * B * N
+            nbytes = wbytes + 4 * N + 2 * B * K + 2 * B * N
             gbs = nbytes / (us * 1e-6) / 1e9
             out[name][str(B)] = {"us": round(us, 2), "gbs_per_gpu": round(gbs, 1),
                                  "frac_hbm": round(gbs / hbm, 4) if hbm else None}
@@ -1046,10 +1061,11 @@ def main():
     if dev_err:
         vdetail["device_error_word"] = "set: a bounded pipeline wait gave up"
 
-    gemv = gemv_shapes = None
+    gemv = gemv_shapes = gemv_shapes_w4 = None
     if not a.no_gemv:
         gemv = gemv_sweep(dev, world, rank)
         gemv_shapes = gemv_shape_sweep(dev, world)
+        gemv_shapes_w4 = gemv_shape_sweep(dev, world, batches=(1, 2, 4), int4=True)
 
     peaks = load_peaks()
     hbm = peaks.get("hbm_gbs")
@@ -1080,7 +1096,8 @@ def main():
                         "hbm_peak_gbs": hbm,
                         "frac_b1": {m: round(v / hbm, 4) for m, v in b1.items()} if hbm else None,
                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured copy bandwidth)",
-                        "per_shape_w16": gemv_shapes}
+                        "per_shape_w16": gemv_shapes,
+                        "per_shape_int4": gemv_shapes_w4}
         else:
             gemv_out = None
         out = {

@@ -120,6 +120,15 @@ int lfm2q_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, const floa
 int lfm2q_linear_a8(const uint16_t *x, const int8_t *W, const float *sw, const uint16_t *bias, uint16_t *y, int N,
                     int K, int B, int gelu, void *stream);
 
+/* Replaces launch_gemv_w4 (kernels/lfm2_decode.cu:938-945) behind gemv_w4 (kernels/lfm2_decode.cpp:87-98).
+ * INT4 weight-only GEMV: Wp uint8 [N, K/2], byte j of a row holding inputs 2j (low nibble) and 2j + 1 (high nibble),
+ * each stored as q + 8, q in [-8, 7]; S fp32 [N, K / group], one scale per row and group of `group` inputs
+ * (lfm2opt.quant.quantize_int4). y bf16 [B, N] = bf16(sum_g S[n, g] * (x . q)_g). x bf16 [B, K], 1 <= B <= 4 (the
+ * reference: batch 1). Needs group % 128 == 0 (the reference: % 32; its models use 128), K % group == 0,
+ * B * K <= 16384. */
+int lfm2q_gemv_w4(const uint8_t *Wp, const float *S, const uint16_t *x, uint16_t *y, int N, int K, int group, int B,
+                  void *stream);
+
 /* ------------------------------------------------------------------ chained decode GEMV
  * No single counterpart in the reference: it replaces a run of gemv launches (kernels/lfm2_decode.cu:708-714 behind
  * gemv, kernels/lfm2_decode.cpp:73-85) that the reference's decode step issues back to back inside its captured

@@ -286,6 +286,18 @@ int lfm2q_gemv_chain(const lfm2q_gemv_layer *layers, int n_layers, int B, void *
   return launched(launch_gemv_chain(L.data(), n_layers, B, g_pdl.load(), (cudaStream_t)stream), "gemv_chain");
 }
 
+int lfm2q_gemv_w4(const uint8_t *Wp, const float *S, const uint16_t *x, uint16_t *y, int N, int K, int group, int B,
+                  void *stream) {
+  REQUIRE(N > 0 && K > 0 && B >= 1 && B <= 4, "Wp [N, K/2], x [B, K]: need N > 0, K > 0, 1 <= B <= 4");
+  REQUIRE(group > 0 && group % 128 == 0 && K % group == 0, "group size must be a multiple of 128 dividing K");
+  REQUIRE(Wp && S && x && y, "Wp, S, x and y must be non-null");
+  REQUIRE(aligned16(Wp) && aligned16(x), "Wp and x must be 16-byte aligned");
+  REQUIRE(gemv_w4_slices(K, B) != 0, "K too large for this batch (B * K <= 16384 and the token slices in 160 KB)");
+  if (int e = device_gate()) return e;
+  return launched(launch_gemv_w4(Wp, S, x, y, N, K, group, B, g_pdl.load(), gemv_trigger_mode(), (cudaStream_t)stream),
+                  "gemv_w4");
+}
+
 int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int S,
                    int K, uint16_t *state, const uint16_t *cw, const uint16_t *cbias, void *stream) {
   REQUIRE(epi == 0 || epi == 1, "epi 0 (swiglu) or 1 (shortconv)");

@@ -576,6 +576,7 @@ int gemv_xs_slices(int K, int B) {
 }
 
 void gemv_set_early_trigger(bool early) { g_early_trigger = early; }
+int gemv_trigger_mode() { return g_early_trigger ? 2 : 1; }
 void gemv_set_impl(int impl) { g_gemv_impl = impl; }
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,

@@ -245,7 +245,9 @@ __device__ __forceinline__ int frag_tok(int lane, int j, int e) { return 8 * j +
 // reduction, XS_CH chunks per thread and token at most: K <= 8 * 256 * XS_CH / B); the block is synchronised inside
 // and the caller synchronises again before reading the slices.
 constexpr int XS_CH = 8;
-template <int NSL>
+// EO: within every 8-element chunk the bytes are stored in the order of the elements 0, 2, 4, 6, 1, 3, 5, 7 (the
+// order in which the INT4 GEMV unpacks a word of packed nibbles: low nibbles, then high nibbles).
+template <int NSL, bool EO = false>
 __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride, int *e_s,
                                              float (&red_max)[4][8]) {
   constexpr int QBITS = 8 * NSL - 2;  // |q| < 2^QBITS
@@ -319,7 +321,9 @@ __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, 
       for (int sl = 0; sl < NSL; ++sl) acc[sl] = 0u;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float xv = (e & 1) ? bf_hi(w[2 * h + (e >> 1)]) : bf_lo(w[2 * h + (e >> 1)]);
+        // element 4h + e (EO: 2e + h) of the chunk
+        const float xv = EO ? (h ? bf_hi(w[e]) : bf_lo(w[e]))
+                            : ((e & 1) ? bf_hi(w[2 * h + (e >> 1)]) : bf_lo(w[2 * h + (e >> 1)]));
         int q = __float2int_rn(__fmul_rn(__fmul_rn(xv, f1), f2));  // exact scaling, one rounding
 #pragma unroll
         for (int sl = 0; sl < NSL; ++sl) {

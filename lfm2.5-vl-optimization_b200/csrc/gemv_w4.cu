@@ -1,0 +1,242 @@
+// INT4 weight-only decode GEMV: y[b, n] = bf16( sum_g s[n, g] * sum_{k in g} q[n, k] x[b, k] ), q in [-8, 7] with one
+// fp32 scale per group of `group` inputs along K.
+//
+// Reference: gemv_w4_kernel / launch_gemv_w4 (kernels/lfm2_decode.cu:829-945), binding gemv_w4
+// (kernels/lfm2_decode.cpp:87-98), packing quantize_int4 (src/lfm2opt/quant.py:22-40): Wp [N, K/2] bytes, element 2j
+// in the low nibble and 2j + 1 in the high nibble of byte j, each stored as q + 8; S [N, K / group] fp32.
+//
+// B200 design: the int8 tensor path of the x-sliced weight-only GEMV (gemv.cu), fed with nibbles. The tokens are
+// written once per block into shared memory as exact NSL-byte fixed point (x = q_x * 2^E, q_x = sum_s q_s 256^s),
+// so every partial sum is an exact int32 and the weights go to the MMA without any conversion to floating point:
+//   - a warp step is 16 weight rows x 128 inputs = 64 packed bytes per row (the same 1 KB cp.async ring slots as the
+//     int8 GEMV), lane (g, t) holding 16 packed bytes = 32 inputs of rows g and g + 8;
+//   - a word of 4 packed bytes (8 inputs) becomes two MMA words with two masks and a shift: the low nibbles (the
+//     even inputs) and the high nibbles (the odd inputs) as bytes u = q + 8 in 0..15. The token slices are stored
+//     in the same order (slice_tokens<NSL, EO = true>), so each MMA pairs every u with its own x;
+//   - sum_k q x = sum_k u x - 8 sum_k x: the group sums of every token slice are computed once per block, so the
+//     +8 is removed exactly from each group's int32 partial, which then folds into the fp32 result with the group's
+//     scale: f += (float)(A - 8 C) * s[n, g]. |A - 8 C| < 2^19, so the conversion is exact.
+// One 128-input step is one group-128 block; groups of 256, 384, ... fold every group / 128 steps (group must be a
+// multiple of 128: one MMA spans inputs from all four 32-input blocks of a step).
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "gemv_core.cuh"
+#include "launch.h"
+
+namespace lfm2q {
+namespace {
+
+constexpr int W4_RING = 6;  // K steps (1 KB of packed weights each) a warp keeps in flight
+
+template <int KS, int NSL>
+__global__ void __launch_bounds__(GV_THREADS) gemv_w4_kernel(const uint8_t *__restrict__ Wp, const float *__restrict__ S,
+                                                             const bf16 *__restrict__ x, bf16 *__restrict__ y, int N,
+                                                             int K, int B, int group, int pdl) {
+  constexpr int RG = 8 / KS;
+  extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x W4_RING x 1 KB, sliced tokens, group sums
+  __shared__ float red[8 * 16 * 8];
+  __shared__ int e_s[4];
+  __shared__ float red_max[4][8];
+  if (pdl == 2) pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int rg = warp / KS, ks = warp % KS;
+  const int cols = B * NSL;                 // MMA columns: NSL slices per token
+  const int kslice = K / KS;                // inputs per K-slice (a multiple of group)
+  const int steps = kslice / 128;
+  const int sets = ((N + 15) / 16 + RG - 1) / RG;
+  const int xstride = K + 64;
+  const int groups = K / group, gsteps = group / 128;
+  int8_t *xs = reinterpret_cast<int8_t *>(rings + 8 * W4_RING * 1024);
+  int *csum = reinterpret_cast<int *>(xs + (size_t)cols * xstride);  // [K / 128][8]: slice sums per 128 inputs
+  const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(rings + warp * W4_RING * 1024) + g * 64 + t * 16;
+
+  // the weight stream of one set: rows r0 + g and r0 + g + 8, this warp's K-slice, 64 packed bytes per step
+  int r0 = (blockIdx.x * RG + rg) * 16;
+  const uint8_t *row0 = nullptr, *row1 = nullptr;
+  auto set_rows = [&]() {
+    row0 = Wp + (size_t)min(r0 + g, N - 1) * (K / 2) + (size_t)ks * (kslice / 2) + t * 16;
+    row1 = Wp + (size_t)min(r0 + g + 8, N - 1) * (K / 2) + (size_t)ks * (kslice / 2) + t * 16;
+  };
+  auto issue = [&](int st) {
+    if (st < steps) {
+      const uint32_t d = slot0 + (st % W4_RING) * 1024;
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + st * 64) : "memory");
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(row1 + st * 64) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  set_rows();
+#pragma unroll
+  for (int st = 0; st < W4_RING; ++st) issue(st);  // weights are immutable: stream before the dependency wait
+  if (pdl) pdl_wait();
+  slice_tokens<NSL, true>(x, K, B, xs, xstride, e_s, red_max);
+  __syncthreads();
+  // slice sums per 128 inputs: warp task (block, column), one word (4 slice bytes) per lane, dp4a against ones
+  for (int task = warp; task < (K / 128) * cols; task += 8) {
+    const int blk = task / cols, col = task % cols;
+    const int w = *reinterpret_cast<const int *>(xs + (size_t)col * xstride + blk * 128 + lane * 4);
+    int sum = __dp4a(w, 0x01010101, 0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) csum[blk * 8 + col] = sum;
+  }
+  __syncthreads();
+
+  for (int set = blockIdx.x; set < sets; set += gridDim.x) {
+    if (set != (int)blockIdx.x) {
+      r0 = (set * RG + rg) * 16;
+      set_rows();
+#pragma unroll
+      for (int st = 0; st < W4_RING; ++st) issue(st);
+    }
+    const int na = r0 + g, nb = r0 + g + 8;  // this lane's rows
+    const int c0 = 2 * t, c1 = 2 * t + 1;    // this lane's columns
+    const int8_t *xrow = xs + (size_t)g * xstride + ks * kslice + t * 32;
+    float f[4] = {0.f, 0.f, 0.f, 0.f};  // (row g, c0), (g, c1), (g + 8, c0), (g + 8, c1)
+    int acc[4] = {0, 0, 0, 0};
+    int cs0 = 0, cs1 = 0;  // this group's slice sums of columns c0, c1
+    float sa = 0.f, sb = 0.f;  // this group's scales of rows na, nb
+    for (int st = 0; st < steps; ++st) {
+      const int blk = (ks * kslice) / 128 + st;  // global 128-input block
+      if (st % gsteps == 0) {  // a group starts: its scales (immutable) and slice sums
+        const int gi = blk / gsteps;
+        sa = __ldg(S + (size_t)min(na, N - 1) * groups + gi);
+        sb = __ldg(S + (size_t)min(nb, N - 1) * groups + gi);
+        cs0 = cs1 = 0;
+      }
+      if (c0 < cols) cs0 += csum[blk * 8 + c0];
+      if (c1 < cols) cs1 += csum[blk * 8 + c1];
+      asm volatile("cp.async.wait_group %0;" ::"n"(W4_RING - 1) : "memory");
+      const uint32_t d = slot0 + (st % W4_RING) * 1024;
+      uint4 wa, wb;
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(wa.x), "=r"(wa.y), "=r"(wa.z), "=r"(wa.w) : "r"(d)
+                   : "memory");
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(wb.x), "=r"(wb.y), "=r"(wb.z), "=r"(wb.w)
+                   : "r"(d + 512)
+                   : "memory");
+      uint4 xv0 = make_uint4(0u, 0u, 0u, 0u), xv1 = xv0;
+      if (g < cols) {
+        xv0 = *reinterpret_cast<const uint4 *>(xrow + st * 128);
+        xv1 = *reinterpret_cast<const uint4 *>(xrow + st * 128 + 16);
+      }
+      issue(st + W4_RING);  // the slot just read refills
+      const uint32_t pa[4] = {wa.x, wa.y, wa.z, wa.w}, pb[4] = {wb.x, wb.y, wb.z, wb.w};
+      const uint32_t xw[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // packed word j: inputs 8j .. 8j + 7 of the lane's 32
+        const uint32_t a[4] = {pa[j] & 0x0F0F0F0Fu, pb[j] & 0x0F0F0F0Fu, (pa[j] >> 4) & 0x0F0F0F0Fu,
+                               (pb[j] >> 4) & 0x0F0F0F0Fu};
+        mma_s8_16832(acc, a, xw[2 * j], xw[2 * j + 1]);
+      }
+      if ((st + 1) % gsteps == 0) {  // the group ends: remove the +8 exactly, fold with the group scale
+        f[0] = __fmaf_rn((float)(acc[0] - 8 * cs0), sa, f[0]);
+        f[1] = __fmaf_rn((float)(acc[1] - 8 * cs1), sa, f[1]);
+        f[2] = __fmaf_rn((float)(acc[2] - 8 * cs0), sb, f[2]);
+        f[3] = __fmaf_rn((float)(acc[3] - 8 * cs1), sb, f[3]);
+        acc[0] = acc[1] = acc[2] = acc[3] = 0;
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();
+#pragma unroll
+    for (int e = 0; e < 4; ++e) red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 + frag_tok(lane, 0, e)] = f[e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < RG * 16 * B; i += GV_THREADS) {
+      const int b = i % B, rr = (i / B) % 16, g2 = i / (16 * B);
+      const int n = (set * RG + g2) * 16 + rr;
+      if (n >= N) continue;
+      float v = 0.f;
+#pragma unroll
+      for (int sl = NSL - 1; sl >= 0; --sl) {
+        float a = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < KS; ++s2) a += red[((g2 * KS + s2) * 16 + rr) * 8 + b * NSL + sl];
+        v = __fmaf_rn(v, 256.f, a);
+      }
+      y[(size_t)b * N + n] = f2bf(ldexpf(v, e_s[b]));
+    }
+    __syncthreads();
+  }
+}
+
+// dynamic shared memory: rings, the sliced tokens, the slice sums
+size_t w4_smem(int K, int B, int nsl) {
+  return (size_t)8 * W4_RING * 1024 + (size_t)B * nsl * (K + 64) + (size_t)(K / 128) * 8 * sizeof(int);
+}
+
+std::mutex g_w4_mu;
+std::set<std::pair<const void *, int>> g_w4_attr;
+
+template <int KS, int NSL>
+cudaError_t w4_launch(const uint8_t *Wp, const float *S, const bf16 *x, bf16 *y, int N, int K, int B, int group,
+                      bool pdl, int trigger, cudaStream_t st) {
+  auto kern = gemv_w4_kernel<KS, NSL>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(g_w4_mu);
+    const auto key = std::make_pair(reinterpret_cast<const void *>(kern), dev);
+    if (!g_w4_attr.count(key)) {
+      if (const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024))
+        return e;
+      g_w4_attr.insert(key);
+    }
+  }
+  const size_t dyn = w4_smem(K, B, NSL);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GV_THREADS, dyn) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int rg = 8 / KS, sets = ((N + 15) / 16 + rg - 1) / rg;
+  const int resident = per_sm * device_sm_count();  // one wave: the grid strides over the sets
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sets < resident ? sets : resident);
+  cfg.blockDim = dim3(GV_THREADS);
+  cfg.dynamicSmemBytes = dyn;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, Wp, S, x, y, N, K, B, group, pdl ? trigger : 0);
+}
+
+template <int NSL>
+cudaError_t w4_ks(int ks, const uint8_t *Wp, const float *S, const bf16 *x, bf16 *y, int N, int K, int B, int group,
+                  bool pdl, int trigger, cudaStream_t st) {
+  switch (ks) {
+    case 1: return w4_launch<1, NSL>(Wp, S, x, y, N, K, B, group, pdl, trigger, st);
+    case 2: return w4_launch<2, NSL>(Wp, S, x, y, N, K, B, group, pdl, trigger, st);
+    case 4: return w4_launch<4, NSL>(Wp, S, x, y, N, K, B, group, pdl, trigger, st);
+    default: return w4_launch<8, NSL>(Wp, S, x, y, N, K, B, group, pdl, trigger, st);
+  }
+}
+
+}  // namespace
+
+// Slices per token of the INT4 GEMV (3 up to 2 tokens, 2 up to 4) if its shared memory fits, else 0.
+int gemv_w4_slices(int K, int B) {
+  const int nsl = B <= 2 ? 3 : (B <= 4 ? 2 : 0);
+  if (nsl == 0 || w4_smem(K, B, nsl) > 160 * 1024 || K > 8 * GV_THREADS * XS_CH / B) return 0;
+  return nsl;
+}
+
+cudaError_t launch_gemv_w4(const uint8_t *Wp, const float *S, const void *x, void *y, int N, int K, int group, int B,
+                           bool pdl, int trigger, cudaStream_t st) {
+  if (N <= 0 || B <= 0) return cudaSuccess;
+  const int nsl = gemv_w4_slices(K, B);
+  if (!nsl) return cudaErrorInvalidValue;
+  // K-slices per 16-row group: the fewest that give ~8 warps per SM, each slice a whole number of groups
+  const long groups16 = (N + 15) / 16, target = 8L * device_sm_count();
+  int ks = 1;
+  while (ks < 8 && groups16 * ks < target && (K / (2 * ks)) % group == 0) ks *= 2;
+  return nsl == 3 ? w4_ks<3>(ks, Wp, S, (const bf16 *)x, (bf16 *)y, N, K, B, group, pdl, trigger, st)
+                  : w4_ks<2>(ks, Wp, S, (const bf16 *)x, (bf16 *)y, N, K, B, group, pdl, trigger, st);
+}
+
+}  // namespace lfm2q

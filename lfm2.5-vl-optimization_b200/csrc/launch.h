@@ -25,6 +25,7 @@ cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void
                         int B, bool pdl, cudaStream_t st);
 // tuning: let dependents launch at kernel start (default: after the K loop)
 void gemv_set_early_trigger(bool early);
+int gemv_trigger_mode();  // the PDL trigger argument of the GEMV kernels: 1 = after the K loop, 2 = at the start
 void gemv_set_impl(int impl);
 // per-token W8A8 linear for few tokens in one launch: quant_rows(x) fused into the A8 GEMV
 cudaError_t launch_linear_a8(const void *x, const int8_t *W, const float *sw, const void *bias, void *y, int N, int K,
@@ -59,6 +60,11 @@ cudaError_t launch_gemv_chain(const ChainLayer *layers, int n, int B, bool pdl, 
 // gemv.cu: one weight-only int8 GEMV of a chain (the x-sliced path where it applies, else the bf16 path)
 cudaError_t launch_gemv_pf(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
                            const L2Prefetch &pf, bool pdl, cudaStream_t st);
+
+// gemv_w4.cu: INT4 weight-only GEMV (packed nibbles, one fp32 scale per group of `group` inputs, group % 128 == 0)
+int gemv_w4_slices(int K, int B);  // 0: this K / B does not fit the kernel's shared memory
+cudaError_t launch_gemv_w4(const uint8_t *Wp, const float *S, const void *x, void *y, int N, int K, int group, int B,
+                           bool pdl, int trigger, cudaStream_t st);
 
 // gemm_tc.cu: tcgen05 W8A8 GEMMs
 enum GemmEpi { EPI_TOKEN = 0, EPI_GROUP = 1, EPI_GROUP_Q = 2, EPI_SILU = 3, EPI_W8 = 4 };

@@ -5,7 +5,7 @@ prebuilt sm_100a library liblfm2q.so instead of a JIT build.
                 gemm_i8, gemm_i8_q, gemm_w8, quant_rows, add_layernorm_q, add_rmsnorm_q, silu_mul_q,
                 plus gemm_i8_silu (W8A8 GEMM with the SiLU(w1) * w3 gate fused into its epilogue)
     ext()       the GEMV part of the reference's lfm2_decode extension (kernels/lfm2_decode.cpp:152-168):
-                gemv, gemv_epi, set_pdl, set_gemv_impl, plus gemv_a8 (int8 tokens x int8 weights, exact int32)
+                gemv, gemv_epi, gemv_w4, set_pdl, set_gemv_impl, plus gemv_a8 (int8 tokens x int8 weights, exact int32)
 
 Argument names, meaning, in-place outputs and the RuntimeError messages of the shape checks follow the reference
 bindings (kernels/int8_gemm.cpp:20-141, kernels/lfm2_decode.cpp:30-150). Every op enqueues on PyTorch's current
@@ -298,6 +298,23 @@ class DecodeGemvExt:
         with _DeviceOf(xq):
             _capi.call("lfm2q_gemv_a8", W.data_ptr(), sw.data_ptr(), xq.data_ptr(), sx.data_ptr(), _ptr(bias),
                        y.data_ptr(), N, K, B, int(bool(gelu)), _stream(xq))
+
+    def gemv_w4(self, Wp, S, x, y, rows=0):
+        """INT4 weight-only GEMV: y [1, N] = x [1, K] . dequant(Wp)^T, Wp uint8 [N, K/2] (two codes + 8 per byte, low
+        nibble first), S fp32 [N, K / group] (lfm2opt.quant.quantize_int4). rows: accepted for compatibility."""
+        _req(Wp.is_cuda and Wp.is_contiguous() and Wp.dtype == torch.uint8 and Wp.dim() == 2,
+             "Wp: contiguous uint8 [N, K/2]")
+        _req(S.is_cuda and S.is_contiguous() and S.dtype == _F32, "S: contiguous fp32 [N, K/128]")
+        _check(x, _BF, "x")
+        _check(y, _BF, "y")
+        N, K = Wp.size(0), Wp.size(1) * 2
+        _req(S.size(0) == N and K % S.size(1) == 0, "S must be [N, K / group]")
+        group = K // S.size(1)
+        _req(group % 32 == 0, "group size must be a multiple of 32")
+        _req(x.numel() == K and y.numel() == N, "batch 1 only")
+        with _DeviceOf(x):
+            _capi.call("lfm2q_gemv_w4", Wp.data_ptr(), S.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, group, 1,
+                       _stream(x))
 
     def set_pdl(self, on):
         """Enable/disable Programmatic Dependent Launch for the GEMV kernels (default on)."""

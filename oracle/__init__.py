@@ -11,7 +11,7 @@ Parity is pinned: tests/golden/ holds vectors produced by the reference's own Py
 container (tests/golden/make_golden.py); tests/test_oracle.py checks this oracle against them bit for bit.
 """
 
-from .quant import quantize_int8_ref, quant_rows_ref, quant_groups_ref  # noqa: F401
+from .quant import quantize_int8_ref, quantize_int4_ref, quant_rows_ref, quant_groups_ref  # noqa: F401
 from .gemm import (gemm_i8_ref, gemm_i8_grouped_ref, gemm_i8_grouped_f64, gemm_i8_q_ref, gemm_i8_silu_ref,  # noqa: F401
                    gemm_w8_f64, int_mm_exact, bf16_ulps, silu_chain_close, gelu_close)
-from .gemv import gemv_ref, gemv_f64, gemv_epi_ref  # noqa: F401
+from .gemv import gemv_ref, gemv_f64, gemv_epi_ref, gemv_w4_ref, gemv_w4_f64, dequantize_int4_ref  # noqa: F401

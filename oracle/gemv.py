@@ -47,3 +47,26 @@ def gemv_epi_ref(epi, W, scale, x, state=None, cw=None, cbias=None):
         acc = acc + cbias.float()
     y = (c_ * acc.to(torch.bfloat16).float()).to(torch.bfloat16)
     return y, new_state
+
+
+@torch.no_grad()
+def dequantize_int4_ref(packed, scale):
+    """int4 codes (low nibble = input 2j, high nibble = 2j + 1, stored + 8) times the group scales, fp32 [N, K] (the
+    reference's dequantize_int4, src/lfm2opt/quant.py:43-48)."""
+    p = packed.to(torch.int32)
+    q = torch.stack([(p & 0xF) - 8, (p >> 4) - 8], dim=-1).reshape(packed.shape[0], -1).float()
+    group = q.shape[1] // scale.shape[1]
+    return (q.reshape(q.shape[0], -1, group) * scale.float()[..., None]).reshape(q.shape[0], -1)
+
+
+@torch.no_grad()
+def gemv_w4_ref(packed, scale, x):
+    """The reference's INT4 GEMV check expression (tests/test_kernels.py:148-150): F.linear(x.float(),
+    dequantize_int4(Wp, S)).to(bf16)."""
+    return F.linear(x.float(), dequantize_int4_ref(packed, scale)).to(torch.bfloat16)
+
+
+@torch.no_grad()
+def gemv_w4_f64(packed, scale, x):
+    """fp64 value of the INT4 GEMV before the final bf16 rounding."""
+    return x.double() @ dequantize_int4_ref(packed, scale).double().t()

@@ -31,3 +31,24 @@ def quant_groups_ref(x: torch.Tensor):
     s = a / torch.full_like(a, 127.0)
     q = torch.round(xg / s[..., None]).clamp(-127, 127).to(torch.int8).flatten(-2)
     return q, s.t().contiguous()
+
+
+@torch.no_grad()
+def quantize_int4_ref(w: torch.Tensor, group: int = 128, clip_search: bool = False):
+    """Group-wise symmetric INT4 with two codes per byte; the reference's quantize_int4 (src/lfm2opt/quant.py:22-40):
+    scale = max(amax, 1e-12) / 7 per row and group (optionally the clipped scale amax * a / 7, a on 16 steps of
+    [0.70, 1.00], with the smallest squared error, first best kept); q = clamp(round(w / scale), -8, 7); byte j of a
+    row = (q[2j] + 8) | (q[2j + 1] + 8) << 4. Returns (packed uint8 [N, K/2], scale fp32 [N, K/group])."""
+    N, K = w.shape
+    wg = w.float().reshape(N, K // group, group)
+    amax = wg.abs().amax(-1).clamp_min(1e-12)
+    scale = amax / 7
+    if clip_search:
+        best = torch.full_like(amax, float("inf"))
+        for a in torch.linspace(0.70, 1.00, 16).tolist():
+            s = amax * a / 7
+            err = (torch.round(wg / s[..., None]).clamp(-8, 7) * s[..., None] - wg).pow(2).sum(-1)
+            scale = torch.where(err < best, s, scale)
+            best = torch.minimum(err, best)
+    q = (torch.round(wg / scale[..., None]).clamp(-8, 7) + 8).to(torch.int32).reshape(N, K)
+    return (q[:, 0::2] | (q[:, 1::2] << 4)).to(torch.uint8), scale

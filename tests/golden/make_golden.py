@@ -2,6 +2,7 @@
 container (the reference tree is not present on the GPU box; the vectors travel as committed .npz files).
 
 What is executed from the reference (jainilbavishi24/LFM2.5-VL-Optimization, checked out read-only):
+  * src/lfm2opt/quant.py            quantize_int4, dequantize_int4 (imported as a module)
   * src/lfm2opt/quant.py            quantize_int8 (imported as a module)
   * tests/test_int8_gemm.py         ref_quant, ref_quant_groups, bf16_ulps, test_quant_rows, test_quant_groups,
                                     test_i8, test_i8_grouped (function definitions taken from the file's AST)
@@ -108,6 +109,21 @@ def main():
         out[f"w{i}"], out[f"q{i}"], out[f"s{i}"] = t2np(w), t2np(q), t2np(s)
     np.savez_compressed(HERE / "quantize_int8.npz", **out)
 
+    # ---------------------------------------------------------------- INT4 weight quantizer (imported)
+    out4 = {}
+    g = torch.Generator().manual_seed(4)
+    cases4 = [(8, 256, 128, False), (33, 1024, 128, True), (16, 2048, 256, False), (5, 512, 128, True)]
+    for i, (N, K, group, clip) in enumerate(cases4):
+        w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+        if i == 1:
+            w[2, :128] = 0  # an all-zero group: its scale clamps to 1e-12 / 7
+            w[4, 9] = 0.4  # an outlier in one group
+        p4, s4 = rq.quantize_int4(w, group, clip_search=clip)
+        out4[f"w{i}"], out4[f"p{i}"], out4[f"s{i}"] = t2np(w), t2np(p4), t2np(s4)
+        out4[f"d{i}"] = t2np(rq.dequantize_int4(p4, s4))
+        out4[f"meta{i}"] = np.array([N, K, group, int(clip)])
+    np.savez_compressed(HERE / "quantize_int4.npz", **out4)
+
     # ---------------------------------------------------------------- activation quantizers + W8A8 (test functions)
     tests = load_functions(ref / "tests/test_int8_gemm.py",
                            ["ref_quant", "ref_quant_groups", "bf16_ulps", "test_quant_rows", "test_quant_groups",
@@ -166,11 +182,15 @@ def main():
     run_in(ns2, tk["test_gemv"])
     torch.manual_seed(3)
     ns2["test_gemv"]()
-    gv = {}
-    n = 0
+    gv, g4 = {}, {}
+    n = n4 = 0
     for c in cap2.cases:
         name, _, ref_y = c["_args"]
-        if "int4" in name:
+        if "int4" in name:  # the reference's expression: F.linear(x.float(), dequantize_int4(Wp, S4)).to(bf16)
+            g4[f"name{n4}"] = np.array(name)
+            g4[f"p{n4}"], g4[f"s{n4}"], g4[f"x{n4}"], g4[f"y{n4}"] = (t2np(c["Wp"]), t2np(c["S4"]), t2np(c["x"]),
+                                                                      t2np(ref_y))
+            n4 += 1
             continue
         batched = "B=" in name
         xin = c["xb"] if batched else c["x"]
@@ -183,6 +203,7 @@ def main():
         gv[f"s{n}"] = t2np(sc) if sc is not None else np.zeros(0, np.float32)
         n += 1
     np.savez_compressed(HERE / "gemv.npz", **gv)
+    np.savez_compressed(HERE / "gemv_w4.npz", **g4)
     print("golden vectors written to", HERE)
 
 

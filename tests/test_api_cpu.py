@@ -57,3 +57,14 @@ def test_int8linear_pads_and_quantizes_on_cpu_without_kernels():
     assert lin0.group == 0
     with pytest.raises(ValueError):
         L.Int8Linear(w, None, group=32)
+
+
+def test_quantize_int4_matches_reference_golden():
+    """lfm2opt.quant.quantize_int4 / dequantize_int4 (load-time torch ops) give the reference's bytes and scales."""
+    from lfm2opt.quant import dequantize_int4, quantize_int4
+    d = golden("quantize_int4")
+    for i in range(4):
+        N, K, group, clip = (int(v) for v in d[f"meta{i}"])
+        p, s = quantize_int4(to_t(d[f"w{i}"], bf16=True), group, clip_search=bool(clip))
+        assert torch.equal(p, to_t(d[f"p{i}"])) and torch.equal(s, to_t(d[f"s{i}"])), i
+        assert torch.equal(dequantize_int4(p, s), to_t(d[f"d{i}"])), i

@@ -116,3 +116,13 @@ def test_gemv_chain_rejects_bad_layers_without_a_gpu():
     arr[1] = _capi.GemvLayer(1 << 20, 1 << 20, (2 << 20) + 8, 3 << 20, 256, 2048)  # x not 16-byte aligned
     assert L.lfm2q_gemv_chain(arr, 2, 1, None) == _capi.EINVAL
     del fake
+
+
+def test_gemv_w4_rejects_bad_shapes_without_a_gpu():
+    L = _capi.lib()
+    p = 1 << 20
+    assert L.lfm2q_gemv_w4(p, p, p, p, 256, 2048, 64, 1, None) == _capi.EINVAL  # group % 128
+    assert L.lfm2q_gemv_w4(p, p, p, p, 256, 2000, 128, 1, None) == _capi.EINVAL  # K % group
+    assert L.lfm2q_gemv_w4(p, p, p, p, 256, 2048, 128, 5, None) == _capi.EINVAL  # B > 4
+    assert L.lfm2q_gemv_w4(p, p, p, p, 256, 8192, 128, 4, None) == _capi.EINVAL  # B * K > 16384
+    assert L.lfm2q_gemv_w4(None, p, p, p, 256, 2048, 128, 1, None) == _capi.EINVAL

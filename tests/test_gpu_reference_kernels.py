@@ -258,11 +258,11 @@ def test_silu_gate_equals_reference_composition(cuda_dev, refk, M, K, I, gate_bi
     assert torch.equal(y, ry), f"{(y != ry).sum().item()} of {y.numel()} outputs differ"
 
 
-def test_silu_gate_every_table_value_equals_reference(cuda_dev, refk):
-    """The fused SiLU epilogue evaluates bf16(silu(g)) from a table for 2^-8 <= |g| < 2^8 and directly elsewhere. With
-    all-zero activations every gate equals its bias, so the bias enumerates every bf16 value the table holds (both
-    signs, 16 binades x 128 mantissas) and a spread outside it (zero, subnormal, tiny, large, around -88); the result
-    must equal the reference's gemm_i8 -> silu_mul composition bit for bit. The up half is 1, so y = bf16(silu(g))."""
+def test_silu_gate_every_gate_value_equals_reference(cuda_dev, refk):
+    """With all-zero activations every gate of the fused SiLU epilogue equals its bias, so the bias can enumerate gate
+    values: every bf16 value with 2^-8 <= |g| < 2^8 (both signs, 16 binades x 128 mantissas), zero, subnormals, tiny
+    and large values, the region around -88 where 1 + exp(-g) passes 2^126, and random bf16 values. The result must
+    equal the reference's gemm_i8 -> silu_mul composition bit for bit. The up half is 1, so y = bf16(silu(g))."""
     table = [((s << 15) | (e << 7) | m) for s in (0, 1) for e in range(119, 135) for m in range(128)]
     extra = [0x0000, 0x8000, 0x0001, 0x8001, 0x0080, 0x3B00, 0xBB00, 0x3BFF, 0xBBFF, 0x4380, 0xC380, 0x43FF, 0xC3FF,
              0x4700, 0xC2B0, 0xC2B1, 0xC2AF, 0xC2B2, 0xC2C0, 0x7F7F, 0xFF7F]

@@ -146,3 +146,21 @@ def test_rmsnorm_order_matches_thread_loop():
             ss = _butterfly_scalar(warps + [_f32(0)] * 24)
             v = _f32(_f32(ss / _f32(H)) + _f32(1e-5))
             assert _f32(1.0 / np.sqrt(np.float64(v))) == rs[r], (H, r)
+
+
+def test_quantize_int4_matches_reference():
+    d = golden("quantize_int4")
+    for i in range(4):
+        N, K, group, clip = (int(v) for v in d[f"meta{i}"])
+        p, s = oracle.quantize_int4_ref(to_t(d[f"w{i}"], bf16=True), group, bool(clip))
+        assert torch.equal(p, to_t(d[f"p{i}"])) and torch.equal(s, to_t(d[f"s{i}"])), i
+        assert torch.equal(oracle.dequantize_int4_ref(p, s), to_t(d[f"d{i}"])), i
+
+
+def test_gemv_w4_matches_reference():
+    d = golden("gemv_w4")
+    n = len([k for k in d.files if k.startswith("name")])
+    assert n >= 2
+    for i in range(n):
+        y = oracle.gemv_w4_ref(to_t(d[f"p{i}"]), to_t(d[f"s{i}"]), to_t(d[f"x{i}"], bf16=True))
+        assert torch.equal(y.view(torch.int16), to_t(d[f"y{i}"])), str(d[f"name{i}"])
