@@ -294,6 +294,18 @@ class Job:
         return y
 
     def _plan(self):
+        # The head's input does not depend on this step's LM layers (in this throughput job it stands for the head of
+        # the previous batch), so its chunks run first: their NCCL all-gathers (N > 1) then proceed under the vision
+        # and LM GEMMs instead of after the last of them.
+        self.head_chunks = 4
+        from lfm2opt.parallel import shard_rows
+        self.logits = torch.empty(self.world * HEAD_M * (self.hs.hi - self.hs.lo), device=self.dev,
+                                  dtype=torch.bfloat16)
+        self.head_local = []
+        for c in range(self.head_chunks):
+            s0, cnt = shard_rows(HEAD_M, self.head_chunks, c)
+            y = self._linear(self.xh[s0:s0 + cnt], self.hq, self.hsc, None, self.hq.shape[0], "none", f"head{c}")
+            self.head_local.append((len(self.calls), s0, cnt, y))
         for l in range(VISION_LAYERS):
             for j, (name, K, N, _, epi) in enumerate(VISION):
                 x = self.xv if K == 1152 else self.xv2
@@ -304,15 +316,6 @@ class Job:
             for j, (name, K, N) in enumerate(mix + LM_MLP):
                 x = self.xl if K == 2048 else self.xl2
                 self._linear(x, *self.lw[l][j], None, N, "silu" if name == "l.w13" else "none", name)
-        self.head_chunks = 4
-        from lfm2opt.parallel import shard_rows
-        self.logits = torch.empty(self.world * HEAD_M * (self.hs.hi - self.hs.lo), device=self.dev,
-                                  dtype=torch.bfloat16)
-        self.head_local = []
-        for c in range(self.head_chunks):
-            s0, cnt = shard_rows(HEAD_M, self.head_chunks, c)
-            y = self._linear(self.xh[s0:s0 + cnt], self.hq, self.hsc, None, self.hq.shape[0], "none", f"head{c}")
-            self.head_local.append((len(self.calls), s0, cnt, y))
 
     def run(self, rec=None):
         """Enqueue one step. rec: a StepRecorder that receives CUDA events around every launch and at the step's end."""
@@ -446,10 +449,11 @@ class E2E:
         self.h2d_bytes = (self.hv.numel() + self.hl.numel() + self.hh.numel()) * 2
         self.d2h_bytes = cnt * 2
         self.logits = None
-        self.cs = torch.cuda.Stream(dev)  # host copies overlap the compute stream
+        self.cs = torch.cuda.Stream(dev)  # host-to-device copies overlap the compute stream
+        self.ds = torch.cuda.Stream(dev)  # device-to-host copies of the logits, likewise
 
     def _d2h_chunk(self, off, dst, work):
-        """Copy this rank's share of a finished logits chunk to the host on the copy stream."""
+        """Copy this rank's share of a finished logits chunk to the host on the device-to-host stream."""
         s0, cnt = self.out_slice
         a, b = max(off, s0), min(off + dst.numel(), s0 + cnt)
         if a >= b:
@@ -457,29 +461,32 @@ class E2E:
         if work is None:
             ev = torch.cuda.Event()
             ev.record(torch.cuda.current_stream(self.job.dev))
-        with torch.cuda.stream(self.cs):
+        with torch.cuda.stream(self.ds):
             if work is None:
-                self.cs.wait_event(ev)
+                self.ds.wait_event(ev)
             else:
                 work.wait()  # the copy stream (only) waits for this chunk's all-gather
             flat = dst.reshape(-1)
             self.hout[a - s0:b - s0].copy_(flat[a - off:b - off], non_blocking=True)
 
     def step(self):
-        """One step: inputs H2D, the job, this rank's logits share D2H. The vision input is copied first on the
-        compute stream; the LM and head inputs follow on a copy stream while the vision layers run, and each logits
-        chunk goes to the host on the copy stream as soon as it is complete. The step ends (compute stream) when its
-        outputs are on the host."""
+        """One step: inputs H2D, the job, this rank's logits share D2H. The head's input is copied first and the head
+        runs first (its input does not depend on this step's layers), each logits chunk going to the host on its own
+        stream as soon as its all-gather completes, so that copy overlaps the vision and LM layers; the vision and LM
+        inputs arrive on a copy stream meanwhile. The step ends (compute stream) when its outputs are on the host."""
         cur = torch.cuda.current_stream(self.job.dev)
-        self.dv.copy_(self.hv, non_blocking=True)
+        self.dh.copy_(self.hh, non_blocking=True)
         self.cs.wait_stream(cur)  # after everything this step's buffers were used for
+        self.ds.wait_stream(cur)
         with torch.cuda.stream(self.cs):
+            self.dv.copy_(self.hv, non_blocking=True)
+            ev_v = torch.cuda.Event()
+            ev_v.record(self.cs)
             self.dl.copy_(self.hl, non_blocking=True)
             ev_l = torch.cuda.Event()
             ev_l.record(self.cs)
-            self.dh.copy_(self.hh, non_blocking=True)
-            ev_h = torch.cuda.Event()
-            ev_h.record(self.cs)
+        self.logits = self.head(self.dh, self.logits, on_chunk=self._d2h_chunk, wait=False)
+        cur.wait_event(ev_v)
         for layer in self.vlin:
             layer[0](self.dv)
             layer[1](self.dv)
@@ -491,8 +498,8 @@ class E2E:
             layer[1](self.dl)
             a = layer[2](self.dl, silu_gate=True)
             layer[3](a)
-        cur.wait_event(ev_h)
-        self.logits = self.head(self.dh, self.logits, on_chunk=self._d2h_chunk)
+        self.head.wait()
+        cur.wait_stream(self.ds)
         cur.wait_stream(self.cs)
 
 
@@ -907,25 +914,35 @@ def run_gemv_case(a):
     rows = parts[3] if len(parts) > 3 else 0
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
-    copies = max(1, -(-256 * 2 ** 20 // (N * K)))
-    Ws = [torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8) for _ in range(copies)]
-    s = torch.rand(N, generator=g, device=dev) * 1e-3
+    mode = os.environ.get("GEMV_MODE", "w16")  # w16 (default path), w16bf (bf16-MMA path forced), a8, w4 (INT4)
+    w4 = mode == "w4"
+    copies = max(1, -(-256 * 2 ** 20 // (N * K // (2 if w4 else 1))))
+    if w4:
+        Ws = [torch.randint(0, 256, (N, K // 2), generator=g, device=dev, dtype=torch.uint8) for _ in range(copies)]
+        s = torch.rand(N, K // 128, generator=g, device=dev) * 1e-2 + 1e-3
+    else:
+        Ws = [torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8) for _ in range(copies)]
+        s = torch.rand(N, generator=g, device=dev) * 1e-3
     x = torch.randn(B, K, generator=g, device=dev).to(torch.bfloat16)
     y = torch.empty(B, N, device=dev, dtype=torch.bfloat16)
     E = ext()
     per = 20
 
-    mode = os.environ.get("GEMV_MODE", "w16")  # w16 (default path), w16bf (bf16-MMA path forced), a8
     a8 = mode == "a8"
     from lfm2opt import _capi
     _capi.lib().lfm2q_set_gemv_path(1 if mode == "w16bf" else 0)
     xq = torch.randint(-127, 128, (B, K), generator=g, device=dev, dtype=torch.int8)
     sx = torch.rand(B, generator=g, device=dev) * 1e-2
 
+    L = _capi.lib()
+
     def burst():
         for i in range(per):
             if a8:
                 E.gemv_a8(Ws[i % copies], s, xq, sx, y)
+            elif w4:
+                L.lfm2q_gemv_w4(Ws[i % copies].data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, 128, B,
+                                torch.cuda.current_stream(dev).cuda_stream)
             else:
                 E.gemv(Ws[i % copies], s, x, y, rows)
 
@@ -938,7 +955,7 @@ def run_gemv_case(a):
     with torch.cuda.graph(graph):
         burst()
     ms = time_steps(graph.replay, a.steps, max(3, a.warmup), 1) / (a.steps * per)
-    nbytes = N * K + 4 * N + 2 * B * K + 2 * B * N
+    nbytes = (N * K // 2 + 4 * N * (K // 128) if w4 else N * K) + 4 * N + 2 * B * K + 2 * B * N
     peak = load_peaks().get("hbm_gbs")
     gbs = nbytes / (ms * 1e-3) / 1e9
     print(json.dumps({"gemv_case": a.gemv_case, "mode": mode, "pdl": os.environ.get("LFM2_PDL", "1"),

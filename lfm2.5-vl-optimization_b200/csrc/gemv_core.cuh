@@ -171,16 +171,17 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
   const int8_t *row1 = W + (size_t)min(r0 + g + 8, N - 1) * K + kb + t * 16;
   const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(ring) + g * 64 + t * 16;
   const int nsteps = (ke - kb) / 64;
-  auto issue = [&](int st) {
+  // step st goes to ring slot st mod RING; the loops below keep the slot of the current step incrementally
+  auto issue = [&](int st, int slot) {
     if (st < nsteps) {
-      const uint32_t d = slot0 + (st % RING) * 1024;
+      const uint32_t d = slot0 + slot * 1024;
       asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + st * 64) : "memory");
       asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(row1 + st * 64) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  auto lds = [&](int st, uint4 &w0, uint4 &w1) {
-    const uint32_t d = slot0 + (st % RING) * 1024;
+  auto lds = [&](int slot, uint4 &w0, uint4 &w1) {
+    const uint32_t d = slot0 + slot * 1024;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
                  : "memory");
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
@@ -200,7 +201,7 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
   };
   if (phase != 2) {
 #pragma unroll
-    for (int st = 0; st < RING; ++st) issue(st);
+    for (int st = 0; st < RING; ++st) issue(st, st);
   }
   if (phase == 1) return;
 #pragma unroll
@@ -214,10 +215,12 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
     lds(0, wc0, wc1);
     ldx(0, xc);
   }
+  int slot = 0;  // ring slot of step st
   for (int st = 0; st < nsteps; ++st) {
+    const int nslot = slot + 1 == RING ? 0 : slot + 1;
     if (st + 1 < nsteps) {
       asm volatile("cp.async.wait_group %0;" ::"n"(RING - 2) : "memory");
-      lds(st + 1, wn0, wn1);
+      lds(nslot, wn0, wn1);
       ldx(st + 1, xn);
     }
 #pragma unroll
@@ -226,7 +229,8 @@ __device__ __forceinline__ void warp_gemv_a8(const int8_t *__restrict__ W, const
 #pragma unroll
       for (int j = 0; j < NT; ++j) mma_s8_16832(acc[j], a, (&xc[j].x)[2 * s], (&xc[j].x)[2 * s + 1]);
     }
-    issue(st + RING);
+    issue(st + RING, slot);  // step st's slot: its data is already in registers
+    slot = nslot;
     wc0 = wn0;
     wc1 = wn1;
 #pragma unroll
@@ -247,9 +251,11 @@ __device__ __forceinline__ int frag_tok(int lane, int j, int e) { return 8 * j +
 constexpr int XS_CH = 8;
 // EO: within every 8-element chunk the bytes are stored in the order of the elements 0, 2, 4, 6, 1, 3, 5, 7 (the
 // order in which the INT4 GEMV unpacks a word of packed nibbles: low nibbles, then high nibbles).
+// csum (optional, needs K % 128 == 0): the sums of the slice bytes of every 128 elements, csum[blk * 8 + b * NSL + s]
+// for token b, slice s and block blk of 128 elements (16 chunks, held by 16 consecutive lanes).
 template <int NSL, bool EO = false>
 __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride, int *e_s,
-                                             float (&red_max)[4][8]) {
+                                             float (&red_max)[4][8], int *csum = nullptr) {
   constexpr int QBITS = 8 * NSL - 2;  // |q| < 2^QBITS
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K8 = K / 8, total = B * K8;
@@ -302,7 +308,7 @@ __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, 
 #pragma unroll
   for (int j = 0; j < XS_CH; ++j) {
     const int i = threadIdx.x + j * GV_THREADS;
-    if (i >= total) break;
+    if (i >= total) continue;  // whole 16-lane halves drop out together when total % 16 == 0
     const int b = i / K8, c = i - b * K8;
     int fb1 = f1b[0], fb2 = f2b[0];
 #pragma unroll
@@ -338,6 +344,16 @@ __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, 
 #pragma unroll
     for (int sl = 0; sl < NSL; ++sl)
       *reinterpret_cast<uint2 *>(xs + (size_t)(b * NSL + sl) * xstride + c * 8) = make_uint2(o[sl][0], o[sl][1]);
+    if (csum) {
+      const unsigned half = 0xFFFFu << (lane & 16);
+#pragma unroll
+      for (int sl = 0; sl < NSL; ++sl) {
+        int sum = __dp4a((int)o[sl][0], 0x01010101, __dp4a((int)o[sl][1], 0x01010101, 0));
+#pragma unroll
+        for (int o2 = 8; o2 > 0; o2 >>= 1) sum += __shfl_xor_sync(half, sum, o2);
+        if ((lane & 15) == 0) csum[(c >> 4) * 8 + b * NSL + sl] = sum;
+      }
+    }
   }
 }
 

@@ -10,10 +10,12 @@
 // so every partial sum is an exact int32 and the weights go to the MMA without any conversion to floating point:
 //   - a warp step is 16 weight rows x 128 inputs = 64 packed bytes per row (the same 1 KB cp.async ring slots as the
 //     int8 GEMV), lane (g, t) holding 16 packed bytes = 32 inputs of rows g and g + 8;
-//   - a word of 4 packed bytes (8 inputs) becomes two MMA words with two masks and a shift: the low nibbles (the
-//     even inputs) and the high nibbles (the odd inputs) as bytes u = q + 8 in 0..15. The token slices are stored
-//     in the same order (slice_tokens<NSL, EO = true>), so each MMA pairs every u with its own x;
-//   - sum_k q x = sum_k u x - 8 sum_k x: the group sums of every token slice are computed once per block, so the
+//   - a word of 4 packed bytes (8 inputs) becomes two MMA words with two masks: the low nibbles (the even inputs)
+//     as bytes u = q + 8 in 0..15, and the high nibbles (the odd inputs) left in place as bytes 16 u (unsigned
+//     int8 MMA operands), accumulated separately and divided by 16 (exactly) at the group's end. The token slices
+//     are stored in the matching order (slice_tokens<NSL, EO = true>), so each MMA pairs every u with its own x;
+//   - sum_k q x = sum_k u x - 8 sum_k x: the group sums of every token slice are computed once per block while the
+//     tokens are sliced (half-warp reductions), so the
 //     +8 is removed exactly from each group's int32 partial, which then folds into the fp32 result with the group's
 //     scale: f += (float)(A - 8 C) * s[n, g]. |A - 8 C| < 2^19, so the conversion is exact.
 // One 128-input step is one group-128 block; groups of 256, 384, ... fold every group / 128 steps (group must be a
@@ -32,6 +34,14 @@ namespace lfm2q {
 namespace {
 
 constexpr int W4_RING = 6;  // K steps (1 KB of packed weights each) a warp keeps in flight
+
+// unsigned int8 A (the weights' nibbles as bytes) x signed int8 B (the token slices) -> exact int32
+__device__ __forceinline__ void mma_u8s8_16832(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 
 template <int KS, int NSL>
 __global__ void __launch_bounds__(GV_THREADS) gemv_w4_kernel(const uint8_t *__restrict__ Wp, const float *__restrict__ S,
@@ -70,21 +80,19 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_w4_kernel(const uint8_t *__re
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
+  // this lane's rows' scales of the K-slice's first group (immutable, like the weights)
+  const int g_first = (ks * kslice) / group, g_count = kslice / group;
+  auto scales = [&](int gi, float &a, float &b) {
+    a = __ldg(S + (size_t)min(r0 + g, N - 1) * groups + gi);
+    b = __ldg(S + (size_t)min(r0 + g + 8, N - 1) * groups + gi);
+  };
+  float sa_n, sb_n;  // the next group's scales, loaded one group ahead of their use
   set_rows();
 #pragma unroll
   for (int st = 0; st < W4_RING; ++st) issue(st);  // weights are immutable: stream before the dependency wait
+  scales(g_first, sa_n, sb_n);
   if (pdl) pdl_wait();
-  slice_tokens<NSL, true>(x, K, B, xs, xstride, e_s, red_max);
-  __syncthreads();
-  // slice sums per 128 inputs: warp task (block, column), one word (4 slice bytes) per lane, dp4a against ones
-  for (int task = warp; task < (K / 128) * cols; task += 8) {
-    const int blk = task / cols, col = task % cols;
-    const int w = *reinterpret_cast<const int *>(xs + (size_t)col * xstride + blk * 128 + lane * 4);
-    int sum = __dp4a(w, 0x01010101, 0);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) csum[blk * 8 + col] = sum;
-  }
+  slice_tokens<NSL, true>(x, K, B, xs, xstride, e_s, red_max, csum);
   __syncthreads();
 
   for (int set = blockIdx.x; set < sets; set += gridDim.x) {
@@ -93,53 +101,64 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_w4_kernel(const uint8_t *__re
       set_rows();
 #pragma unroll
       for (int st = 0; st < W4_RING; ++st) issue(st);
+      scales(g_first, sa_n, sb_n);
     }
-    const int na = r0 + g, nb = r0 + g + 8;  // this lane's rows
-    const int c0 = 2 * t, c1 = 2 * t + 1;    // this lane's columns
+    const int c0 = 2 * t, c1 = 2 * t + 1;  // this lane's columns
     const int8_t *xrow = xs + (size_t)g * xstride + ks * kslice + t * 32;
+    const int *cs_col = csum + ((ks * kslice) / 128) * 8;  // this K-slice's first block of slice sums
     float f[4] = {0.f, 0.f, 0.f, 0.f};  // (row g, c0), (g, c1), (g + 8, c0), (g + 8, c1)
-    int acc[4] = {0, 0, 0, 0};
-    int cs0 = 0, cs1 = 0;  // this group's slice sums of columns c0, c1
-    float sa = 0.f, sb = 0.f;  // this group's scales of rows na, nb
-    for (int st = 0; st < steps; ++st) {
-      const int blk = (ks * kslice) / 128 + st;  // global 128-input block
-      if (st % gsteps == 0) {  // a group starts: its scales (immutable) and slice sums
-        const int gi = blk / gsteps;
-        sa = __ldg(S + (size_t)min(na, N - 1) * groups + gi);
-        sb = __ldg(S + (size_t)min(nb, N - 1) * groups + gi);
-        cs0 = cs1 = 0;
-      }
-      if (c0 < cols) cs0 += csum[blk * 8 + c0];
-      if (c1 < cols) cs1 += csum[blk * 8 + c1];
-      asm volatile("cp.async.wait_group %0;" ::"n"(W4_RING - 1) : "memory");
-      const uint32_t d = slot0 + (st % W4_RING) * 1024;
-      uint4 wa, wb;
-      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(wa.x), "=r"(wa.y), "=r"(wa.z), "=r"(wa.w) : "r"(d)
-                   : "memory");
-      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(wb.x), "=r"(wb.y), "=r"(wb.z), "=r"(wb.w)
-                   : "r"(d + 512)
-                   : "memory");
-      uint4 xv0 = make_uint4(0u, 0u, 0u, 0u), xv1 = xv0;
-      if (g < cols) {
-        xv0 = *reinterpret_cast<const uint4 *>(xrow + st * 128);
-        xv1 = *reinterpret_cast<const uint4 *>(xrow + st * 128 + 16);
-      }
-      issue(st + W4_RING);  // the slot just read refills
-      const uint32_t pa[4] = {wa.x, wa.y, wa.z, wa.w}, pb[4] = {wb.x, wb.y, wb.z, wb.w};
-      const uint32_t xw[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
+    int st = 0, slot = 0;  // step of the K-slice, and its ring slot (st mod W4_RING, kept incrementally)
+    for (int gl = 0; gl < g_count; ++gl) {
+      const float sa = sa_n, sb = sb_n;  // this group's scales of rows r0 + g, r0 + g + 8 (loaded a group ago)
+      if (gl + 1 < g_count) scales(g_first + gl + 1, sa_n, sb_n);
+      int acc[4] = {0, 0, 0, 0};  // low nibbles (even inputs): sum u x
+      int acc_h[4] = {0, 0, 0, 0};  // high nibbles left in place (odd inputs): sum 16 u x
+      int cs0 = 0, cs1 = 0;  // this group's slice sums of columns c0, c1
+      for (int sg = 0; sg < gsteps; ++sg, ++st) {
+        if (c0 < cols) cs0 += cs_col[st * 8 + c0];
+        if (c1 < cols) cs1 += cs_col[st * 8 + c1];
+        asm volatile("cp.async.wait_group %0;" ::"n"(W4_RING - 1) : "memory");
+        const uint32_t d = slot0 + slot * 1024;
+        uint4 wa, wb;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(wa.x), "=r"(wa.y), "=r"(wa.z), "=r"(wa.w) : "r"(d)
+                     : "memory");
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(wb.x), "=r"(wb.y), "=r"(wb.z), "=r"(wb.w)
+                     : "r"(d + 512)
+                     : "memory");
+        uint4 xv0 = make_uint4(0u, 0u, 0u, 0u), xv1 = xv0;
+        if (g < cols) {
+          xv0 = *reinterpret_cast<const uint4 *>(xrow + st * 128);
+          xv1 = *reinterpret_cast<const uint4 *>(xrow + st * 128 + 16);
+        }
+        // the slot just read refills with the step W4_RING ahead
+        if (st + W4_RING < steps) {
+          asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(row0 + (st + W4_RING) * 64)
+                       : "memory");
+          asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512),
+                       "l"(row1 + (st + W4_RING) * 64)
+                       : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        slot = slot + 1 == W4_RING ? 0 : slot + 1;
+        const uint32_t pa[4] = {wa.x, wa.y, wa.z, wa.w}, pb[4] = {wb.x, wb.y, wb.z, wb.w};
+        const uint32_t xw[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
+        // packed words j, j + 1 (inputs 8j .. 8j + 15 of the lane's 32): one MMA over their low nibbles with the even
+        // inputs' slices, one over their high nibbles (as 16 u, unsigned, no shift) with the odd inputs' slices
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {  // packed word j: inputs 8j .. 8j + 7 of the lane's 32
-        const uint32_t a[4] = {pa[j] & 0x0F0F0F0Fu, pb[j] & 0x0F0F0F0Fu, (pa[j] >> 4) & 0x0F0F0F0Fu,
-                               (pb[j] >> 4) & 0x0F0F0F0Fu};
-        mma_s8_16832(acc, a, xw[2 * j], xw[2 * j + 1]);
+        for (int j = 0; j < 4; j += 2) {
+          const uint32_t lo[4] = {pa[j] & 0x0F0F0F0Fu, pb[j] & 0x0F0F0F0Fu, pa[j + 1] & 0x0F0F0F0Fu,
+                                  pb[j + 1] & 0x0F0F0F0Fu};
+          const uint32_t hi[4] = {pa[j] & 0xF0F0F0F0u, pb[j] & 0xF0F0F0F0u, pa[j + 1] & 0xF0F0F0F0u,
+                                  pb[j + 1] & 0xF0F0F0F0u};
+          mma_u8s8_16832(acc, lo, xw[2 * j], xw[2 * j + 2]);
+          mma_u8s8_16832(acc_h, hi, xw[2 * j + 1], xw[2 * j + 3]);
+        }
       }
-      if ((st + 1) % gsteps == 0) {  // the group ends: remove the +8 exactly, fold with the group scale
-        f[0] = __fmaf_rn((float)(acc[0] - 8 * cs0), sa, f[0]);
-        f[1] = __fmaf_rn((float)(acc[1] - 8 * cs1), sa, f[1]);
-        f[2] = __fmaf_rn((float)(acc[2] - 8 * cs0), sb, f[2]);
-        f[3] = __fmaf_rn((float)(acc[3] - 8 * cs1), sb, f[3]);
-        acc[0] = acc[1] = acc[2] = acc[3] = 0;
-      }
+      // the group ends: sum u x = acc + acc_h / 16 (exact), remove the +8, fold with the group's scales
+      f[0] = __fmaf_rn((float)(acc[0] + (acc_h[0] >> 4) - 8 * cs0), sa, f[0]);
+      f[1] = __fmaf_rn((float)(acc[1] + (acc_h[1] >> 4) - 8 * cs1), sa, f[1]);
+      f[2] = __fmaf_rn((float)(acc[2] + (acc_h[2] >> 4) - 8 * cs0), sb, f[2]);
+      f[3] = __fmaf_rn((float)(acc[3] + (acc_h[3] >> 4) - 8 * cs1), sb, f[3]);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();

@@ -62,7 +62,8 @@ class NSplitHead:
     with the same M (the collectives are matched in order). on_chunk(off, dst, work), if given, is called as each chunk
     is enqueued: off = its offset in the flat buffer, dst = its [g * rows, V/g] block, work = its all-gather handle
     (None on one rank: dst is then complete in stream order on the current stream), so a consumer can start on a chunk
-    (e.g. copy it to the host on another stream after work.wait() there) while later chunks compute.
+    (e.g. copy it to the host on another stream after work.wait() there) while later chunks compute. wait=False returns
+    before the current stream waits for the gathers (call wait() later), so independent work can be enqueued first.
     """
 
     def __init__(self, linear, V: int, group=None, chunks: int = 4):
@@ -77,7 +78,7 @@ class NSplitHead:
     def chunk_bounds(self, M: int):
         return [shard_rows(M, self.chunks, c) for c in range(self.chunks)]
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor = None, on_chunk=None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out: torch.Tensor = None, on_chunk=None, wait: bool = True) -> torch.Tensor:
         M = x.shape[0]
         if out is None:
             out = torch.empty(self.world * M * self.slab, device=x.device, dtype=torch.bfloat16)
@@ -98,9 +99,17 @@ class NSplitHead:
             works.append(dist.all_gather_into_tensor(dst, local.contiguous(), group=self.group, async_op=True))
             if on_chunk is not None:
                 on_chunk(c_off, dst, works[-1])
-        for w in works:
-            w.wait()
+        self._works = works
+        if wait:
+            self.wait()
         return out
+
+    def wait(self):
+        """Make the current stream wait for the all-gathers of the last call (the call does this itself unless it was
+        made with wait=False, which lets the caller enqueue other work first while the gathers proceed)."""
+        for w in getattr(self, "_works", []):
+            w.wait()
+        self._works = []
 
     def as_rows(self, buf: torch.Tensor, M: int) -> torch.Tensor:
         """Chunk-major gathered buffer -> [M, V] (a copy)."""
