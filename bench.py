@@ -254,7 +254,12 @@ class Job:
         self.xv2 = torch.nn.functional.pad(act(self.vrows, 4304, False), (0, VISION_PAD["v.fc2"][1]))
         self.xl = act(self.lrows, 2048, True)
         self.xl2 = act(self.lrows, 8192, True)
-        self.xh = act(HEAD_M, 2048, True)
+        # the head's input is the same on every rank (the N-split head computes each rank's vocabulary slab of the
+        # same rows), so it comes from a rank-independent generator
+        gh = torch.Generator(device=dev).manual_seed(4321)
+        self.xh = torch.randn(HEAD_M, 2048, generator=gh, device=dev).to(torch.bfloat16)
+        idx = torch.randperm(2048, generator=torch.Generator().manual_seed(2))[:3]
+        self.xh[:, idx.to(dev)] *= 20
         self.q = {}
         self.y = {}
         self.stream = torch.cuda.current_stream(dev).cuda_stream

@@ -83,11 +83,13 @@ class NSplitHead:
         if out is None:
             out = torch.empty(self.world * M * self.slab, device=x.device, dtype=torch.bfloat16)
         works = []
+        keep = []  # the chunks' local slabs stay referenced until wait(): see there
         off = 0
         for start, cnt in self.chunk_bounds(M):
             if cnt == 0:
                 continue
-            local = self.linear(x[start:start + cnt])  # [cnt, slab] on the current stream
+            local = self.linear(x[start:start + cnt]).contiguous()  # [cnt, slab] on the current stream
+            keep.append(local)
             dst = out[off:off + self.world * cnt * self.slab].view(self.world * cnt, self.slab)
             c_off = off
             off += self.world * cnt * self.slab
@@ -96,20 +98,23 @@ class NSplitHead:
                 if on_chunk is not None:
                     on_chunk(c_off, dst, None)
                 continue
-            works.append(dist.all_gather_into_tensor(dst, local.contiguous(), group=self.group, async_op=True))
+            works.append(dist.all_gather_into_tensor(dst, local, group=self.group, async_op=True))
             if on_chunk is not None:
                 on_chunk(c_off, dst, works[-1])
-        self._works = works
+        self._works, self._keep = works, keep
         if wait:
             self.wait()
         return out
 
     def wait(self):
         """Make the current stream wait for the all-gathers of the last call (the call does this itself unless it was
-        made with wait=False, which lets the caller enqueue other work first while the gathers proceed)."""
+        made with wait=False, which lets the caller enqueue other work first while the gathers proceed). The local
+        slabs the gathers read are released only here, after the current stream has waited: an on_chunk consumer that
+        waits on another stream would otherwise let the caching allocator hand their memory to new work on the current
+        stream while NCCL still reads it."""
         for w in getattr(self, "_works", []):
             w.wait()
-        self._works = []
+        self._works, self._keep = [], []
 
     def as_rows(self, buf: torch.Tensor, M: int) -> torch.Tensor:
         """Chunk-major gathered buffer -> [M, V] (a copy)."""

@@ -46,7 +46,7 @@ def _oracle_linear(wq, sw):
     return lin
 
 
-def _head_worker(rank, world, port, M, V, K, chunks, q):
+def _head_worker(rank, world, port, M, V, K, chunks, wait, q):
     os.environ["OMP_NUM_THREADS"] = "1"
     torch.set_num_threads(1)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -66,7 +66,11 @@ def _head_worker(rank, world, port, M, V, K, chunks, q):
                 work.wait()
             seen.append((off, dst.reshape(-1).clone()))
 
-        buf = head(x, on_chunk=on_chunk)
+        buf = head(x, on_chunk=on_chunk, wait=wait)
+        if not wait:  # the gathered slabs' sources stay referenced until wait() and are released there
+            assert len(head._keep) == sum(1 for _, c in head.chunk_bounds(M) if c)
+            head.wait()
+            assert head._keep == [] and head._works == []
         full = head.as_rows(buf, M)
         # the chunks reported tile the buffer in order and hold the final gathered values
         offs = [o for o, _ in seen]
@@ -82,13 +86,13 @@ def _head_worker(rank, world, port, M, V, K, chunks, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M,chunks", [(37, 3), (64, 4), (5, 8)])
-def test_nsplit_head_gathers_the_full_logits(M, chunks):
+@pytest.mark.parametrize("M,chunks,wait", [(37, 3, True), (64, 4, False), (5, 8, True)])
+def test_nsplit_head_gathers_the_full_logits(M, chunks, wait):
     world, V, K = 2, 96, 128
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_head_worker, args=(r, world, port, M, V, K, chunks, q)) for r in range(world)]
+    procs = [ctx.Process(target=_head_worker, args=(r, world, port, M, V, K, chunks, wait, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]
