@@ -190,22 +190,24 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_a8_kernel(const int8_t *__res
   }
 }
 
-// Weight-only GEMV on the int8 tensor path ("x-sliced"), for 1..8/NSL tokens. Each token's bf16 activations are
-// written exactly as NSL-byte fixed point, q = x * 2^-E with E from the token's absmax so that |q| < 2^(8 NSL - 2),
-// and q is split into NSL balanced signed bytes, q = sum_s q_s 256^s. The bytes of token b are the NSL MMA columns
-// b * NSL + s, so the int8 weights feed m16n8k32 s8 MMAs unconverted (the A8 inner loop) and every partial sum
-// A_s = sum_k W[n, k] q_s[k] is an exact int32. y[b, n] = bf16( ((sum_s 256^s A_s) * scale[n]) * 2^E ), combined in
-// fp32: the sum is exact up to the fp32 rounding of the combination and of elements below |x| < 2^(E-1) (at most
-// 2^-(8 NSL - 2) of the token's absmax each), so the result is the exact dot product rounded, at least as accurate
-// as the reference's fp32 accumulation (kernels/lfm2_decode.cu:576-661). Every block slices x into shared memory
-// after its first weights are in flight (rows of K + 64 bytes, bank-conflict-free fragment loads).
-template <int KS, int NSL, int RING>
+// Weight-only GEMV on the int8 tensor path ("x-sliced"), for 1..4 tokens. Each token's bf16 activations are written
+// exactly as NSL = 3 byte fixed point, q = x * 2^-E with E from the token's absmax so that |q| < 2^22, and q is split
+// into 3 balanced signed bytes, q = sum_s q_s 256^s. The bytes of token b are the MMA columns 3 b + s (NT groups of 8
+// columns: 1 up to 2 tokens, 2 up to 4), so the int8 weights feed m16n8k32 s8 MMAs unconverted (the A8 inner loop)
+// and every partial sum A_s = sum_k W[n, k] q_s[k] is an exact int32. y[b, n] = bf16( ((sum_s 256^s A_s) * scale[n])
+// * 2^E ), combined in fp32. Every bf16 element within 2^14 of the token's absmax is represented exactly (8
+// significant bits above 2^E) and smaller ones to within 2^(E-1) <= 2^-22 of the absmax, so the result is the exact
+// dot product rounded, at least as accurate as the reference's fp32 accumulation (kernels/lfm2_decode.cu:576-661)
+// also with outlier channels. Every block slices x into shared memory after its first weights are in flight (rows of
+// K + 64 bytes, bank-conflict-free fragment loads).
+constexpr int XS_NSL = 3;
+template <int KS, int NT, int RING>
 __global__ void __launch_bounds__(GV_THREADS) gemv_xs_kernel(const int8_t *__restrict__ W, const float *__restrict__ scale,
                                                              const bf16 *__restrict__ x, bf16 *__restrict__ y, int N,
                                                              int K, int B, int pdl, const L2Prefetch pf) {
-  constexpr int RG = 8 / KS;
+  constexpr int RG = 8 / KS, NSL = XS_NSL;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x RING x 1 KB, then the sliced tokens
-  __shared__ int red[RG * KS * 16 * 8];
+  __shared__ int red[RG * KS * 16 * 8 * NT];
   __shared__ int e_s[4];
   __shared__ float red_max[4][8];
   if (pdl == 2) pdl_trigger();
@@ -218,22 +220,24 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_xs_kernel(const int8_t *__res
   int8_t *xs = reinterpret_cast<int8_t *>(rings + 8 * RING * 1024);
   {
     // stream the first set's weights before anything waits on the previous kernel
-    int dummy[1][4];
-    warp_gemv_a8<1, RING>(W, xs, xstride, N, K, B * NSL, (blockIdx.x * RG + rg) * 16, ks * kslice, (ks + 1) * kslice, dummy,
-                    rings + warp * RING * 1024, false, 1);
+    int dummy[NT][4];
+    warp_gemv_a8<NT, RING>(W, xs, xstride, N, K, B * NSL, (blockIdx.x * RG + rg) * 16, ks * kslice, (ks + 1) * kslice,
+                           dummy, rings + warp * RING * 1024, false, 1);
   }
   if (pdl) pdl_wait();
   slice_tokens<NSL>(x, K, B, xs, xstride, e_s, red_max);
   __syncthreads();
   for (int set = blockIdx.x; set < sets; set += gridDim.x) {
     const int r0 = (set * RG + rg) * 16;
-    int acc[1][4];
-    warp_gemv_a8<1, RING>(W, xs, xstride, N, K, B * NSL, r0, ks * kslice, (ks + 1) * kslice, acc,
-                    rings + warp * RING * 1024, false, set == blockIdx.x ? 2 : 0);
+    int acc[NT][4];
+    warp_gemv_a8<NT, RING>(W, xs, xstride, N, K, B * NSL, r0, ks * kslice, (ks + 1) * kslice, acc,
+                           rings + warp * RING * 1024, false, set == blockIdx.x ? 2 : 0);
     if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
-      red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 + frag_tok(lane, 0, e)] = acc[0][e];
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
     __syncthreads();
     for (int i = threadIdx.x; i < RG * 16 * B; i += GV_THREADS) {
       const int b = i % B, rr = (i / B) % 16, g2 = i / (16 * B);
@@ -244,13 +248,152 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_xs_kernel(const int8_t *__res
       for (int sl = NSL - 1; sl >= 0; --sl) {
         int a = 0;
 #pragma unroll
-        for (int s2 = 0; s2 < KS; ++s2) a += red[((g2 * KS + s2) * 16 + rr) * 8 + b * NSL + sl];
+        for (int s2 = 0; s2 < KS; ++s2) a += red[((g2 * KS + s2) * 16 + rr) * 8 * NT + b * NSL + sl];
         f = __fmaf_rn(f, 256.f, (float)a);
       }
       y[(size_t)b * N + n] = f2bf(ldexpf(__fmul_rn(f, scale[n]), e_s[b]));
     }
     __syncthreads();
   }
+}
+
+// x-sliced GEMV with deep weight prefetch, for decode chains. Same arithmetic as gemv_xs_kernel (the tokens sliced
+// into exact fixed-point bytes, exact int32 partials, the same fp32 combination), so the values are identical; the
+// schedule differs. Grid = at most one block per SM. Each warp's steps over all of its sets (row group x K-slice)
+// run through ONE ring of R 1 KB slots that continues across set boundaries, and the first R steps (up to 96 KB
+// per block) are requested before the dependency wait. With pdl == 2 the dependent launch is triggered at the
+// start; the block's shared memory stays below half an SM's, so the next GEMV's blocks are resident beside this one
+// and fill their own rings while this one waits, slices and computes. The weight stream of consecutive GEMVs thus
+// overlaps, instead of restarting from an empty pipe after every dependency (what bounds a chain of small GEMVs).
+template <int KS, int NT, int R>
+__global__ void __launch_bounds__(GV_THREADS, 2) gemv_deep_kernel(const int8_t *__restrict__ W,
+                                                                   const float *__restrict__ scale,
+                                                                   const bf16 *__restrict__ x, bf16 *__restrict__ y,
+                                                                   int N, int K, int B, int pdl, const L2Prefetch pf) {
+  constexpr int RG = 8 / KS, NSL = XS_NSL;
+  extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x R x 1 KB, then the sliced tokens
+  __shared__ int red[RG * KS * 16 * 8 * NT];
+  __shared__ int e_s[4];
+  __shared__ float red_max[4][8];
+  if (pdl == 2) pdl_trigger();
+  l2_prefetch_share(pf);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int rg = warp / KS, ks = warp % KS;
+  const int kslice = K / KS, nst = kslice / 64;
+  const int sets = ((N + 15) / 16 + RG - 1) / RG;
+  const int my_sets = (int)blockIdx.x < sets ? (sets - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = my_sets * nst;  // this warp's 64-wide K steps, over all of its sets
+  const int xstride = K + 64;
+  int8_t *xs = reinterpret_cast<int8_t *>(rings + 8 * R * 1024);
+  const uint32_t slot0 = (uint32_t)__cvta_generic_to_shared(rings + warp * R * 1024) + g * 64 + t * 16;
+
+  // issue cursor: the next step to request is step ist of set iset; rows g and g + 8 of its row group
+  int iset = blockIdx.x, ist = 0;
+  const int8_t *p0 = W, *p1 = W;
+  auto rows_of = [&](int set) {
+    const int r0 = (set * RG + rg) * 16;
+    p0 = W + (size_t)min(r0 + g, N - 1) * K + ks * kslice + t * 16;
+    p1 = W + (size_t)min(r0 + g + 8, N - 1) * K + ks * kslice + t * 16;
+  };
+  if (iset < sets) rows_of(iset);
+  auto issue = [&](int slot) {
+    if (iset < sets) {
+      const uint32_t d = slot0 + slot * 1024;
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(p0 + ist * 64) : "memory");
+      asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d + 512), "l"(p1 + ist * 64) : "memory");
+      if (++ist == nst) {
+        ist = 0;
+        iset += gridDim.x;
+        if (iset < sets) rows_of(iset);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  auto lds = [&](int slot, uint4 &w0, uint4 &w1) {
+    const uint32_t d = slot0 + slot * 1024;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w0.x), "=r"(w0.y), "=r"(w0.z), "=r"(w0.w) : "r"(d)
+                 : "memory");
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(w1.x), "=r"(w1.y), "=r"(w1.z), "=r"(w1.w)
+                 : "r"(d + 512)
+                 : "memory");
+  };
+  // MMA column c = g + 8 j holds token c / NSL, slice c % NSL (columns past B * NSL are zero)
+  const int8_t *xrow = xs + ks * kslice + t * 16;
+  auto ldx = [&](int st, uint4 (&xw)[NT]) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+      xw[j] = g + 8 * j < B * NSL ? *reinterpret_cast<const uint4 *>(xrow + (size_t)(g + 8 * j) * xstride + st * 64)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+  };
+
+#pragma unroll
+  for (int s = 0; s < R; ++s) issue(s);  // weights are immutable: requested before the dependency wait
+  if (pdl) pdl_wait();
+  slice_tokens<NSL>(x, K, B, xs, xstride, e_s, red_max);
+  __syncthreads();
+
+  uint4 wc0, wc1, xc[NT], wn0, wn1, xn[NT];
+  asm volatile("cp.async.wait_group %0;" ::"n"(R - 1) : "memory");
+  if (total > 0) {
+    lds(0, wc0, wc1);
+    ldx(0, xc);
+  }
+  int acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0;
+  int slot = 0, st = 0, set = blockIdx.x;
+  for (int c = 0; c < total; ++c) {
+    const int nslot = slot + 1 == R ? 0 : slot + 1;
+    const int nstp = st + 1 == nst ? 0 : st + 1;
+    if (c + 1 < total) {
+      asm volatile("cp.async.wait_group %0;" ::"n"(R - 2) : "memory");
+      lds(nslot, wn0, wn1);
+      ldx(nstp, xn);
+    }
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const uint32_t a[4] = {(&wc0.x)[2 * s], (&wc1.x)[2 * s], (&wc0.x)[2 * s + 1], (&wc1.x)[2 * s + 1]};
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mma_s8_16832(acc[j], a, (&xc[j].x)[2 * s], (&xc[j].x)[2 * s + 1]);
+    }
+    issue(slot);  // step c's slot (its data is in registers) takes step c + R
+    slot = nslot;
+    wc0 = wn0;
+    wc1 = wn1;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) xc[j] = xn[j];
+    st = nstp;
+    if (st == 0) {  // the set is complete: K-slices meet in shared memory, then the epilogue of gemv_xs_kernel
+      if (pdl == 1 && set + (int)gridDim.x >= sets) pdl_trigger();
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          red[((rg * KS + ks) * 16 + frag_row(lane, e)) * 8 * NT + frag_tok(lane, j, e)] = acc[j][e];
+          acc[j][e] = 0;
+        }
+      __syncthreads();
+      for (int i = threadIdx.x; i < RG * 16 * B; i += GV_THREADS) {
+        const int b = i % B, rr = (i / B) % 16, g2 = i / (16 * B);
+        const int n = (set * RG + g2) * 16 + rr;
+        if (n >= N) continue;
+        float f = 0.f;
+#pragma unroll
+        for (int sl = NSL - 1; sl >= 0; --sl) {
+          int a = 0;
+#pragma unroll
+          for (int s2 = 0; s2 < KS; ++s2) a += red[((g2 * KS + s2) * 16 + rr) * 8 * NT + b * NSL + sl];
+          f = __fmaf_rn(f, 256.f, (float)a);
+        }
+        y[(size_t)b * N + n] = f2bf(ldexpf(__fmul_rn(f, scale[n]), e_s[b]));
+      }
+      __syncthreads();
+      set += gridDim.x;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // Elementwise epilogue of the fused decode GEMVs on the NR bf16 GEMV values of output index n0 + threadIdx.x
@@ -390,7 +533,9 @@ constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
 constexpr int XS_RING = 6;  // ring depth of the x-sliced kernels (K steps of 1 KB per warp)
 constexpr int GV_X_SMEM_MAX = 64 * 1024;  // fused-quantization A8 GEMV: B * (K + 64) bytes of int8 tokens
 std::atomic<bool> g_early_trigger{false};
-std::atomic<int> g_gemv_impl{0};  // 0: x-sliced int8 path where it applies, 1: always the bf16-MMA path
+std::atomic<int> g_gemv_impl{0};  // 0: x-sliced int8 path where it applies, 1: always the bf16-MMA path,
+                                  // 2: the deep-prefetch x-sliced kernel wherever the slices fit
+std::atomic<bool> g_deep_late{false};  // deep kernel: trigger the dependent launch after the last set, not at start
 
 // (kernel, device) pairs whose dynamic shared memory limit has been raised
 std::mutex g_attr_mu;
@@ -543,54 +688,124 @@ cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const
   }
 }
 
-template <int KS, int NSL>
+template <int KS, int NT>
 cudaError_t gemv_xs_launch(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
                            cudaStream_t st, const L2Prefetch &pf) {
-  auto kern = gemv_xs_kernel<KS, NSL, XS_RING>;
+  auto kern = gemv_xs_kernel<KS, NT, XS_RING>;
   const int groups = (N + 15) / 16, rg = 8 / KS;
   const int sets = (groups + rg - 1) / rg;
-  const size_t dyn = (size_t)8 * XS_RING * 1024 + (size_t)B * NSL * (K + 64);
+  const size_t dyn = (size_t)8 * XS_RING * 1024 + (size_t)B * XS_NSL * (K + 64);
   const int resident = resident_blocks(kern, dyn);  // one wave: the grid strides over the sets
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
   return launch_dyn(kern, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
 }
 
-template <int NSL>
-cudaError_t gemv_xs_ks(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
-                       cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
+template <int NT>
+cudaError_t gemv_xs_nt(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
+                       cudaStream_t st, const L2Prefetch &pf) {
   switch (ks) {
-    case 1: return gemv_xs_launch<1, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
-    case 2: return gemv_xs_launch<2, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
-    case 4: return gemv_xs_launch<4, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
-    default: return gemv_xs_launch<8, NSL>(W, scale, x, y, N, K, B, pdl, st, pf);
+    case 1: return gemv_xs_launch<1, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
+    case 2: return gemv_xs_launch<2, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
+    case 4: return gemv_xs_launch<4, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
+    default: return gemv_xs_launch<8, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
   }
 }
 
-// Slices per token for the x-sliced path (0: the batch does not fit one MMA column tile, or its slices do not fit
-// the shared-memory budget): 3 bytes up to 2 tokens, 2 bytes up to 4.
+// the ring x-sliced kernel for B <= 4 tokens: one MMA column group (8 columns) up to 2 tokens, two up to 4
+cudaError_t gemv_xs_ks(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
+                       cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
+  return B * XS_NSL <= 8 ? gemv_xs_nt<1>(W, scale, x, y, N, K, B, ks, pdl, st, pf)
+                         : gemv_xs_nt<2>(W, scale, x, y, N, K, B, ks, pdl, st, pf);
+}
+
+// Deep-prefetch x-sliced GEMV (gemv_deep_kernel). Shared memory per block at most GV_DEEP_SMEM, so that two
+// blocks (this GEMV's and the next one's) fit on an SM.
+constexpr size_t GV_DEEP_SMEM = 104 * 1024;
+
+template <int NT, int R>
+cudaError_t gemv_deep_r(int ks, dim3 grid, size_t dyn, const int8_t *W, const float *scale, const bf16 *x, bf16 *y,
+                        int N, int K, int B, bool pdl, int p, cudaStream_t st, const L2Prefetch &pf) {
+  switch (ks) {
+    case 1: return launch_dyn(gemv_deep_kernel<1, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
+    case 2: return launch_dyn(gemv_deep_kernel<2, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
+    case 4: return launch_dyn(gemv_deep_kernel<4, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
+    default: return launch_dyn(gemv_deep_kernel<8, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
+  }
+}
+
+// K-slices for the deep kernel: the fewest that minimise the steps of the busiest warp, one block per SM
+int deep_ks(int N, int K, int sms) {
+  const long groups = (N + 15) / 16;
+  int best = 1;
+  long best_cost = -1;
+  for (int ks = 1; ks <= 8; ks *= 2) {
+    if ((K / 64) % ks) continue;
+    const long sets = (groups * ks + 7) / 8;
+    const long cost = (sets + sms - 1) / sms * (K / 64 / ks);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = ks;
+    }
+  }
+  return best;
+}
+
+// Ring depth that fits beside the token slices (0: none does)
+int deep_ring(int K, int B) {
+  const size_t xsb = (size_t)B * XS_NSL * (K + 64);
+  for (int r : {12, 10, 8, 6})
+    if ((size_t)r * 8 * 1024 + xsb <= GV_DEEP_SMEM) return r;
+  return 0;
+}
+
+cudaError_t gemv_deep(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
+                      cudaStream_t st, const L2Prefetch &pf) {
+  const int sms = device_sm_count();
+  const int ks = deep_ks(N, K, sms), R = deep_ring(K, B);
+  const long sets = ((long)(N + 15) / 16 * ks + 7) / 8;
+  const dim3 grid((unsigned)(sets < sms ? sets : sms));
+  const size_t dyn = (size_t)R * 8 * 1024 + (size_t)B * XS_NSL * (K + 64);
+  const int p = pdl ? (g_deep_late ? 1 : 2) : 0;
+  if (B * XS_NSL <= 8) {
+    switch (R) {
+      case 12: return gemv_deep_r<1, 12>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+      case 10: return gemv_deep_r<1, 10>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+      case 8: return gemv_deep_r<1, 8>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+      default: return gemv_deep_r<1, 6>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+    }
+  }
+  switch (R) {
+    case 12: return gemv_deep_r<2, 12>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+    case 10: return gemv_deep_r<2, 10>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+    case 8: return gemv_deep_r<2, 8>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+    default: return gemv_deep_r<2, 6>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+  }
+}
+
+// Slices per token for the x-sliced path: 3 for 1..4 tokens whose slices fit the shared-memory budget, else 0.
 int gemv_xs_slices(int K, int B) {
-  const int nsl = B <= 2 ? 3 : (B <= 4 ? 2 : 0);
-  if (nsl == 0 || (size_t)B * nsl * (K + 64) > (size_t)GV_X_SMEM_MAX || K % 64 != 0 || K > xs_max_k(B)) return 0;
-  return nsl;
+  if (B < 1 || B > 4 || (size_t)B * XS_NSL * (K + 64) > (size_t)GV_X_SMEM_MAX || K % 64 != 0 || K > xs_max_k(B))
+    return 0;
+  return XS_NSL;
 }
 
 void gemv_set_early_trigger(bool early) { g_early_trigger = early; }
 int gemv_trigger_mode() { return g_early_trigger ? 2 : 1; }
-void gemv_set_impl(int impl) { g_gemv_impl = impl; }
+void gemv_set_impl(int impl) {
+  g_gemv_impl = impl == 3 ? 2 : impl;
+  g_deep_late = impl == 3;
+}
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st) {
   if (N <= 0 || B <= 0) return cudaSuccess;
   // the sliced path's token prologue (absmax, slicing, two block barriers) costs ~0.4 us, which the faster weight
   // stream repays from ~8 M weights up; below that the bf16 path is quicker (measured on B200)
-  if (int8 && g_gemv_impl == 0 && (long)N * K >= 8L * 1024 * 1024) {
-    if (const int nsl = gemv_xs_slices(K, B)) {
-      const int ks = pick_ks(N, K, 64, rows);
-      return nsl == 3 ? gemv_xs_ks<3>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st)
-                      : gemv_xs_ks<2>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st);
-    }
-  }
+  if (int8 && g_gemv_impl == 2 && gemv_xs_slices(K, B) && deep_ring(K, B))
+    return gemv_deep((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pdl, st, kNoPrefetch);
+  if (int8 && g_gemv_impl == 0 && (long)N * K >= 8L * 1024 * 1024 && gemv_xs_slices(K, B))
+    return gemv_xs_ks((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pick_ks(N, K, 64, rows), pdl, st);
   if (int8)
     return gemv_dispatch<int8_t>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
   return gemv_dispatch<bf16>((const bf16 *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
@@ -601,10 +816,9 @@ cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void
 cudaError_t launch_gemv_pf(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
                            const L2Prefetch &pf, bool pdl, cudaStream_t st) {
   if (N <= 0 || B <= 0) return cudaSuccess;
-  if (const int nsl = gemv_xs_slices(K, B)) {
-    const int ks = pick_ks(N, K, 64, 0);
-    return nsl == 3 ? gemv_xs_ks<3>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st, pf)
-                    : gemv_xs_ks<2>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, ks, pdl, st, pf);
+  if (gemv_xs_slices(K, B)) {
+    if (g_gemv_impl == 2 && deep_ring(K, B)) return gemv_deep(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pdl, st, pf);
+    return gemv_xs_ks(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pick_ks(N, K, 64, 0), pdl, st, pf);
   }
   return gemv_dispatch<int8_t>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, 0, B, pdl, st, pf);
 }

@@ -251,8 +251,9 @@ __device__ __forceinline__ int frag_tok(int lane, int j, int e) { return 8 * j +
 constexpr int XS_CH = 8;
 // EO: within every 8-element chunk the bytes are stored in the order of the elements 0, 2, 4, 6, 1, 3, 5, 7 (the
 // order in which the INT4 GEMV unpacks a word of packed nibbles: low nibbles, then high nibbles).
-// csum (optional, needs K % 128 == 0): the sums of the slice bytes of every 128 elements, csum[blk * 8 + b * NSL + s]
-// for token b, slice s and block blk of 128 elements (16 chunks, held by 16 consecutive lanes).
+// csum (optional, needs K % 128 == 0, B * NSL <= 16): the sums of the slice bytes of every 128 elements,
+// csum[blk * 16 + b * NSL + s] for token b, slice s and block blk of 128 elements (16 chunks, held by 16 consecutive
+// lanes).
 template <int NSL, bool EO = false>
 __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride, int *e_s,
                                              float (&red_max)[4][8], int *csum = nullptr) {
@@ -351,7 +352,7 @@ __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, 
         int sum = __dp4a((int)o[sl][0], 0x01010101, __dp4a((int)o[sl][1], 0x01010101, 0));
 #pragma unroll
         for (int o2 = 8; o2 > 0; o2 >>= 1) sum += __shfl_xor_sync(half, sum, o2);
-        if ((lane & 15) == 0) csum[(c >> 4) * 8 + b * NSL + sl] = sum;
+        if ((lane & 15) == 0) csum[(c >> 4) * 16 + b * NSL + sl] = sum;
       }
     }
   }

@@ -31,9 +31,10 @@ SHAPES = [(3072, 2048), (6144, 2048), (2048, 2048), (16384, 2048), (2048, 8192),
           (1000, 1536)]
 
 
-@pytest.fixture(params=[0, 1], ids=["auto", "bf16path"])
+@pytest.fixture(params=[0, 1, 2], ids=["auto", "bf16path", "deep"])
 def gemv_path(request):
-    """0: the int8 path with the tokens sliced into exact fixed-point bytes (B <= 4), else bf16; 1: always bf16."""
+    """0: the int8 path with the tokens sliced into exact fixed-point bytes (B <= 4), else bf16; 1: always bf16;
+    2: the deep-prefetch sliced kernel wherever the slices fit."""
     from lfm2opt import _capi
     _capi.lib().lfm2q_set_gemv_path(request.param)
     yield request.param
@@ -45,7 +46,7 @@ def gemv_path(request):
 def test_gemv_int8(cuda_dev, gemv_path, N, K, B):
     if N * K > 40_000_000 and B not in (1, 8, 16):
         pytest.skip("large shape: a few batch sizes suffice")
-    if gemv_path == 1 and B > 4:
+    if gemv_path in (1, 2) and B > 4:
         pytest.skip("the path knob only matters for B <= 4")
     g = torch.Generator().manual_seed(N + K + B)
     W = (torch.randn(N, K, generator=g) * 0.02).to(BF)

@@ -32,8 +32,7 @@ def weights(N, K, seed, dev):
 
 def sliced_in_gemv(N, K, B):
     """Whether lfm2q_gemv runs its x-sliced int8 path for this shape (launch_gemv, gemv_xs_slices)."""
-    nsl = 3 if B <= 2 else (2 if B <= 4 else 0)
-    return N * K >= 8 * 1024 * 1024 and nsl and B * nsl * (K + 64) <= 64 * 1024 and K <= 16384 // B
+    return N * K >= 8 * 1024 * 1024 and B <= 4 and B * 3 * (K + 64) <= 64 * 1024 and K <= 16384 // B
 
 
 @pytest.mark.parametrize("B", [1, 2, 3, 4])

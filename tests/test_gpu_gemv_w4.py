@@ -150,3 +150,16 @@ def test_gemv_w4_against_reference_kernel(cuda_dev, N, K):
     ours = t(lambda: ext().gemv_w4(Wd, Sd, xd, y))
     ref = t(lambda: L.refk_gemv_w4(Wd.data_ptr(), Sd.data_ptr(), xd.data_ptr(), ry.data_ptr(), N, K, 128, st))
     print(f"\n[vs reference kernel] gemv_w4 {N}x{K}: lfm2q {ours:.1f} us, reference {ref:.1f} us ({ref / ours:.2f}x)")
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 4])
+def test_gemv_w4_outlier_channels_batched(cuda_dev, B):
+    """Outlier channels (x300) in every token of a batch: each token keeps 3 exact slice bytes whatever B, so the
+    small elements beside the outliers keep their bits and the result stays within the fp64 rounding bound."""
+    g = torch.Generator().manual_seed(70 + B)
+    N, K = 3072, 2048
+    Wp, S = quantize_int4((torch.randn(N, K, generator=g) * 0.02).to(BF))
+    x = torch.randn(B, K, generator=g)
+    x[:, :: K // 7] *= 300
+    x = x.to(BF)
+    check(run(Wp, S, x, 128, cuda_dev), Wp, S, x)
