@@ -135,9 +135,9 @@ int lfm2q_gemv_w4(const uint8_t *Wp, const float *S, const uint16_t *x, uint16_t
  * graph (src/lfm2opt/runtime.py:223-244, :247-294). The layers run in list order, each after the previous one has
  * completed (so a layer may read an earlier layer's y as its x); each is lfm2q_gemv with int8 weights, y = bf16((x .
  * W^T) * scale), computed on the int8 tensor path with the tokens sliced into exact fixed-point bytes where the
- * slices fit in shared memory (B * (B <= 2 ? 3 : 2) * (K + 64) <= 65536 and B * K <= 16384; else the bf16 path).
- * While a layer runs, the weights of the next layers of the list stream into L2, so small layers do not wait for
- * HBM. One kernel launch per layer, capturable in a CUDA graph; nothing is allocated. */
+ * slices fit in shared memory (B * 3 * (K + 64) <= 65536 and B * K <= 16384; else the bf16 path). For B <= 2 each
+ * layer is the deep-prefetch kernel: its blocks start while the previous layer runs and have their weights in flight
+ * before the dependency wait. One kernel launch per layer, capturable in a CUDA graph; nothing is allocated. */
 typedef struct {
   const int8_t *W;    /* int8 [N, K], 16-byte aligned */
   const float *scale; /* fp32 [N] */
@@ -167,11 +167,16 @@ int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, co
 void lfm2q_set_pdl(int on);
 void lfm2q_set_gemv_impl(int impl);
 
-/* Path of the int8 weight-only GEMV (lfm2q_gemv and lfm2q_gemv_epi with w_is_int8): 0 (default) = int8 tensor path
- * with the tokens sliced into exact fixed-point bytes where it applies (N * K >= 8 M for lfm2q_gemv, B <= 4,
- * B * slices * (K + 64) <= 64 KB), else the bf16 path; 1 = always the bf16 path (weights converted exactly to bf16,
- * bf16 MMAs). No counterpart in the reference
- * (its set_gemv_impl chooses how x is loaded, kernels/lfm2_decode.cu:662-675). Tuning and testing only. */
+/* Path of the int8 weight-only GEMV (lfm2q_gemv, lfm2q_gemv_chain and lfm2q_gemv_epi with w_is_int8). The int8
+ * tensor path slices the tokens into exact fixed-point bytes (B <= 4, B * 3 * (K + 64) <= 64 KB, K <= 16384 / B);
+ * two kernels implement it with identical values: the deep-prefetch kernel (one block per SM, weights requested
+ * before the dependency wait while the previous GEMV still runs) and the ring kernel.
+ *   0 (default): deep kernel for B <= 2; ring kernel for B = 3, 4 from N * K >= 8 M; else the bf16 path
+ *   1: always the bf16 path (weights converted exactly to bf16, bf16 MMAs)
+ *   2: deep kernel wherever the slices fit    3: as 2, next launch triggered after the last row group
+ *   4: ring kernel from N * K >= 8 M (the earlier default)
+ * No counterpart in the reference (its set_gemv_impl chooses how x is loaded, kernels/lfm2_decode.cu:662-675).
+ * Tuning and testing only; a process-wide setting. */
 void lfm2q_set_gemv_path(int path);
 
 /* GEMV kernels launched with Programmatic Dependent Launch let the next kernel launch after their K loop

@@ -107,7 +107,7 @@ void lfm2q_set_pdl(int on) {
 }
 void lfm2q_set_gemv_trigger(int early) { gemv_set_early_trigger(early != 0); }
 void lfm2q_set_gemv_impl(int) {}
-void lfm2q_set_gemv_path(int path) { gemv_set_impl(path >= 1 && path <= 3 ? path : 0); }
+void lfm2q_set_gemv_path(int path) { gemv_set_impl(path >= 1 && path <= 4 ? path : 0); }
 void lfm2q_set_gemm_tile(int bn) { gemm_set_tile_override(bn); }
 
 // ------------------------------------------------------------------ quantizers

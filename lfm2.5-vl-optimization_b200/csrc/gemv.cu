@@ -30,30 +30,14 @@ namespace {
 
 // Plain GEMV. Block = RG row groups x KS K-slices (RG * KS == 8 warps); blocks walk the row-group sets in a grid
 // stride (grid = min(sets, resident blocks)), so large N runs in one wave with balanced work.
-// This block's share of every range of pf requested into L2 (one bulk prefetch per range, thread 0).
-__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch &pf) {
-  if (threadIdx.x != 0) return;
-  for (int i = 0; i < pf.cnt; ++i) {
-    const unsigned long long chunk = ((pf.n[i] + gridDim.x - 1) / gridDim.x + 255) / 256 * 256;
-    const unsigned long long lo = chunk * blockIdx.x;
-    if (lo < pf.n[i]) {
-      const unsigned long long len = pf.n[i] - lo < chunk ? pf.n[i] - lo : chunk;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char *>(pf.p[i]) + lo),
-                   "r"((uint32_t)len)
-                   : "memory");
-    }
-  }
-}
-
 template <typename WT, int NT, int KS>
 __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const WT *__restrict__ W, const float *__restrict__ scale,
                                                           const bf16 *__restrict__ x, bf16 *__restrict__ y, int N, int K,
-                                                          int B, int pdl, const L2Prefetch pf) {
+                                                          int B, int pdl) {
   constexpr int RG = 8 / KS;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x GV_RING x 1 KB
   __shared__ float red[(KS > 1) ? RG * KS * 16 * 8 * NT : 1];
   if (pdl == 2) pdl_trigger();
-  l2_prefetch_share(pf);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
@@ -204,14 +188,13 @@ constexpr int XS_NSL = 3;
 template <int KS, int NT, int RING>
 __global__ void __launch_bounds__(GV_THREADS) gemv_xs_kernel(const int8_t *__restrict__ W, const float *__restrict__ scale,
                                                              const bf16 *__restrict__ x, bf16 *__restrict__ y, int N,
-                                                             int K, int B, int pdl, const L2Prefetch pf) {
+                                                             int K, int B, int pdl) {
   constexpr int RG = 8 / KS, NSL = XS_NSL;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x RING x 1 KB, then the sliced tokens
   __shared__ int red[RG * KS * 16 * 8 * NT];
   __shared__ int e_s[4];
   __shared__ float red_max[4][8];
   if (pdl == 2) pdl_trigger();
-  l2_prefetch_share(pf);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS;
@@ -269,14 +252,13 @@ template <int KS, int NT, int R>
 __global__ void __launch_bounds__(GV_THREADS, 2) gemv_deep_kernel(const int8_t *__restrict__ W,
                                                                    const float *__restrict__ scale,
                                                                    const bf16 *__restrict__ x, bf16 *__restrict__ y,
-                                                                   int N, int K, int B, int pdl, const L2Prefetch pf) {
+                                                                   int N, int K, int B, int pdl) {
   constexpr int RG = 8 / KS, NSL = XS_NSL;
   extern __shared__ __align__(128) uint8_t rings[];  // 8 warps x R x 1 KB, then the sliced tokens
   __shared__ int red[RG * KS * 16 * 8 * NT];
   __shared__ int e_s[4];
   __shared__ float red_max[4][8];
   if (pdl == 2) pdl_trigger();
-  l2_prefetch_share(pf);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int rg = warp / KS, ks = warp % KS;
   const int kslice = K / KS, nst = kslice / 64;
@@ -328,6 +310,18 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_deep_kernel(const int8_t *
 
 #pragma unroll
   for (int s = 0; s < R; ++s) issue(s);  // weights are immutable: requested before the dependency wait
+  // the weight-row scales the epilogue items i = tid, tid + 256 of a set need, loaded a set ahead (the first set's
+  // before the dependency wait), so no global load sits on the epilogue's critical path
+  float sc[2] = {0.f, 0.f};
+  auto scales_of = [&](int set) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = threadIdx.x + k * GV_THREADS;
+      const int n = (set * RG + i / (16 * B)) * 16 + (i / B) % 16;
+      if (set < sets && i < RG * 16 * B && n < N) sc[k] = __ldg(scale + n);
+    }
+  };
+  scales_of(blockIdx.x);
   if (pdl) pdl_wait();
   slice_tokens<NSL>(x, K, B, xs, xstride, e_s, red_max);
   __syncthreads();
@@ -375,7 +369,10 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_deep_kernel(const int8_t *
           acc[j][e] = 0;
         }
       __syncthreads();
-      for (int i = threadIdx.x; i < RG * 16 * B; i += GV_THREADS) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int i = threadIdx.x + k * GV_THREADS;
+        if (i >= RG * 16 * B) break;
         const int b = i % B, rr = (i / B) % 16, g2 = i / (16 * B);
         const int n = (set * RG + g2) * 16 + rr;
         if (n >= N) continue;
@@ -387,10 +384,11 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_deep_kernel(const int8_t *
           for (int s2 = 0; s2 < KS; ++s2) a += red[((g2 * KS + s2) * 16 + rr) * 8 * NT + b * NSL + sl];
           f = __fmaf_rn(f, 256.f, (float)a);
         }
-        y[(size_t)b * N + n] = f2bf(ldexpf(__fmul_rn(f, scale[n]), e_s[b]));
+        y[(size_t)b * N + n] = f2bf(ldexpf(__fmul_rn(f, sc[k]), e_s[b]));
       }
       __syncthreads();
       set += gridDim.x;
+      scales_of(set);
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -533,8 +531,10 @@ constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
 constexpr int XS_RING = 6;  // ring depth of the x-sliced kernels (K steps of 1 KB per warp)
 constexpr int GV_X_SMEM_MAX = 64 * 1024;  // fused-quantization A8 GEMV: B * (K + 64) bytes of int8 tokens
 std::atomic<bool> g_early_trigger{false};
-std::atomic<int> g_gemv_impl{0};  // 0: x-sliced int8 path where it applies, 1: always the bf16-MMA path,
-                                  // 2: the deep-prefetch x-sliced kernel wherever the slices fit
+// 0 (default): deep-prefetch x-sliced kernel for 1-2 tokens, ring x-sliced kernel for 3-4 tokens from 8 M weights,
+// else the bf16-MMA path; 1: always the bf16-MMA path; 2: the deep kernel wherever the slices fit; 4: the ring
+// x-sliced kernel from 8 M weights (the deep kernel's predecessor, for comparisons)
+std::atomic<int> g_gemv_impl{0};
 std::atomic<bool> g_deep_late{false};  // deep kernel: trigger the dependent launch after the last set, not at start
 
 // (kernel, device) pairs whose dynamic shared memory limit has been raised
@@ -605,21 +605,19 @@ cudaError_t launch_ex(KernelT kernel, dim3 grid, dim3 block, bool pdl, cudaStrea
   return launch_dyn(kernel, grid, block, pdl, st, GV_DYN_SMEM + extra_smem, args...);
 }
 
-const L2Prefetch kNoPrefetch = {};
-
 template <typename WT, int NT>
 cudaError_t gemv_ks(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
-                    cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
+                    cudaStream_t st) {
   const int groups = (N + 15) / 16, rg = 8 / ks;
   const int sets = (groups + rg - 1) / rg;
   const int resident = 4 * device_sm_count();  // 48 KB of rings per block: 4 blocks per SM
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
   switch (ks) {
-    case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
-    case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
-    case 4: return launch_ex(gemv_kernel<WT, NT, 4>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
-    default: return launch_ex(gemv_kernel<WT, NT, 8>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p, pf);
+    case 1: return launch_ex(gemv_kernel<WT, NT, 1>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
+    case 2: return launch_ex(gemv_kernel<WT, NT, 2>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
+    case 4: return launch_ex(gemv_kernel<WT, NT, 4>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
+    default: return launch_ex(gemv_kernel<WT, NT, 8>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, N, K, B, p);
   }
 }
 
@@ -635,14 +633,14 @@ int pick_ks(int N, int K, int kstep, int rows_override) {
 
 template <typename WT>
 cudaError_t gemv_dispatch(const WT *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int rows, int B,
-                          bool pdl, cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
+                          bool pdl, cudaStream_t st) {
   const int ks = pick_ks(N, K, WFmt<WT>::KSTEP, rows);
   for (int b0 = 0; b0 < B; b0 += 16) {
     const int bs = min(16, B - b0);
     const bf16 *xb = x + (size_t)b0 * K;
     bf16 *yb = y + (size_t)b0 * N;
-    const cudaError_t e = bs > 8 ? gemv_ks<WT, 2>(W, scale, xb, yb, N, K, bs, ks, pdl, st, b0 ? kNoPrefetch : pf)
-                                 : gemv_ks<WT, 1>(W, scale, xb, yb, N, K, bs, ks, pdl, st, b0 ? kNoPrefetch : pf);
+    const cudaError_t e = bs > 8 ? gemv_ks<WT, 2>(W, scale, xb, yb, N, K, bs, ks, pdl, st)
+                                 : gemv_ks<WT, 1>(W, scale, xb, yb, N, K, bs, ks, pdl, st);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -653,7 +651,7 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
                               bf16 *state, const bf16 *cw, const bf16 *cbias, bool pdl, cudaStream_t st) {
   const dim3 grid((S + 15) / 16);
   const int p = pdl ? 1 : 0;
-  if (sizeof(WT) == 1 && g_gemv_impl == 0 && 3 * (size_t)(K + 64) <= (size_t)GV_X_SMEM_MAX && K % 256 == 0 &&
+  if (sizeof(WT) == 1 && g_gemv_impl != 1 && 3 * (size_t)(K + 64) <= (size_t)GV_X_SMEM_MAX && K % 256 == 0 &&
       K <= xs_max_k(1)) {
     const int8_t *Wi = reinterpret_cast<const int8_t *>(W);
     const size_t dyn = (size_t)8 * XS_RING * 1024 + 3 * (size_t)(K + 64);
@@ -690,7 +688,7 @@ cudaError_t gemv_a8_ks(const int8_t *W, const float *sw, const int8_t *xq, const
 
 template <int KS, int NT>
 cudaError_t gemv_xs_launch(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
-                           cudaStream_t st, const L2Prefetch &pf) {
+                           cudaStream_t st) {
   auto kern = gemv_xs_kernel<KS, NT, XS_RING>;
   const int groups = (N + 15) / 16, rg = 8 / KS;
   const int sets = (groups + rg - 1) / rg;
@@ -698,25 +696,25 @@ cudaError_t gemv_xs_launch(const int8_t *W, const float *scale, const bf16 *x, b
   const int resident = resident_blocks(kern, dyn);  // one wave: the grid strides over the sets
   const dim3 grid(sets < resident ? sets : resident);
   const int p = pdl ? (g_early_trigger ? 2 : 1) : 0;
-  return launch_dyn(kern, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
+  return launch_dyn(kern, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p);
 }
 
 template <int NT>
 cudaError_t gemv_xs_nt(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
-                       cudaStream_t st, const L2Prefetch &pf) {
+                       cudaStream_t st) {
   switch (ks) {
-    case 1: return gemv_xs_launch<1, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
-    case 2: return gemv_xs_launch<2, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
-    case 4: return gemv_xs_launch<4, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
-    default: return gemv_xs_launch<8, NT>(W, scale, x, y, N, K, B, pdl, st, pf);
+    case 1: return gemv_xs_launch<1, NT>(W, scale, x, y, N, K, B, pdl, st);
+    case 2: return gemv_xs_launch<2, NT>(W, scale, x, y, N, K, B, pdl, st);
+    case 4: return gemv_xs_launch<4, NT>(W, scale, x, y, N, K, B, pdl, st);
+    default: return gemv_xs_launch<8, NT>(W, scale, x, y, N, K, B, pdl, st);
   }
 }
 
 // the ring x-sliced kernel for B <= 4 tokens: one MMA column group (8 columns) up to 2 tokens, two up to 4
 cudaError_t gemv_xs_ks(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, int ks, bool pdl,
-                       cudaStream_t st, const L2Prefetch &pf = kNoPrefetch) {
-  return B * XS_NSL <= 8 ? gemv_xs_nt<1>(W, scale, x, y, N, K, B, ks, pdl, st, pf)
-                         : gemv_xs_nt<2>(W, scale, x, y, N, K, B, ks, pdl, st, pf);
+                       cudaStream_t st) {
+  return B * XS_NSL <= 8 ? gemv_xs_nt<1>(W, scale, x, y, N, K, B, ks, pdl, st)
+                         : gemv_xs_nt<2>(W, scale, x, y, N, K, B, ks, pdl, st);
 }
 
 // Deep-prefetch x-sliced GEMV (gemv_deep_kernel). Shared memory per block at most GV_DEEP_SMEM, so that two
@@ -725,30 +723,35 @@ constexpr size_t GV_DEEP_SMEM = 104 * 1024;
 
 template <int NT, int R>
 cudaError_t gemv_deep_r(int ks, dim3 grid, size_t dyn, const int8_t *W, const float *scale, const bf16 *x, bf16 *y,
-                        int N, int K, int B, bool pdl, int p, cudaStream_t st, const L2Prefetch &pf) {
+                        int N, int K, int B, bool pdl, int p, cudaStream_t st) {
   switch (ks) {
-    case 1: return launch_dyn(gemv_deep_kernel<1, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
-    case 2: return launch_dyn(gemv_deep_kernel<2, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
-    case 4: return launch_dyn(gemv_deep_kernel<4, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
-    default: return launch_dyn(gemv_deep_kernel<8, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p, pf);
+    case 1: return launch_dyn(gemv_deep_kernel<1, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p);
+    case 2: return launch_dyn(gemv_deep_kernel<2, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p);
+    case 4: return launch_dyn(gemv_deep_kernel<4, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p);
+    default: return launch_dyn(gemv_deep_kernel<8, NT, R>, grid, GV_THREADS, pdl, st, dyn, W, scale, x, y, N, K, B, p);
   }
 }
 
-// K-slices for the deep kernel: the fewest that minimise the steps of the busiest warp, one block per SM
+// K-slices for the deep kernel. Cost of a choice = sets per block x (steps per set + ~3 steps of per-set epilogue:
+// block barriers and the reduction of the K-slices); a large GEMV (>= 16 M weights) also needs a block on every SM,
+// because one SM streams only ~40-50 GB/s (measured: 16384 x 2048 on 128 blocks, 8.5 us; on 148, 6.9 us).
 int deep_ks(int N, int K, int sms) {
   const long groups = (N + 15) / 16;
-  int best = 1;
-  long best_cost = -1;
-  for (int ks = 1; ks <= 8; ks *= 2) {
-    if ((K / 64) % ks) continue;
-    const long sets = (groups * ks + 7) / 8;
-    const long cost = (sets + sms - 1) / sms * (K / 64 / ks);
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = ks;
+  const bool big = (long)N * K >= 16L * 1024 * 1024;
+  int best = 0;
+  long best_cost = 0;
+  for (int pass = 0; pass < 2 && !best; ++pass)
+    for (int ks = 1; ks <= 8; ks *= 2) {
+      if ((K / 64) % ks) continue;
+      const long sets = (groups * ks + 7) / 8;
+      if (pass == 0 && big && sets < sms) continue;
+      const long cost = (sets + sms - 1) / sms * (K / 64 / ks + 3);
+      if (!best || cost < best_cost) {
+        best_cost = cost;
+        best = ks;
+      }
     }
-  }
-  return best;
+  return best ? best : 1;
 }
 
 // Ring depth that fits beside the token slices (0: none does)
@@ -760,7 +763,7 @@ int deep_ring(int K, int B) {
 }
 
 cudaError_t gemv_deep(const int8_t *W, const float *scale, const bf16 *x, bf16 *y, int N, int K, int B, bool pdl,
-                      cudaStream_t st, const L2Prefetch &pf) {
+                      cudaStream_t st) {
   const int sms = device_sm_count();
   const int ks = deep_ks(N, K, sms), R = deep_ring(K, B);
   const long sets = ((long)(N + 15) / 16 * ks + 7) / 8;
@@ -769,17 +772,17 @@ cudaError_t gemv_deep(const int8_t *W, const float *scale, const bf16 *x, bf16 *
   const int p = pdl ? (g_deep_late ? 1 : 2) : 0;
   if (B * XS_NSL <= 8) {
     switch (R) {
-      case 12: return gemv_deep_r<1, 12>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
-      case 10: return gemv_deep_r<1, 10>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
-      case 8: return gemv_deep_r<1, 8>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
-      default: return gemv_deep_r<1, 6>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+      case 12: return gemv_deep_r<1, 12>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
+      case 10: return gemv_deep_r<1, 10>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
+      case 8: return gemv_deep_r<1, 8>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
+      default: return gemv_deep_r<1, 6>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
     }
   }
   switch (R) {
-    case 12: return gemv_deep_r<2, 12>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
-    case 10: return gemv_deep_r<2, 10>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
-    case 8: return gemv_deep_r<2, 8>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
-    default: return gemv_deep_r<2, 6>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st, pf);
+    case 12: return gemv_deep_r<2, 12>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
+    case 10: return gemv_deep_r<2, 10>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
+    case 8: return gemv_deep_r<2, 8>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
+    default: return gemv_deep_r<2, 6>(ks, grid, dyn, W, scale, x, y, N, K, B, pdl, p, st);
   }
 }
 
@@ -794,17 +797,18 @@ void gemv_set_early_trigger(bool early) { g_early_trigger = early; }
 int gemv_trigger_mode() { return g_early_trigger ? 2 : 1; }
 void gemv_set_impl(int impl) {
   g_gemv_impl = impl == 3 ? 2 : impl;
-  g_deep_late = impl == 3;
+  g_deep_late = impl == 3;  // 3: the deep kernel everywhere, dependent launch triggered after the last set
 }
 
 cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows,
                         int B, bool pdl, cudaStream_t st) {
   if (N <= 0 || B <= 0) return cudaSuccess;
-  // the sliced path's token prologue (absmax, slicing, two block barriers) costs ~0.4 us, which the faster weight
-  // stream repays from ~8 M weights up; below that the bf16 path is quicker (measured on B200)
-  if (int8 && g_gemv_impl == 2 && gemv_xs_slices(K, B) && deep_ring(K, B))
-    return gemv_deep((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pdl, st, kNoPrefetch);
-  if (int8 && g_gemv_impl == 0 && (long)N * K >= 8L * 1024 * 1024 && gemv_xs_slices(K, B))
+  const int impl = g_gemv_impl;
+  if (int8 && impl != 1 && impl != 4 && (B <= 2 || impl == 2) && gemv_xs_slices(K, B) && deep_ring(K, B))
+    return gemv_deep((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pdl, st);
+  // the ring kernel's token prologue (absmax, slicing, two block barriers) is repaid by its faster weight stream
+  // from ~8 M weights up; below that the bf16 path is quicker (measured on B200)
+  if (int8 && impl != 1 && (long)N * K >= 8L * 1024 * 1024 && gemv_xs_slices(K, B))
     return gemv_xs_ks((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pick_ks(N, K, 64, rows), pdl, st);
   if (int8)
     return gemv_dispatch<int8_t>((const int8_t *)W, scale, (const bf16 *)x, (bf16 *)y, N, K, rows, B, pdl, st);
@@ -812,15 +816,17 @@ cudaError_t launch_gemv(const void *W, bool int8, const float *scale, const void
 }
 
 // One GEMV of a chain: the x-sliced int8 path wherever its token buffer fits (the chain's contract: every layer gives
-// the sliced path's exact-product values), else the bf16 path; both issue the prefetch list first.
-cudaError_t launch_gemv_pf(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
-                           const L2Prefetch &pf, bool pdl, cudaStream_t st) {
+// the sliced path's exact-product values), else the bf16 path.
+cudaError_t launch_gemv_sliced(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
+                               bool pdl, cudaStream_t st) {
   if (N <= 0 || B <= 0) return cudaSuccess;
   if (gemv_xs_slices(K, B)) {
-    if (g_gemv_impl == 2 && deep_ring(K, B)) return gemv_deep(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pdl, st, pf);
-    return gemv_xs_ks(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pick_ks(N, K, 64, 0), pdl, st, pf);
+    const int impl = g_gemv_impl;
+    if (impl != 4 && (B <= 2 || impl == 2) && deep_ring(K, B))
+      return gemv_deep(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pdl, st);
+    return gemv_xs_ks(W, scale, (const bf16 *)x, (bf16 *)y, N, K, B, pick_ks(N, K, 64, 0), pdl, st);
   }
-  return gemv_dispatch<int8_t>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, 0, B, pdl, st, pf);
+  return gemv_dispatch<int8_t>(W, scale, (const bf16 *)x, (bf16 *)y, N, K, 0, B, pdl, st);
 }
 
 cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,

@@ -254,38 +254,41 @@ constexpr int XS_CH = 8;
 // csum (optional, needs K % 128 == 0, B * NSL <= 16): the sums of the slice bytes of every 128 elements,
 // csum[blk * 16 + b * NSL + s] for token b, slice s and block blk of 128 elements (16 chunks, held by 16 consecutive
 // lanes).
-template <int NSL, bool EO = false>
-__device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride, int *e_s,
-                                             float (&red_max)[4][8], int *csum = nullptr) {
+// J: chunks per thread, a compile-time bound (J * 256 >= B * K / 8), so the register array and every loop are sized
+// to the case at hand (a single-token K = 2048 call runs one chunk per thread without any idle iteration).
+template <int NSL, bool EO, int J>
+__device__ __forceinline__ void slice_tokens_j(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride,
+                                               int *e_s, float (&red_max)[4][8], int *csum) {
   constexpr int QBITS = 8 * NSL - 2;  // |q| < 2^QBITS
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K8 = K / 8, total = B * K8;
-  // this thread's chunks over all tokens: index i = tid + j * 256 -> token i / K8, chunk i % K8
-  uint4 v[XS_CH];
+  // token of chunk i (B <= 4), by comparisons
+  auto tok = [K8](int i) { return (int)(i >= K8) + (int)(i >= 2 * K8) + (int)(i >= 3 * K8); };
+  // this thread's chunks over all tokens: index i = tid + j * 256 -> token tok(i), chunk i - tok(i) * K8
+  uint4 v[J];
 #pragma unroll
-  for (int j = 0; j < XS_CH; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int i = threadIdx.x + j * GV_THREADS;
     v[j] = i < total ? ld_cg16(reinterpret_cast<const uint4 *>(x) + i) : make_uint4(0u, 0u, 0u, 0u);
   }
   {
     float m[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < XS_CH; ++j) {
-      if (threadIdx.x + j * GV_THREADS < total) {
-        const int b = (threadIdx.x + j * GV_THREADS) / K8;
-        const uint32_t m2 = __vmaxu2(__vmaxu2(v[j].x & 0x7FFF7FFFu, v[j].y & 0x7FFF7FFFu),
-                                     __vmaxu2(v[j].z & 0x7FFF7FFFu, v[j].w & 0x7FFF7FFFu));
-        const float mm = fmaxf(bf_lo(m2), bf_hi(m2));
+    for (int j = 0; j < J; ++j) {
+      if (j * GV_THREADS >= total) break;  // uniform; chunks past the end are zero and leave the maxima unchanged
+      const int b = tok(threadIdx.x + j * GV_THREADS);
+      const uint32_t m2 = __vmaxu2(__vmaxu2(v[j].x & 0x7FFF7FFFu, v[j].y & 0x7FFF7FFFu),
+                                   __vmaxu2(v[j].z & 0x7FFF7FFFu, v[j].w & 0x7FFF7FFFu));
+      const float mm = fmaxf(bf_lo(m2), bf_hi(m2));
 #pragma unroll
-        for (int bb = 0; bb < 4; ++bb)
-          if (bb == b) m[bb] = fmaxf(m[bb], mm);
+      for (int bb = 0; bb < 4; ++bb) m[bb] = bb == b ? fmaxf(m[bb], mm) : m[bb];
+    }
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb)
+      if (bb < B) {  // B is uniform: the whole warp takes part in each reduction it reaches
+        const float w = warp_max(m[bb]);
+        if (lane == 0) red_max[bb][warp] = w;
       }
-    }
-#pragma unroll
-    for (int bb = 0; bb < 4; ++bb) {
-      const float w = warp_max(m[bb]);
-      if (lane == 0 && bb < B) red_max[bb][warp] = w;
-    }
   }
   __syncthreads();
   int E[4], f1b[4], f2b[4];
@@ -307,10 +310,11 @@ __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, 
   if (threadIdx.x < B)
     e_s[threadIdx.x] = threadIdx.x == 0 ? E[0] : (threadIdx.x == 1 ? E[1] : (threadIdx.x == 2 ? E[2] : E[3]));
 #pragma unroll
-  for (int j = 0; j < XS_CH; ++j) {
+  for (int j = 0; j < J; ++j) {
+    if (j * GV_THREADS >= total) break;  // uniform
     const int i = threadIdx.x + j * GV_THREADS;
     if (i >= total) continue;  // whole 16-lane halves drop out together when total % 16 == 0
-    const int b = i / K8, c = i - b * K8;
+    const int b = tok(i), c = i - b * K8;
     int fb1 = f1b[0], fb2 = f2b[0];
 #pragma unroll
     for (int bb = 1; bb < 4; ++bb)
@@ -320,27 +324,29 @@ __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, 
       }
     const float f1 = __int_as_float(fb1), f2 = __int_as_float(fb2);
     const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    // q = round(x 2^-E) (exact scaling, one rounding) is written in balanced bytes q = sum_s q_s 256^s. With
+    // u = q + 128 (1 + 256 + ...), |q| <= 2^QBITS, every base-256 digit of u is q_s + 128 (no carries), so the slice
+    // bytes are u's bytes with the top bit flipped. u comes from one add: y + 1.5 2^23 rounds y to an integer (round
+    // to nearest even, as __float2int_rn) in the low mantissa bits, |y| <= 2^22.
+    constexpr uint32_t BIAS = NSL == 3 ? 0x808080u : (NSL == 2 ? 0x8080u : 0x80u);
+    constexpr uint32_t MAGIC = 0x4B400000u - BIAS;
+    uint32_t u[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float xv = (e & 1) ? bf_hi(w[e >> 1]) : bf_lo(w[e >> 1]);
+      u[e] = (uint32_t)__float_as_int(__fadd_rn(__fmul_rn(__fmul_rn(xv, f1), f2), 12582912.f)) - MAGIC;
+    }
     uint32_t o[NSL][2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      uint32_t acc[NSL];
+      // byte e of word h holds element 4h + e (EO: 2e + h) of the chunk
+      const int e0 = EO ? h : 4 * h, de = EO ? 2 : 1;
 #pragma unroll
-      for (int sl = 0; sl < NSL; ++sl) acc[sl] = 0u;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        // element 4h + e (EO: 2e + h) of the chunk
-        const float xv = EO ? (h ? bf_hi(w[e]) : bf_lo(w[e]))
-                            : ((e & 1) ? bf_hi(w[2 * h + (e >> 1)]) : bf_lo(w[2 * h + (e >> 1)]));
-        int q = __float2int_rn(__fmul_rn(__fmul_rn(xv, f1), f2));  // exact scaling, one rounding
-#pragma unroll
-        for (int sl = 0; sl < NSL; ++sl) {
-          const int qs = ((q + 128) & 255) - 128;  // balanced byte: q = qs + 256 * q'
-          acc[sl] |= (uint32_t)(qs & 255) << (8 * e);
-          q = (q - qs) >> 8;
-        }
+      for (int sl = 0; sl < NSL; ++sl) {
+        const uint32_t sel = sl | ((sl + 4) << 4);  // byte sl of each operand into bytes 0, 1
+        const uint32_t lo = __byte_perm(u[e0], u[e0 + de], sel), hi = __byte_perm(u[e0 + 2 * de], u[e0 + 3 * de], sel);
+        o[sl][h] = __byte_perm(lo, hi, 0x5410) ^ 0x80808080u;
       }
-#pragma unroll
-      for (int sl = 0; sl < NSL; ++sl) o[sl][h] = acc[sl];
     }
 #pragma unroll
     for (int sl = 0; sl < NSL; ++sl)
@@ -356,6 +362,16 @@ __device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, 
       }
     }
   }
+}
+
+template <int NSL, bool EO = false>
+__device__ __forceinline__ void slice_tokens(const bf16 *__restrict__ x, int K, int B, int8_t *xs, int xstride, int *e_s,
+                                             float (&red_max)[4][8], int *csum = nullptr) {
+  const int total = B * (K / 8);
+  if (total <= GV_THREADS) slice_tokens_j<NSL, EO, 1>(x, K, B, xs, xstride, e_s, red_max, csum);
+  else if (total <= 2 * GV_THREADS) slice_tokens_j<NSL, EO, 2>(x, K, B, xs, xstride, e_s, red_max, csum);
+  else if (total <= 4 * GV_THREADS) slice_tokens_j<NSL, EO, 4>(x, K, B, xs, xstride, e_s, red_max, csum);
+  else slice_tokens_j<NSL, EO, XS_CH>(x, K, B, xs, xstride, e_s, red_max, csum);
 }
 
 // Largest K the sliced path handles for B tokens (chunks held in registers by the 256 threads of a block)

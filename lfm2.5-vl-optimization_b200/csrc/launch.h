@@ -38,15 +38,7 @@ cudaError_t launch_gemv_a8(const int8_t *W, const float *sw, const int8_t *xq, c
 cudaError_t launch_gemv_epi(int epi, const void *W, bool int8, const float *scale, const void *x, void *y, int S, int K,
                             void *state, const void *cw, const void *cbias, bool pdl, cudaStream_t st);
 
-// Bulk L2 prefetch ranges a GEMV launch issues when it starts (before its dependency wait): every block requests its
-// share of each range into L2. Used by the chained GEMV to stream the weights of the layers ahead.
-struct L2Prefetch {
-  const void *p[8];
-  unsigned long long n[8];  // bytes, multiples of 16; p 16-byte aligned
-  int cnt;
-};
-
-// gemv_chain.cu: a list of weight-only int8 GEMVs, one PDL launch each, with an L2 prefetch window ahead of them
+// gemv_chain.cu: a list of weight-only int8 GEMVs, one PDL launch each
 constexpr int CHAIN_MAX = 96;
 constexpr int CHAIN_MAX_TOKENS = 4;
 struct ChainLayer {
@@ -58,8 +50,8 @@ struct ChainLayer {
 };
 cudaError_t launch_gemv_chain(const ChainLayer *layers, int n, int B, bool pdl, cudaStream_t st);
 // gemv.cu: one weight-only int8 GEMV of a chain (the x-sliced path where it applies, else the bf16 path)
-cudaError_t launch_gemv_pf(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
-                           const L2Prefetch &pf, bool pdl, cudaStream_t st);
+cudaError_t launch_gemv_sliced(const int8_t *W, const float *scale, const void *x, void *y, int N, int K, int B,
+                               bool pdl, cudaStream_t st);
 
 // gemv_w4.cu: INT4 weight-only GEMV (packed nibbles, one fp32 scale per group of `group` inputs, group % 128 == 0)
 int gemv_w4_slices(int K, int B);  // 0: this K / B does not fit the kernel's shared memory

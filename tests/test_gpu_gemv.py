@@ -31,10 +31,11 @@ SHAPES = [(3072, 2048), (6144, 2048), (2048, 2048), (16384, 2048), (2048, 8192),
           (1000, 1536)]
 
 
-@pytest.fixture(params=[0, 1, 2], ids=["auto", "bf16path", "deep"])
+@pytest.fixture(params=[0, 1, 2, 4], ids=["auto", "bf16path", "deep", "ring"])
 def gemv_path(request):
-    """0: the int8 path with the tokens sliced into exact fixed-point bytes (B <= 4), else bf16; 1: always bf16;
-    2: the deep-prefetch sliced kernel wherever the slices fit."""
+    """0: the int8 path with the tokens sliced into exact fixed-point bytes (deep kernel up to 2 tokens, ring kernel
+    for 3-4 from 8 M weights), else bf16; 1: always bf16; 2: the deep kernel wherever the slices fit; 4: the ring
+    kernel from 8 M weights."""
     from lfm2opt import _capi
     _capi.lib().lfm2q_set_gemv_path(request.param)
     yield request.param
@@ -46,7 +47,7 @@ def gemv_path(request):
 def test_gemv_int8(cuda_dev, gemv_path, N, K, B):
     if N * K > 40_000_000 and B not in (1, 8, 16):
         pytest.skip("large shape: a few batch sizes suffice")
-    if gemv_path in (1, 2) and B > 4:
+    if gemv_path in (1, 2, 4) and B > 4:
         pytest.skip("the path knob only matters for B <= 4")
     g = torch.Generator().manual_seed(N + K + B)
     W = (torch.randn(N, K, generator=g) * 0.02).to(BF)
@@ -101,8 +102,17 @@ def test_gemv_int8_sliced_extremes(cuda_dev, B):
 @pytest.mark.parametrize("N", [3072, 4096], ids=["bf16path", "sliced"])
 @pytest.mark.parametrize("rows", [1, 2, 4, 8])
 def test_gemv_kslices_agree(cuda_dev, rows, N):
-    """The K-split tuning knob changes only the fp32 summation order (bf16 path) or nothing at all (sliced path:
-    exact int32 partial sums)."""
+    """The K-split tuning knob changes only the fp32 summation order (bf16 path) or nothing at all (ring sliced
+    kernel: exact int32 partial sums)."""
+    from lfm2opt import _capi
+    _capi.lib().lfm2q_set_gemv_path(1 if N == 3072 else 4)
+    try:
+        _kslices_case(cuda_dev, rows, N)
+    finally:
+        _capi.lib().lfm2q_set_gemv_path(0)
+
+
+def _kslices_case(cuda_dev, rows, N):
     g = torch.Generator().manual_seed(rows)
     Wq = torch.randint(-127, 128, (N, 2048), generator=g, dtype=torch.int8)
     s = torch.rand(N, generator=g) * 1e-3

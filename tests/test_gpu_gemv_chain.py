@@ -31,8 +31,10 @@ def weights(N, K, seed, dev):
 
 
 def sliced_in_gemv(N, K, B):
-    """Whether lfm2q_gemv runs its x-sliced int8 path for this shape (launch_gemv, gemv_xs_slices)."""
-    return N * K >= 8 * 1024 * 1024 and B <= 4 and B * 3 * (K + 64) <= 64 * 1024 and K <= 16384 // B
+    """Whether lfm2q_gemv runs an x-sliced int8 kernel for this shape on the default path (launch_gemv: the deep
+    kernel up to 2 tokens whenever the slices fit, the ring kernel for 3-4 tokens from 8 M weights)."""
+    fits = B <= 4 and B * 3 * (K + 64) <= 64 * 1024 and K <= 16384 // B
+    return fits and (B <= 2 or N * K >= 8 * 1024 * 1024)
 
 
 @pytest.mark.parametrize("B", [1, 2, 3, 4])

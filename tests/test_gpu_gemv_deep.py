@@ -4,10 +4,10 @@ The deep kernel computes exactly what the ring x-sliced kernel computes (exact i
 tokens, the same fp32 combination), with another schedule: one block per SM, each warp's weight steps over all of its
 row groups streamed through one ring requested before the dependency wait, the dependent launch triggered at the start
 (path 2) or after the last row group (path 3). So:
-  - it equals the ring kernel bit for bit (a one-layer GemvChain on path 0 always runs the ring kernel);
+  - it equals the ring kernel bit for bit (a one-layer GemvChain on path 4 always runs the ring kernel);
   - it meets the oracle bound of the plain GEMV tests;
   - in a chain of dependent GEMVs (each x the previous y) launched with PDL and early triggers, every layer reads
-    its input complete: the chain equals the same layers run one at a time on path 0.
+    its input complete: the chain equals the same layers run one at a time on the ring kernel.
 """
 
 import pytest
@@ -39,8 +39,8 @@ def weights(N, K, seed, dev):
 
 
 def ring_result(W, s, x):
-    """The ring x-sliced kernel's values (path 0, one-layer chain)."""
-    _capi.lib().lfm2q_set_gemv_path(0)
+    """The ring x-sliced kernel's values (path 4, one-layer chain)."""
+    _capi.lib().lfm2q_set_gemv_path(4)
     y = torch.full((x.shape[0], W.shape[0]), float("nan"), device=x.device, dtype=BF)
     GemvChain([(W, s, x, y)])()
     torch.cuda.synchronize()
