@@ -609,7 +609,7 @@ def gemv_sweep(dev, world, rank, batches=(1, 2, 4, 8, 16), replays=20):
             nbytes = sum(W.shape[0] * W.shape[1] + 4 * W.shape[0] + 2 * B * W.shape[1] + 2 * B * W.shape[0]
                          for W, _ in layers)
             if mode == "w16_chain":
-                # the 65 GEMVs through lfm2q_gemv_chain (one launch each, in order, L2 window ahead), replayed from
+                # the 65 GEMVs through one lfm2q_gemv_chain call (one launch each, in order), replayed from
                 # a CUDA graph like the other modes
                 from lfm2opt.kernels import GemvChain
                 chain = GemvChain([(W, s, xs[W.shape[1]], y) for (W, s), y in zip(layers, ys)])
@@ -1109,7 +1109,7 @@ def main():
             b1 = {m: gemv[m][1]["gbs"] / world for m in ("w16", "w16_chain", "a8")}
             gemv_out = {"metric": "decode GEMV HBM GB/s (16-layer LFM2 stack + lm_head: 65 GEMVs, each after the one "
                                   "before, replayed from a CUDA graph; w16: lfm2q_gemv per layer; w16_chain: "
-                                  "lfm2q_gemv_chain (same GEMVs, weights of the layers ahead streamed into L2); "
+                                  "lfm2q_gemv_chain (the same GEMVs from one C call, x-sliced kernels at every size); "
                                   "a8: quant_rows + A8 GEMV per layer)",
                         "w16_weight_only": {str(k): v for k, v in gemv["w16"].items()},
                         "w16_chain": {str(k): v for k, v in gemv["w16_chain"].items()},
