@@ -192,7 +192,9 @@ int lfm2q_selftest_wait_timeout(int limit_log2, void *stream);
 /* Forces the per-token GEMM tile: 128 or 256 = one CTA per 128-row tile of that many columns; -192 or -256 = a CTA
  * pair (cluster of two, tcgen05 cta_group::2) per 256-row tile of that many columns; 0 = automatic. The SiLU GEMM
  * follows the sign (one CTA or a pair, 128 output columns per tile); 64 = one CTA per 128 x 64 tile (W8A16 only, its
- * small-M choice; the int8 GEMMs treat it as automatic). Tuning and testing only. */
+ * small-M choice; the int8 GEMMs treat it as automatic); 1 = the per-token W8A8 GEMM splits K over a cluster of
+ * CTAs per 128 x 128 tile wherever K has two 128-byte blocks per CTA (automatic: when the tiles fill fewer than half
+ * the SMs). Tuning and testing only. */
 void lfm2q_set_gemm_tile(int bn);
 
 #ifdef __cplusplus

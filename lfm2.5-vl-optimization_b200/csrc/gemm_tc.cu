@@ -1017,15 +1017,13 @@ bool make_map_w8(CUtensorMap *map, const void *ptr, int inner, int rows, int box
 
 std::atomic<int> g_tile_override{0};
 // Per-token GEMMs with few rows: the A8 GEMV (one pass over W, int8 mma.sync, tokens on the MMA's N side) against
-// one 128-row tcgen05 tile per CTA, whose time is set by its pipeline depth per K stage (~7.9 us at K = 2048,
-// ~21 us at K = 8192 for M = 16..128, measured). The GEMV wins at M <= 16 always, and up to 64 rows when K is long
-// (K = 8192: 9-14 us) or, up to 32 rows, when the weights are small (<= 8 M) — its 32- and 64-token variants hold
-// more registers and fewer blocks per SM, so at K = 2048 with large N the tiles are faster.
+// the tcgen05 tiles, split-K or not (graph-timed on B200, weights beyond L2): the GEMV wins up to 16 rows, and up to
+// 32 rows when the weights are small (<= 8 M: 2048 x 2048 at M = 32, 3.9 us against 4.9 us split-K); from 8 M
+// weights split-K is faster (2048 x 8192 at M = 17..32: 7.9 us against 9.7-10.6 us).
 bool a8_rows(int M, int N, int K) {
   if (K % 64 != 0) return false;
   if (M <= 16) return true;
-  if (M <= 32) return K >= 4096 || (long)N * K <= 8L * 1024 * 1024;
-  return M <= A8_MAX_TOKENS && K >= 4096;
+  return M <= 32 && (long)N * K <= 8L * 1024 * 1024;
 }
 std::atomic<bool> g_gemm_pdl{true};  // GEMMs launch as programmatic dependents (lfm2q_set_pdl)
 
@@ -1103,6 +1101,338 @@ GemmArgs base_args(const float *sa, const float *sb, const void *bias, int M, in
   return a;
 }
 
+
+// ------------------------------------------------------------------ split-K tiles for few rows
+// Per-token W8A8 GEMMs with few rows (decode batches of 17-256 tokens) have too few 128 x 128 output tiles to put
+// every SM on the weight stream, and each tile's time is its K loop of load round trips. Split-K: a cluster of S CTAs
+// per tile, CTA r multiplying K blocks [r kbs, (r + 1) kbs) into its own TMEM. The S exact int32 partial tiles meet in
+// distributed shared memory: each CTA writes its partial into its shared memory, the cluster synchronises, and CTA r
+// adds the S partials of output columns [r 128/S, (r + 1) 128/S) (integers: exact in any order) and runs the
+// per-token epilogue (epi_token, the same arithmetic as the one-CTA tile) on them. The result is bit-identical to
+// the one-CTA tile. Roles: warp 0 TMA, warp 1 TMEM allocation and MMAs, warps 2-5 the epilogue (TMEM lane quarter
+// warp % 4). No cluster multicast: every CTA loads its own A and B stages.
+constexpr int SK_BN = 128;
+constexpr int SK_THREADS = 192;
+constexpr int SK_STAGES = 3;  // with <= 100 KB of shared memory a CTA of the next launch fits beside this one
+// The partial tile in shared memory, laid out by the CTA that reduces each part: region p (the output columns
+// [p W, (p + 1) W), W = 128 / S) holds 128 rows of W int32 plus a 16-byte pad per row (conflict-free row writes), so
+// a peer reads its region as contiguous 16-byte chunks.
+__host__ __device__ constexpr int sk_rstride(int S) { return SK_BN / S + 4; }
+struct SkSmem {
+  static constexpr int A_BYTES = TM * TK;
+  static constexpr int B_BYTES = SK_BN * TK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 1024-byte multiple: every operand tile stays aligned
+  static constexpr int PART_BYTES = 8 * TM * sk_rstride(8) * 4;  // the largest (S = 8); reuses the stages
+  static constexpr int DATA_BYTES =
+      SK_STAGES * STAGE_BYTES > PART_BYTES ? SK_STAGES * STAGE_BYTES : PART_BYTES;
+  static constexpr int BAR_OFF = DATA_BYTES;
+  static constexpr int NBARS = 2 * SK_STAGES + 1;
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  // this CTA's columns: weight scales [128], then bias [128]; the tile's per-token scales [128] (fp32, 16-byte reads)
+  static constexpr int PAR_OFF = (MISC_OFF + 16 + 127) / 128 * 128;
+  static constexpr int ALLOC = PAR_OFF + 3 * SK_BN * 4 + 1024;  // room to align the base to 1024
+  static_assert(PAR_OFF % 16 == 0 && (sk_rstride(2) * 4) % 16 == 0 && (sk_rstride(8) * 4) % 16 == 0,
+                "16-byte shared-memory vectors");
+  static_assert(ALLOC <= 100 * 1024, "two CTAs per SM");
+};
+
+// a peer CTA's shared memory (the address from mapa, which itself follows the cluster barrier in program order); no
+// memory clobber, so a run of these loads issues back to back
+__device__ __forceinline__ uint4 ld_shared_cluster16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+// S: CTAs per cluster (2, 4 or 8), kbs: K blocks (128 bytes of K) per CTA
+template <bool GELU, int S>
+__global__ void __launch_bounds__(SK_THREADS, 1)
+    gemm_sk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args, int kbs) {
+  using L = SkSmem;
+  constexpr uint32_t IDESC = idesc_i8(SK_BN, TM);
+  constexpr uint32_t STAGE_TX = L::A_BYTES + L::B_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::MISC_OFF);
+  int *abort_flag = reinterpret_cast<int *>(smem + L::MISC_OFF + 4);
+  auto bar_full = [&](int s) { return smem_addr(bars + s); };
+  auto bar_empty = [&](int s) { return smem_addr(bars + SK_STAGES + s); };
+  const uint32_t bar_tfull = smem_addr(bars + 2 * SK_STAGES);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = args.M, K = args.K;
+  const uint32_t part = cluster_ctarank();  // this CTA's K part, and its share of the output columns
+  int mt, nt;
+  tile_coord((int)blockIdx.x / S, args, mt, nt);
+  const int KB = (K + TK - 1) / TK;
+  const int kb0 = (int)part * kbs;
+  const int nkb = kb0 < KB ? (KB - kb0 < kbs ? KB - kb0 : kbs) : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SK_STAGES; ++s) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_empty(s), 1);
+    }
+    mbar_init(bar_tfull, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(SK_BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // the epilogue's per-column parameters of this CTA's columns (immutable: loaded before any dependency wait, read
+  // after the cluster barrier below)
+  constexpr int W = SK_BN / S;
+  const int c0 = (int)part * W;
+  float *par_sw = reinterpret_cast<float *>(smem + L::PAR_OFF), *par_b = par_sw + SK_BN;
+  float *par_sx = par_b + SK_BN;
+  if (warp >= 2) {
+    const int t = threadIdx.x - 64, n = nt * SK_BN + c0 + t;
+    if (t < W) {
+      par_sw[t] = n < args.Nout ? __ldg(args.sb + n) : 0.f;
+      par_b[t] = (n < args.Nout && args.bias) ? bf2f(args.bias[n]) : 0.f;
+    }
+    // the per-token scales come from the previous kernel: waited for and loaded while the MMAs run
+    if (args.pdl) pdl_wait();
+    par_sx[t] = mt * TM + t < M ? __ldcg(args.sa + mt * TM + t) : 0.f;
+  }
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      auto sa = [&](int st) { return sbase + (uint32_t)(st * L::STAGE_BYTES); };
+      auto sb = [&](int st) { return sbase + (uint32_t)(st * L::STAGE_BYTES + L::A_BYTES); };
+      // programmatic dependent launch: the first stages' weights before the dependency wait, activations after it
+      const int pre = args.pdl ? (nkb < SK_STAGES ? nkb : SK_STAGES) : 0;
+      for (int j = 0; j < pre; ++j) {
+        mbar_expect_tx(bar_full(j), STAGE_TX);
+        tma_load_2d(sb(j), &tmB, bar_full(j), (kb0 + j) * TK, nt * SK_BN);
+      }
+      if (args.pdl) pdl_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int kx = (kb0 + i) * TK;
+        if (i < pre) {
+          tma_load_2d(sa(stage), &tmA, bar_full(stage), kx, mt * TM);  // B on its way, expect_tx posted
+        } else {
+          if (!mbar_wait(bar_empty(stage), phase ^ 1, abort_flag)) break;
+          mbar_expect_tx(bar_full(stage), STAGE_TX);
+          tma_load_2d(sa(stage), &tmA, bar_full(stage), kx, mt * TM);
+          tma_load_2d(sb(stage), &tmB, bar_full(stage), kx, nt * SK_BN);
+        }
+        if (++stage == SK_STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (args.pdl) pdl_trigger();  // every load is issued: the next kernel may start its own prologue
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        if (!mbar_wait(bar_full(stage), phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(sbase + (uint32_t)(stage * L::STAGE_BYTES));
+        const uint64_t bd = sw128_desc(sbase + (uint32_t)(stage * L::STAGE_BYTES + L::A_BYTES));
+#pragma unroll
+        for (int k = 0; k < TK / 32; ++k) umma_i8(tmem_base, ad + 2 * k, bd + 2 * k, IDESC, (i | k) != 0);
+        umma_commit(bar_empty(stage));
+        if (++stage == SK_STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      // the accumulator is complete once the MMAs retire; with nothing multiplied (or a wait given up) the epilogue
+      // is released at once and writes zeros
+      if (ok && nkb > 0)
+        umma_commit(bar_tfull);
+      else
+        mbar_arrive(bar_tfull);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue warps 2-5: the partial tile
+    const int q = warp & 3, row = q * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    bool ok = warp_wait(bar_tfull, 0, abort_flag);
+    int gave_up = lane == 0 ? *(volatile int *)abort_flag : 0;  // warp-uniform: the TMEM loads are .sync.aligned
+    gave_up = __shfl_sync(0xffffffffu, gave_up, 0);
+    ok = ok && nkb > 0 && !gave_up;
+    tc_fence_after();
+    constexpr int RS = sk_rstride(S);
+#pragma unroll 1
+    for (int c = 0; c < SK_BN / 32; ++c) {
+      uint32_t r[32];
+      if (ok) {
+        tmem_ld32(tmem_base + lane_addr + c * 32, r);
+        tmem_wait_tie(r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int col = c * 32 + 4 * j, p = col / W;  // region of the CTA that reduces this column
+        st_shared16(sbase + (uint32_t)(((p * TM + row) * RS + col - p * W) * 4), r[4 * j], r[4 * j + 1], r[4 * j + 2],
+                    r[4 * j + 3]);
+      }
+    }
+    tc_fence_before();
+  }
+  __syncwarp();
+  cluster_sync_all();  // every partial tile of the cluster is in its CTA's shared memory
+
+  if (warp >= 2) {
+    // ---------------------------------------------------------------- this CTA's columns: sum of S partials, epilogue
+    // items = (row, 4-column chunk) of this CTA's region, consecutive threads on consecutive chunks of a row: every
+    // warp-wide peer read is a few contiguous 128-byte runs
+    constexpr int RS = sk_rstride(S), CPR = W / 4;  // chunks per row
+    const int t = threadIdx.x - 64;
+    const uint32_t region = sbase + (uint32_t)(part * TM * RS * 4);
+    const int rows = M - mt * TM < TM ? M - mt * TM : TM;
+    uint32_t peer[S];
+#pragma unroll
+    for (int p = 0; p < S; ++p) peer[p] = mapa_shared(region, (uint32_t)p);
+#pragma unroll 2
+    for (int i = t; i < rows * CPR; i += 128) {
+      const int r = i / CPR, ch = i - r * CPR;
+      const uint32_t off = (uint32_t)((r * RS + 4 * ch) * 4);
+      uint4 v[S];
+#pragma unroll
+      for (int p = 0; p < S; ++p) v[p] = ld_shared_cluster16(peer[p] + off);
+      int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int p = 0; p < S; ++p) {
+        acc[0] += (int)v[p].x;
+        acc[1] += (int)v[p].y;
+        acc[2] += (int)v[p].z;
+        acc[3] += (int)v[p].w;
+      }
+      const int n = nt * SK_BN + c0 + 4 * ch;
+      if (n >= args.Nout) continue;
+      const float sxm = par_sx[r];
+      const float4 s4 = *reinterpret_cast<const float4 *>(par_sw + 4 * ch);
+      const float4 b4 = *reinterpret_cast<const float4 *>(par_b + 4 * ch);
+      const float y0 = epi_token<GELU>(acc[0], sxm, s4.x, b4.x), y1 = epi_token<GELU>(acc[1], sxm, s4.y, b4.y);
+      const float y2 = epi_token<GELU>(acc[2], sxm, s4.z, b4.z), y3 = epi_token<GELU>(acc[3], sxm, s4.w, b4.w);
+      bf16 *yrow = args.Y + (size_t)(mt * TM + r) * args.Nout;
+      if (n + 3 < args.Nout && (args.Nout & 3) == 0) {
+        *reinterpret_cast<uint2 *>(yrow + n) = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+      } else {
+        const float yv[4] = {y0, y1, y2, y3};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (n + e < args.Nout) yrow[n + e] = f2bf(yv[e]);
+      }
+    }
+  }
+  __syncwarp();
+  // no CTA leaves while a peer may still read its partial tile. Relaxed: only execution is ordered here (every read
+  // of a peer's partial has returned its value before this thread arrives); a release would also hold every thread
+  // until its global stores of the output are acknowledged (measured: 4-6 us per launch)
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(SK_BN) : "memory");
+  }
+}
+
+// Clusters of S split-K CTAs that fit on the device at once (occupancy query, cached per device and S): a cluster's
+// CTAs must share a GPC, and with one CTA per SM not every GPC holds two clusters of 8.
+int sk_max_clusters(int S) {
+  static std::once_flag once[64][4];
+  static int n[64][4];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int si = S == 2 ? 1 : (S == 4 ? 2 : (S == 8 ? 3 : 0));
+  std::call_once(once[dev & 63][si], [&] {
+    int c = 0;
+    const void *kern = S == 2 ? (const void *)gemm_sk_kernel<false, 2>
+                              : (S == 4 ? (const void *)gemm_sk_kernel<false, 4> : (const void *)gemm_sk_kernel<false, 8>);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SkSmem::ALLOC) == cudaSuccess) {
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = S;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(S * 16);
+      q.blockDim = dim3(SK_THREADS);
+      q.dynamicSmemBytes = SkSmem::ALLOC;
+      q.attrs = attr;
+      q.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&c, kern, &q) != cudaSuccess) c = 0;
+    }
+    cudaGetLastError();
+    n[dev & 63][si] = c;
+  });
+  return n[dev & 63][si];
+}
+
+// Split-K launch: grid = tiles x S CTAs, clusters of S consecutive CTAs along x (one tile each)
+template <bool GELU, int S>
+cudaError_t run_sk(const int8_t *A, const int8_t *B, GemmArgs a, cudaStream_t st) {
+  auto kern = gemm_sk_kernel<GELU, S>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SkSmem::ALLOC);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, A, a.K, a.M, TM) || !make_map(&tb, B, a.K, a.N, SK_BN)) return cudaErrorInvalidValue;
+  const int KB = (a.K + TK - 1) / TK;
+  const int kbs = (KB + S - 1) / S;
+  cudaLaunchAttribute attr[2];
+  int nattr = 0;
+  attr[nattr].id = cudaLaunchAttributeClusterDimension;
+  attr[nattr].val.clusterDim.x = S;
+  attr[nattr].val.clusterDim.y = 1;
+  attr[nattr].val.clusterDim.z = 1;
+  ++nattr;
+  a.pdl = g_gemm_pdl.load() ? 1 : 0;
+  if (a.pdl) {
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.tiles_m * a.tiles_n * S);
+  cfg.blockDim = dim3(SK_THREADS);
+  cfg.dynamicSmemBytes = SkSmem::ALLOC;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, a, kbs);
+}
+template <bool GELU>
+cudaError_t run_sk_s(const int8_t *A, const int8_t *B, GemmArgs a, int S, cudaStream_t st) {
+  if (S == 2) return run_sk<GELU, 2>(A, B, a, st);
+  if (S == 4) return run_sk<GELU, 4>(A, B, a, st);
+  return run_sk<GELU, 8>(A, B, a, st);
+}
+
 }  // namespace
 
 namespace {
@@ -1139,7 +1469,28 @@ int gemm_device_error(bool clear) {
 void gemm_set_pdl(bool on) { g_gemm_pdl.store(on); }
 
 void gemm_set_tile_override(int bn) {
-  g_tile_override = (bn == 64 || bn == 128 || bn == 256 || bn == -192 || bn == -256) ? bn : 0;
+  g_tile_override = (bn == 1 || bn == 2 || bn == 4 || bn == 8 || bn == 64 || bn == 128 || bn == 256 || bn == -192 ||
+                     bn == -256)
+                        ? bn
+                        : 0;
+}
+
+// CTAs per tile for split-K: while the 128 x 128 tiles fill fewer than half the SMs, the largest power of two <= 8
+// that keeps the grid within the SMs and gives every CTA at least two 128-byte K blocks (force: regardless of the
+// tile count). 1 = no split.
+// Measured (graph-timed, M = 17..256): a long K gains most (K = 8192, N = 2048: 21.3 -> 7.9-13 us, S = 8 or 4); at
+// K = 2048 only very few tiles gain (N = 2048: 7.5 -> 4.9-6.6 us with S = 4), while 48-64 tiles break even or lose
+// (the partial tiles' exchange costs more than the shorter K loop saves).
+int sk_split(int M, int N, int K, bool force) {
+  const int sms = device_sm_count();
+  const long tiles = (long)((M + TM - 1) / TM) * ((N + SK_BN - 1) / SK_BN);
+  const int KB = (K + TK - 1) / TK;
+  if (!force && (2 * tiles > sms || (KB < 32 && tiles > 16))) return 1;
+  int S = (!force && KB < 32) ? 4 : 8;
+  // at most one CTA per SM in all, and clusters the device can hold at once (with 100 KB per CTA two clusters' CTAs
+  // share an SM, so up to twice the one-per-SM count)
+  while (S > 1 && (tiles * S > sms || KB / S < 2 || tiles > 2 * sk_max_clusters(S))) S /= 2;
+  return S;
 }
 
 cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, const float *sb, const void *bias, void *Y,
@@ -1153,9 +1504,19 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
   const int ov = g_tile_override.load() == 64 ? 0 : g_tile_override.load();  // 64: a W8A16-only choice
   if (!ov && a8_rows(M, N, K)) {
     // skinny: the A8 GEMV streams W once with int8 MMAs (same exact int32 sums and the same epilogue)
-    return launch_gemv_a8(B, sb, A, sa, bias, Y, N, K, M, gelu, false, st);
+    return launch_gemv_a8(B, sb, A, sa, bias, Y, N, K, M, gelu, g_gemm_pdl.load(), st);
   }
-  int bn = ov;
+  // few tiles: K split over a cluster of CTAs per 128 x 128 tile (1: forced wherever K has two blocks per CTA;
+  // 2, 4, 8: that many CTAs per tile)
+  if (!ov || ov == 1 || ov == 2 || ov == 4 || ov == 8) {
+    const int S = ov > 1 ? ov : sk_split(M, N, K, ov == 1);
+    if (S > 1) {
+      GemmArgs a = base_args(sa, sb, bias, M, N, K, N, SK_BN);
+      a.Y = (bf16 *)Y;
+      return gelu ? run_sk_s<true>(A, B, a, S, st) : run_sk_s<false>(A, B, a, S, st);
+    }
+  }
+  int bn = (ov == 1 || ov == 2 || ov == 4 || ov == 8) ? 0 : ov;
   if (!bn) {
     // 256 x 256 CTA-pair tiles when there are at least 1.5 per cluster (3-10% faster than one CTA per 128 x 256 tile
     // at 65536 rows, K = 1152 .. 8192); fewer pair tiles leave too much of the last wave idle, so one CTA per

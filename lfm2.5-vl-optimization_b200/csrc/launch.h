@@ -68,7 +68,7 @@ cudaError_t launch_gemm_i8_silu(const int8_t *A, const float *sa, const int8_t *
                                 void *Y, int M, int I, int K, cudaStream_t st);
 int gemm_device_error(bool clear);
 cudaError_t launch_wait_timeout_selftest(int limit_log2, cudaStream_t st);  // sticky code written by a bounded wait that gave up (0 = none)
-void gemm_set_tile_override(int bn);  // 0 = heuristic, 128 / 256 = force the per-token tile width (< 0: CTA pairs)
+void gemm_set_tile_override(int bn);  // 0 = heuristic, 128 / 256 = force the per-token tile width (< 0: CTA pairs), 1 = split-K
 void gemm_set_pdl(bool on);            // GEMMs launch as programmatic dependents
 
 // gemm_tc.cu: tcgen05 W8A16 GEMM

@@ -45,10 +45,11 @@ def make(M, K, N, bias, seed, outlier_ch=False):
     return x, w, b
 
 
-@pytest.fixture(params=[0, 128, 256, -192, -256], ids=["auto", "bn128", "bn256", "pair192", "pair256"])
+@pytest.fixture(params=[0, 128, 256, -192, -256, 1], ids=["auto", "bn128", "bn256", "pair192", "pair256", "splitk"])
 def tile(request):
     """Tile override: 0 = automatic; 128 / 256 = one CTA per 128 x that many columns; -192 / -256 = a CTA pair
-    (cluster of 2, tcgen05 cta_group::2) per 256 x that many columns."""
+    (cluster of 2, tcgen05 cta_group::2) per 256 x that many columns; 1 = K split over a cluster of CTAs per 128 x 128
+    tile (partials summed in distributed shared memory) wherever K has two 128-byte blocks per CTA."""
     _capi.lib().lfm2q_set_gemm_tile(request.param)
     yield request.param
     _capi.lib().lfm2q_set_gemm_tile(0)
