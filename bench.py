@@ -426,18 +426,22 @@ def time_steps(fn, steps, warmup, world, on_start=None, on_end=None):
 
 # ----------------------------------------------------------------------------------------------- e2e (public API)
 class E2E:
-    """The job through Int8Linear / NSplitHead with host-resident inputs and outputs."""
+    """The job through Int8Linear / NSplitHead with host-resident inputs and outputs. default_granularity: every layer
+    built the way a drop-in user gets it (Int8Linear's act_group: 64-wide activation scales by default), and the LM
+    MLP as the reference runs it (w1|w3 GEMM, silu_mul_q, w2 GEMM) instead of the fused SiLU-gate GEMM."""
 
-    def __init__(self, job):
+    def __init__(self, job, default_granularity=False):
         from lfm2opt.int8 import Int8Linear
         from lfm2opt.parallel import NSplitHead
 
         self.job = job
+        self.default_granularity = default_granularity
         dev = job.dev
-        self.vlin = [[Int8Linear(q=q, scale=s, bias=job.vb[j], group=0, kind=VISION[j][0])
+        gkw = {} if default_granularity else {"group": 0}
+        self.vlin = [[Int8Linear(q=q, scale=s, bias=job.vb[j], kind=VISION[j][0], **gkw)
                       for j, (q, s) in enumerate(layer)] for layer in job.vw]
-        self.llin = [[Int8Linear(q=q, scale=s, group=0) for q, s in layer] for layer in job.lw]
-        head_lin = Int8Linear(q=job.hq, scale=job.hsc, group=0)
+        self.llin = [[Int8Linear(q=q, scale=s, **gkw) for q, s in layer] for layer in job.lw]
+        head_lin = Int8Linear(q=job.hq, scale=job.hsc, **gkw)
         self.head = NSplitHead(head_lin, HEAD[2], chunks=4)
         self.hv = job.xv.cpu().pin_memory()
         self.hl = job.xl.cpu().pin_memory()
@@ -501,8 +505,16 @@ class E2E:
         for l, layer in enumerate(self.llin):
             layer[0](self.dl)
             layer[1](self.dl)
-            a = layer[2](self.dl, silu_gate=True)
-            layer[3](a)
+            if self.default_granularity:
+                from lfm2opt.int8 import qbuf
+                from lfm2opt.kernels import int8_ext
+                g = layer[2](self.dl)
+                q, sc = qbuf(g.shape[0], g.shape[1] // 2, layer[3].group, g.device)
+                int8_ext().silu_mul_q(g, q, sc)
+                layer[3]((q, sc))
+            else:
+                a = layer[2](self.dl, silu_gate=True)
+                layer[3](a)
         self.head.wait()
         cur.wait_stream(self.ds)
         cur.wait_stream(self.cs)
@@ -1079,6 +1091,17 @@ def main():
         ok_e2e, edetail = verify_e2e(job, ee)
         vdetail.update(edetail)
         del ee
+        if world == 1:
+            # the drop-in default (64-wide activation scales everywhere, the reference's MLP composition): the
+            # throughput a user of Int8Linear gets without choosing the per-token granularity
+            ed = E2E(job, default_granularity=True)
+            ms_d = time_steps(ed.step, max(3, a.steps // 2), warmup, world)
+            e2e["default_granularity"] = {
+                "value": round(total_ops / (ms_d / max(3, a.steps // 2) * 1e-3) / 1e12, 1), "unit": "TOPS",
+                "ms_per_step": round(ms_d / max(3, a.steps // 2), 2),
+                "activation_quant": "Int8Linear default: per token and 64-channel group (LFM2_INT8_GROUP=64); LM MLP "
+                                    "as gemm_i8 (w1|w3) -> silu_mul_q -> gemm_i8 (w2)"}
+            del ed
     verified = max_over_ranks(0.0 if (ok_job and ok_e2e) else 1.0, world) == 0.0
     if dev_err:
         vdetail["device_error_word"] = "set: a bounded pipeline wait gave up"
