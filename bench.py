@@ -738,6 +738,65 @@ def gemv_shape_sweep(dev, world, batches=(1, 2, 4, 8, 16), per=20, replays=5, in
     return out
 
 
+# LFM2 attention layers: 32 query heads, 8 KV heads, head dim 64; (B, max_len, pos). max_len is a multiple of 256 and
+# the splits are 16, as the reference's decode runtime sizes them (src/lfm2opt/runtime.py:24, :261, :297).
+ATTN_CASES = [(1, 1024, 1000), (1, 4096, 4000), (1, 32768, 32000), (2, 3072, 2300), (8, 4096, 4000),
+              (32, 4096, 4000)]
+
+
+def attention_sweep(dev, world, per=20, replays=5, S=16):
+    """decode_attention_split (lfm2q) at the decode shapes above, each timed as a CUDA graph of `per` calls cycling
+    through enough copies of the KV cache (>= 400 MB) that every call streams its K/V rows from HBM. GB/s = bytes per
+    call / time, bytes = the K and V rows read (B * 8 * (pos + 1) * 256) + q and out (2 * B * 32 * 128); the fp32
+    partials (B * 32 * 16 * 66 * 4 bytes, written then read once) stay in L2 and are not counted."""
+    from lfm2opt.kernels import ext
+
+    E = ext()
+    hbm = load_peaks().get("hbm_gbs")
+    g = torch.Generator(device=dev).manual_seed(47)
+    out = {}
+    for B, max_len, pos in ATTN_CASES:
+        cbytes = B * 8 * max_len * 64 * 2
+        copies = max(2, -(-400 * 10 ** 6 // (2 * cbytes)))
+        caches = [(torch.randn(B, 8, max_len, 64, generator=g, device=dev).to(torch.bfloat16),
+                   torch.randn(B, 8, max_len, 64, generator=g, device=dev).to(torch.bfloat16)) for _ in range(copies)]
+        q = torch.randn(B, 32, 64, generator=g, device=dev).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        ws = torch.empty(B, 32, S, 66, device=dev)
+        p = torch.tensor([pos], device=dev)
+
+        def burst():
+            for i in range(per):
+                kc, vc = caches[i % copies]
+                E.decode_attention_split(q, kc, vc, p, o, ws, 0.125)
+
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            burst()
+        torch.cuda.current_stream(dev).wait_stream(st)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            burst()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(replays):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (replays * per), world)
+        nbytes = B * 8 * (pos + 1) * 256 + 2 * B * 32 * 128
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[f"B{B}_len{pos + 1}"] = {"us": round(us, 2), "gbs_per_gpu": round(gbs, 1),
+                                     "frac_hbm": round(gbs / hbm, 4) if hbm else None}
+        del graph, caches
+        torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------------------------------------------- CPU baseline
 def shape_job_ops():
     """2*M*N*K of the whole job per distinct shape (the config-5 mix), keyed by the names of distinct_shapes()."""
@@ -1106,11 +1165,12 @@ def main():
     if dev_err:
         vdetail["device_error_word"] = "set: a bounded pipeline wait gave up"
 
-    gemv = gemv_shapes = gemv_shapes_w4 = None
+    gemv = gemv_shapes = gemv_shapes_w4 = attn = None
     if not a.no_gemv:
         gemv = gemv_sweep(dev, world, rank)
         gemv_shapes = gemv_shape_sweep(dev, world)
         gemv_shapes_w4 = gemv_shape_sweep(dev, world, batches=(1, 2, 4), int4=True)
+        attn = attention_sweep(dev, world)
 
     peaks = load_peaks()
     hbm = peaks.get("hbm_gbs")
@@ -1155,6 +1215,10 @@ def main():
             "phases_ms_per_step": phases,
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": total_launches, "clocks": clk,
             "gemv": gemv_out,
+            "decode_attention": ({"metric": "decode_attention_split HBM GB/s (K/V rows of positions 0..pos + q + out; "
+                                            "32 query / 8 KV heads, head dim 64, 16 splits, CUDA graph of 20 calls "
+                                            "over >= 400 MB of cache copies)",
+                                  "hbm_peak_gbs": hbm, "cases": attn} if attn else None),
         }
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -38,8 +38,8 @@ const char *lfm2q_version(void);
 /* 1 if the current device is an sm_100 part this library can launch on, else 0. */
 int lfm2q_device_supported(void);
 
-/* Reads (and with clear != 0 resets) the sticky device error word that the tcgen05 GEMMs set when one of their
- * bounded pipeline waits gives up (no other kernel of this library waits on anything). Returns LFM2Q_OK or
+/* Reads (and with clear != 0 resets) the sticky device error words that the tcgen05 GEMMs and the decode attention
+ * set when one of their bounded pipeline waits gives up (no other kernel of this library waits on anything). Returns LFM2Q_OK or
  * LFM2Q_ETIMEOUT. Synchronous (copies one int from the device). Poll it after a batch of work whose outputs matter. */
 int lfm2q_check_device(int clear);
 
@@ -160,6 +160,18 @@ int lfm2q_gemv_chain(const lfm2q_gemv_layer *layers, int n_layers, int B, void *
  *                 cw bf16 [S, 3], cbias bf16 [S] or NULL. */
 int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int S,
                    int K, uint16_t *state, const uint16_t *cw, const uint16_t *cbias, void *stream);
+
+/* ------------------------------------------------------------------ decode attention
+ * Replaces launch_decode_attention_split (kernels/lfm2_decode.cu:418-426) behind decode_attention_split
+ * (kernels/lfm2_decode.cpp:64-71). One decode step of grouped-query attention over a bf16 KV cache, head dim 64, four
+ * query heads per KV head (NQ == 4 * NKV): q bf16 [B, NQ, 64] (unscaled: score = (q * scale) . k),
+ * kc / vc bf16 [B, NKV, max_len, 64], pos int64 [1] on the device (positions 0 .. pos are attended, for every
+ * sequence; positions at or past max_len are not read), out bf16 [B, NQ, 64]. The positions are cut into S splits of
+ * ceil(max_len / S); ws fp32 [B, NQ, S, 66] receives (m, l, acc[64]) of every split and is then merged into out
+ * (no value of ws needs to be set before the call). Per-position arithmetic in the reference kernel's order. */
+int lfm2q_decode_attention_split(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, const int64_t *pos,
+                                 uint16_t *out, float *ws, int B, int NQ, int NKV, int max_len, int S, float scale,
+                                 void *stream);
 
 /* Replace set_pdl / set_gemv_impl (kernels/lfm2_decode.cpp:165-166). set_pdl toggles Programmatic Dependent
  * Launch for the GEMV kernels (default on). set_gemv_impl is accepted for compatibility; this build has one

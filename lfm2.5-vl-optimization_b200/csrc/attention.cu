@@ -1,0 +1,302 @@
+// Flash-decoding attention of one decode step over a bf16 KV cache (grouped-query attention, head dim 64, four
+// query heads per KV head), split over positions, then a combine pass:
+//   split s of (b, q head h): m_s = max_t score, l_s = sum_t e^(score - m_s), acc_s = sum_t e^(score - m_s) v_t over
+//   the positions t of the split, score = (q * scale) . k_t; out[b, h] = bf16( sum_s acc_s e^(m_s - M) /
+//   sum_s l_s e^(m_s - M) ), M = max_s m_s.
+//
+// Reference: decode_attention_split_kernel, attn_combine_kernel, launch_decode_attention_split
+// (kernels/lfm2_decode.cu:284-426), binding decode_attention_split (kernels/lfm2_decode.cpp:64-71); its caller is the
+// fused decode step (src/lfm2opt/runtime.py:258-264), which passes a caller-allocated fp32 workspace
+// ws [B, NQ, S, 66] = (m, l, acc[64]) per (b, q head, split).
+//
+// B200 design. Grid (B * NKV, S); a block covers one KV head's positions [s chunk, (s + 1) chunk) of one sequence
+// (chunk = ceil(max_len / S)): four consumer warps (the four query heads of the KV head) and one producer warp. The
+// producer streams the split's K and V rows (128 bytes per position) into shared memory with cp.async.bulk copies in
+// stages of 64 positions (8 KB of K and 8 KB of V), AT_STAGES deep, each stage completing on an mbarrier; the four
+// warps read every staged row from shared memory (one DRAM read per row, no L1 dependence) and release the stage on
+// a second mbarrier. Every wait is bounded (~1 s of SM clocks); a wait that gives up sets the device error word that
+// lfm2q_check_device reports and the block stops.
+// Per lane (position slot grp = lane / 8, dims 8 sub .. 8 sub + 7, sub = lane % 8) the arithmetic is the reference's
+// operation for operation: the lane's partial dot product over its 8 dims, an xor-shuffle sum over the 8 slices, the
+// online-softmax update per position in increasing order, the merge of the 4 slots by xor 8 then 16; the combine
+// merges the splits in order. So the values equal the reference kernel's.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace lfm2q {
+
+__device__ int g_attn_err = 0;  // sticky: 1 = a stage wait gave up
+
+namespace {
+
+constexpr int AT_D = 64;                 // head dim
+constexpr int AT_HEADS = 4;              // query heads per KV head (consumer warps)
+constexpr int AT_THREADS = 32 * (AT_HEADS + 1);
+constexpr int AT_ROWS = 64;              // positions per stage
+constexpr int AT_STAGES = 4;
+constexpr int AT_ROW_BYTES = AT_D * 2;   // one position of K (or V)
+constexpr int AT_STAGE_BYTES = AT_ROWS * AT_ROW_BYTES;
+constexpr int AT_SMEM = 2 * AT_STAGES * AT_STAGE_BYTES;  // 64 KB, dynamic
+constexpr long long AT_WAIT_LIMIT = 1ll << 31;
+
+__device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void bar_init(uint32_t b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint32_t b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint32_t b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint32_t b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(b), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait; false = gave up (or another role did): the caller stops
+__device__ __forceinline__ bool bar_wait(uint32_t b, uint32_t parity, volatile int *stop) {
+  if (bar_try(b, parity)) return true;
+  const long long t0 = clock64();
+  while (!bar_try(b, parity)) {
+    if (*stop) return false;
+    if (clock64() - t0 > AT_WAIT_LIMIT) {
+      *stop = 1;
+      atomicCAS(&g_attn_err, 0, 1);
+      return false;
+    }
+  }
+  return true;
+}
+// bytes of global memory (16-byte aligned, a multiple of 16) into shared memory, completing on mbarrier b
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(b)
+               : "memory");
+}
+
+// One block per (b * NKV + kv head, split): writes ws[((b * NQ + h) * S + s) * 66 + {0: m, 1: l, 2..65: acc}] for
+// the block's four query heads h.
+__global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__restrict__ q, const bf16 *__restrict__ kc,
+                                                                const bf16 *__restrict__ vc,
+                                                                const int64_t *__restrict__ pos_p, float *__restrict__ ws,
+                                                                int NQ, int NKV, int max_len, int S, float scale,
+                                                                int pdl) {
+  extern __shared__ __align__(128) uint8_t at_smem[];  // [stage][K rows], [stage][V rows]
+  __shared__ __align__(8) uint64_t full[AT_STAGES], empty[AT_STAGES];
+  __shared__ int stop;
+  uint8_t(*stage_k)[AT_STAGE_BYTES] = reinterpret_cast<uint8_t(*)[AT_STAGE_BYTES]>(at_smem);
+  uint8_t(*stage_v)[AT_STAGE_BYTES] = reinterpret_cast<uint8_t(*)[AT_STAGE_BYTES]>(at_smem + AT_STAGES * AT_STAGE_BYTES);
+  if (pdl) {
+    pdl_trigger();
+    pdl_wait();  // q, the newest cache row and pos come from the previous kernels
+  }
+  const int bk = blockIdx.x, s = blockIdx.y;
+  const int b = bk / NKV, kvh = bk % NKV;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long pv = __ldcg(reinterpret_cast<const long long *>(pos_p));
+  const int len = pv + 1 < (long long)max_len ? (int)pv + 1 : max_len;  // positions past the cache are not read
+  const int chunk = (max_len + S - 1) / S;
+  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
+  if (t0 >= t1) {  // empty split: nothing to merge from it
+    if (warp < AT_HEADS && lane == 0) {
+      float *out = ws + (((size_t)b * NQ + kvh * AT_HEADS + warp) * S + s) * (AT_D + 2);
+      out[0] = -INFINITY;
+      out[1] = 0.f;
+    }
+    return;
+  }
+  const int nst = (t1 - t0 + AT_ROWS - 1) / AT_ROWS;  // stages of this split
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < AT_STAGES; ++i) {
+      bar_init(saddr(&full[i]), 1);
+      bar_init(saddr(&empty[i]), AT_HEADS);
+    }
+    stop = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const size_t base = ((size_t)b * NKV + kvh) * max_len * AT_D;  // this KV head's cache rows
+
+  if (warp == AT_HEADS) {
+    // ---------------------------------------------------------------- producer: K and V rows of each stage
+    if (lane == 0) {
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % AT_STAGES;
+        if (i >= AT_STAGES && !bar_wait(saddr(&empty[slot]), (uint32_t)((i / AT_STAGES - 1) & 1), &stop)) break;
+        const int r0 = t0 + i * AT_ROWS;
+        const int rows = min(AT_ROWS, t1 - r0);
+        const uint32_t bytes = (uint32_t)(rows * AT_ROW_BYTES);
+        bar_expect_tx(saddr(&full[slot]), 2 * bytes);
+        bulk_g2s(saddr(stage_k[slot]), kc + base + (size_t)r0 * AT_D, bytes, saddr(&full[slot]));
+        bulk_g2s(saddr(stage_v[slot]), vc + base + (size_t)r0 * AT_D, bytes, saddr(&full[slot]));
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers: warp = query head of this KV head
+  const int h = kvh * AT_HEADS + warp;
+  const int grp = lane >> 3, sub = lane & 7;  // position slot in a group of four, 8-dim slice
+  float qv[8];
+  {
+    const uint4 raw = ld_cg16(reinterpret_cast<const uint4 *>(q + ((size_t)b * NQ + h) * AT_D) + sub);
+    const __nv_bfloat162 *p2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(p2[j]);
+      qv[2 * j] = f.x * scale;
+      qv[2 * j + 1] = f.y * scale;
+    }
+  }
+  float m = -INFINITY, l = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  bool ok = true;
+  for (int i = 0; i < nst && ok; ++i) {
+    const int slot = i % AT_STAGES;
+    // every lane observes the stage's completion itself (the bulk copies' bytes are then visible to it)
+    const bool fine = bar_wait(saddr(&full[slot]), (uint32_t)((i / AT_STAGES) & 1), &stop);
+    if (!__all_sync(0xffffffffu, fine)) {
+      ok = false;
+      break;
+    }
+    const int rows = min(AT_ROWS, t1 - (t0 + i * AT_ROWS));
+    const uint4 *Ks = reinterpret_cast<const uint4 *>(stage_k[slot]);
+    const uint4 *Vs = reinterpret_cast<const uint4 *>(stage_v[slot]);
+#pragma unroll 4
+    for (int it = 0; it < rows; it += 4) {  // the same trip count for every lane (the shuffles take the full warp)
+      const int t = it + grp;
+      const bool valid = t < rows;
+      float dot = 0.f;
+      uint4 vraw = make_uint4(0u, 0u, 0u, 0u);
+      if (valid) {
+        const uint4 kraw = Ks[t * (AT_D / 8) + sub];
+        vraw = Vs[t * (AT_D / 8) + sub];
+        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&kraw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(k2[j]);
+          dot += qv[2 * j] * f.x + qv[2 * j + 1] * f.y;
+        }
+      }
+      dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      if (valid) {
+        const float mn = fmaxf(m, dot), corr = __expf(m - mn), p = __expf(dot - mn);
+        l = l * corr + p;
+        const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&vraw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(v2[j]);
+          acc[2 * j] = acc[2 * j] * corr + p * f.x;
+          acc[2 * j + 1] = acc[2 * j + 1] * corr + p * f.y;
+        }
+        m = mn;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) bar_arrive(saddr(&empty[slot]));  // this warp is done with the stage
+  }
+  // merge the four position slots (same sub = same dims): xor 8, then 16
+#pragma unroll
+  for (int o = 8; o <= 16; o <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+    const float mn = fmaxf(m, m2);
+    const float c1 = (m == -INFINITY) ? 0.f : __expf(m - mn), c2 = (m2 == -INFINITY) ? 0.f : __expf(m2 - mn);
+    l = l * c1 + l2 * c2;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a2 = __shfl_xor_sync(0xffffffffu, acc[j], o);
+      acc[j] = acc[j] * c1 + a2 * c2;
+    }
+    m = mn;
+  }
+  if (grp == 0) {
+    float *out = ws + (((size_t)b * NQ + h) * S + s) * (AT_D + 2);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[2 + sub * 8 + j] = ok ? acc[j] : 0.f;
+    if (sub == 0) {
+      out[0] = ok ? m : -INFINITY;
+      out[1] = ok ? l : 0.f;
+    }
+  }
+}
+
+// One block of 64 threads per (b, q head): the merge of the S partials, in split order.
+__global__ void __launch_bounds__(AT_D) attn_combine_kernel(const float *__restrict__ ws, bf16 *__restrict__ out, int S,
+                                                            int pdl) {
+  if (pdl) {
+    pdl_trigger();
+    pdl_wait();
+  }
+  const int bh = blockIdx.x, d = threadIdx.x;
+  const float *w = ws + (size_t)bh * S * (AT_D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(w + s * (AT_D + 2)));
+  float L = 0.f, o = 0.f;
+  for (int s = 0; s < S; ++s) {
+    const float ls = __ldcg(w + s * (AT_D + 2) + 1);
+    if (ls == 0.f) continue;
+    const float c = __expf(__ldcg(w + s * (AT_D + 2)) - M);
+    L += ls * c;
+    o += __ldcg(w + s * (AT_D + 2) + 2 + d) * c;
+  }
+  out[(size_t)bh * AT_D + d] = f2bf(o / L);
+}
+
+}  // namespace
+
+cudaError_t launch_decode_attention_split(const void *q, const void *kc, const void *vc, const int64_t *pos, void *out,
+                                          float *ws, int B, int NQ, int NKV, int max_len, int S, float scale, bool pdl,
+                                          cudaStream_t st) {
+  if (B <= 0) return cudaSuccess;
+  static std::atomic<int> attr_set[64];  // the shared-memory opt-in, once per device
+  int dev = 0;
+  if (const cudaError_t e = cudaGetDevice(&dev)) return e;
+  if (dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
+    if (const cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM))
+      return e;
+    attr_set[dev].store(1, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.stream = st;
+  cfg.gridDim = dim3(B * NKV, S);
+  cfg.blockDim = dim3(AT_THREADS);
+  cfg.dynamicSmemBytes = AT_SMEM;
+  const int p = pdl ? 1 : 0;
+  if (const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_split_kernel, (const bf16 *)q, (const bf16 *)kc,
+                                               (const bf16 *)vc, pos, ws, NQ, NKV, max_len, S, scale, p))
+    return e;
+  cfg.gridDim = dim3(B * NQ);
+  cfg.blockDim = dim3(AT_D);
+  cfg.dynamicSmemBytes = 0;
+  return cudaLaunchKernelEx(&cfg, attn_combine_kernel, (const float *)ws, (bf16 *)out, S, p);
+}
+
+int attn_device_error(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_attn_err, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_attn_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace lfm2q

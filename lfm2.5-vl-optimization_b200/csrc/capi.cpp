@@ -91,7 +91,9 @@ int lfm2q_device_supported(void) { return device_is_sm100() ? 1 : 0; }
 int lfm2q_check_device(int clear) {
   if (int e = device_gate()) return e;
   const int v = gemm_device_error(clear != 0);
+  const int a = attn_device_error(clear != 0);
   if (v) return fail(LFM2Q_ETIMEOUT, "lfm2q: a GEMM pipeline wait timed out on the device");
+  if (a) return fail(LFM2Q_ETIMEOUT, "lfm2q: a decode-attention stage wait timed out on the device");
   return LFM2Q_OK;
 }
 
@@ -313,6 +315,24 @@ int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, co
   return launched(launch_gemv_epi(epi, W, w_is_int8 != 0, scale, x, y, S, K, state, cw, cbias, g_pdl.load(),
                                   (cudaStream_t)stream),
                   "gemv_epi");
+}
+
+// ------------------------------------------------------------------ decode attention
+int lfm2q_decode_attention_split(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, const int64_t *pos,
+                                 uint16_t *out, float *ws, int B, int NQ, int NKV, int max_len, int S, float scale,
+                                 void *stream) {
+  REQUIRE(B >= 0 && NKV > 0 && max_len > 0, "q [B, NQ, 64], kc / vc [B, NKV, max_len, 64]: need B >= 0, NKV > 0, "
+                                            "max_len > 0");
+  REQUIRE(NQ == 4 * NKV, "head_dim 64 and 4 query heads per KV head only");
+  REQUIRE(S >= 1 && S <= 65535, "ws [B, NQ, S, 66]: need 1 <= S <= 65535");
+  REQUIRE((long long)B * NKV <= 0x7fffffffLL, "B * NKV too large");
+  if (B == 0) return LFM2Q_OK;
+  REQUIRE(q && kc && vc && pos && out && ws, "q, kc, vc, pos, out and ws must be non-null");
+  REQUIRE(aligned16(q) && aligned16(kc) && aligned16(vc), "q, kc and vc must be 16-byte aligned");
+  if (int e = device_gate()) return e;
+  return launched(launch_decode_attention_split(q, kc, vc, pos, out, ws, B, NQ, NKV, max_len, S, scale, g_pdl.load(),
+                                                (cudaStream_t)stream),
+                  "decode_attention_split");
 }
 
 }  // extern "C"

@@ -75,6 +75,12 @@ void gemm_set_pdl(bool on);            // GEMMs launch as programmatic dependent
 cudaError_t launch_gemm_w8(const void *A, const int8_t *B, const float *sb, const void *bias, void *Y, int M, int N,
                            int K, bool gelu, cudaStream_t st);
 
+// attention.cu: split-over-positions decode attention + combine
+cudaError_t launch_decode_attention_split(const void *q, const void *kc, const void *vc, const int64_t *pos, void *out,
+                                          float *ws, int B, int NQ, int NKV, int max_len, int S, float scale, bool pdl,
+                                          cudaStream_t st);
+int attn_device_error(bool clear);
+
 // device facts cached per device
 int device_sm_count();
 bool device_is_sm100();

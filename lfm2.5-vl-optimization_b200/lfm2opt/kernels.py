@@ -316,6 +316,27 @@ class DecodeGemvExt:
             _capi.call("lfm2q_gemv_w4", Wp.data_ptr(), S.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, group, 1,
                        _stream(x))
 
+    def decode_attention_split(self, q, kc, vc, pos, out, ws, scale):
+        """One decode step of attention over the KV cache, split over positions (the reference's
+        decode_attention_split binding, kernels/lfm2_decode.cpp:64-71): q bf16 [B, NQ, 64], kc / vc bf16
+        [B, NKV, max_len, 64] with NQ == 4 * NKV, pos int64 [1] (positions 0 .. pos attended), out bf16 [B, NQ, 64],
+        ws fp32 [B, NQ, S, 66] the per-split partials (S = ws.size(2))."""
+        for t, n in ((q, "q"), (kc, "kc"), (vc, "vc"), (out, "out")):
+            if not (t.is_cuda and t.dtype == _BF and t.is_contiguous()):
+                raise RuntimeError(f"{n} must be contiguous CUDA bf16")
+        _req(kc.dim() == 4 and kc.size(3) == 64 and q.dim() == 3 and q.size(1) == 4 * kc.size(1),
+             "head_dim 64 and 4 query heads per KV head only")
+        B, NQ = q.size(0), q.size(1)
+        NKV, max_len = kc.size(1), kc.size(2)
+        _req(q.size(2) == 64 and kc.size(0) == B and vc.shape == kc.shape and out.shape == q.shape,
+             "q [B, NQ, 64], kc / vc [B, NKV, max_len, 64], out [B, NQ, 64]")
+        _req(ws.is_cuda and ws.dtype == _F32 and ws.is_contiguous() and ws.dim() == 4 and ws.size(3) == 66
+             and ws.size(0) == B and ws.size(1) == NQ, "ws: fp32 [B, NQ, S, 66]")
+        _req(pos.is_cuda and pos.dtype == torch.int64 and pos.numel() >= 1, "pos: CUDA int64 [1]")
+        with _DeviceOf(q):
+            _capi.call("lfm2q_decode_attention_split", q.data_ptr(), kc.data_ptr(), vc.data_ptr(), pos.data_ptr(),
+                       out.data_ptr(), ws.data_ptr(), B, NQ, NKV, max_len, ws.size(2), float(scale), _stream(q))
+
     def set_pdl(self, on):
         """Enable/disable Programmatic Dependent Launch for the GEMV kernels (default on)."""
         _capi.lib().lfm2q_set_pdl(int(bool(on)))
@@ -362,7 +383,8 @@ class GemvChain:
 
 
 def check_device(clear=False):
-    """Raise RuntimeError if a bounded pipeline wait inside a tcgen05 GEMM gave up since the last clear (the outputs of
+    """Raise RuntimeError if a bounded pipeline wait inside a tcgen05 GEMM or the decode attention gave up since the
+    last clear (the outputs of
     that work are then invalid). Synchronises with the current device. clear: reset the word."""
     st = _capi.lib().lfm2q_check_device(int(bool(clear)))
     if st != _capi.OK:

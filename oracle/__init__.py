@@ -15,3 +15,4 @@ from .quant import quantize_int8_ref, quantize_int4_ref, quant_rows_ref, quant_g
 from .gemm import (gemm_i8_ref, gemm_i8_grouped_ref, gemm_i8_grouped_f64, gemm_i8_q_ref, gemm_i8_silu_ref,  # noqa: F401
                    gemm_w8_f64, int_mm_exact, bf16_ulps, silu_chain_close, gelu_close)
 from .gemv import gemv_ref, gemv_f64, gemv_epi_ref, gemv_w4_ref, gemv_w4_f64, dequantize_int4_ref  # noqa: F401
+from .attention import decode_attention_f64, decode_attention_sdpa, split_partials_f64  # noqa: F401

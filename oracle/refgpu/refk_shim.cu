@@ -4,9 +4,10 @@
 // reference kernels through it on the same device buffers as lfm2q's, and time both.
 //
 // The prototypes below restate the reference launchers' signatures (kernels/int8_gemm.cu:741-742, :751-752, :765-766,
-// :782, :787-788, :798-799, :810, :822; kernels/lfm2_decode.cu:36, :708, :818-819, :938, :965); they must match for
+// :782, :787-788, :798-799, :810, :822; kernels/lfm2_decode.cu:36, :418-419, :708, :818-819, :938, :965); they must match for
 // the link to resolve.
 #include <cuda_runtime.h>
+#include <stdint.h>
 
 void launch_gemm_i8(const void *A, const float *sa, const void *B, const float *sb, const void *bias, void *Y, int M,
                     int N, int K, bool gelu, bool grouped, cudaStream_t st);
@@ -28,6 +29,8 @@ void launch_gemv_w4(const void *Wp, const float *S, const void *x, void *y, int 
                     cudaStream_t st);
 void launch_gemv(const void *W, bool int8, const float *scale, const void *x, void *y, int N, int K, int rows, int B,
                  cudaStream_t st);
+void launch_decode_attention_split(const void *q, const void *kc, const void *vc, const int64_t *pos, void *out,
+                                   float *ws, int B, int NQ, int NKV, int max_len, int S, float scale, cudaStream_t st);
 void set_pdl(bool on);
 
 // Each wrapper launches on `stream` and returns the launch status (cudaError_t as int; 0 = success).
@@ -85,6 +88,11 @@ int refk_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, con
 }
 int refk_gemv_w4(const void *Wp, const float *S, const void *x, void *y, int N, int K, int group, void *stream) {
   launch_gemv_w4(Wp, S, x, y, N, K, group, 0, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+int refk_decode_attention_split(const void *q, const void *kc, const void *vc, const int64_t *pos, void *out, float *ws,
+                                int B, int NQ, int NKV, int max_len, int S, float scale, void *stream) {
+  launch_decode_attention_split(q, kc, vc, pos, out, ws, B, NQ, NKV, max_len, S, scale, (cudaStream_t)stream);
   return (int)cudaGetLastError();
 }
 void refk_set_pdl(int on) { set_pdl(on != 0); }

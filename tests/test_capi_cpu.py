@@ -58,6 +58,14 @@ def test_validation_runs_before_the_device():
     assert _st("lfm2q_gemv_epi", 2, fake, 1, fake, fake, fake, 64, 512, None, None, None, None) == _capi.EINVAL
     assert _st("lfm2q_gemv_epi", 1, fake, 1, fake, fake, fake, 64, 512, None, None, None, None) == _capi.EINVAL
     assert b"state" in _capi.lib().lfm2q_last_error()
+    att = "lfm2q_decode_attention_split"
+    assert _st(att, fake, fake, fake, fake, fake, fake, 0, 32, 8, 3072, 16, 0.125, None) == _capi.OK  # B = 0: nothing to do
+    assert _st(att, fake, fake, fake, fake, fake, fake, 2, 24, 8, 3072, 16, 0.125, None) == _capi.EINVAL
+    assert b"4 query heads per KV head" in _capi.lib().lfm2q_last_error()
+    assert _st(att, fake, fake, fake, fake, fake, fake, 2, 32, 8, 3072, 0, 0.125, None) == _capi.EINVAL
+    assert b"ws [B, NQ, S, 66]" in _capi.lib().lfm2q_last_error()
+    assert _st(att, fake + 8, fake, fake, fake, fake, fake, 2, 32, 8, 3072, 16, 0.125, None) == _capi.EINVAL
+    assert b"aligned" in _capi.lib().lfm2q_last_error()
     assert _st("lfm2q_gemm_i8_silu", fake, fake, fake, fake, None, fake, 16, 12, 32, None) == _capi.EINVAL
     assert _st("lfm2q_silu_mul_q", fake, fake, fake, 4, 100, 0, None) == _capi.EINVAL
     assert _st("lfm2q_add_rmsnorm_q", fake, None, fake, fake, fake, 4, 20, ctypes.c_float(1e-5), 0, None) \
