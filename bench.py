@@ -744,57 +744,75 @@ ATTN_CASES = [(1, 1024, 1000), (1, 4096, 4000), (1, 32768, 32000), (2, 3072, 230
               (32, 4096, 4000)]
 
 
-def attention_sweep(dev, world, per=20, replays=5, S=16):
-    """decode_attention_split (lfm2q) at the decode shapes above, each timed as a CUDA graph of `per` calls cycling
-    through enough copies of the KV cache (>= 400 MB) that every call streams its K/V rows from HBM. GB/s = bytes per
-    call / time, bytes = the K and V rows read (B * 8 * (pos + 1) * 256) + q and out (2 * B * 32 * 128); the fp32
-    partials (B * 32 * 16 * 66 * 4 bytes, written then read once) stay in L2 and are not counted."""
+def time_attention(dev, world, B, max_len, pos, S=16, per=20, replays=5):
+    """Device time (us) of one decode_attention_split call (lfm2q) on 32 query / 8 KV heads: a CUDA graph of `per`
+    calls cycling through enough copies of the KV cache (>= 400 MB) that every call streams its K/V rows from HBM,
+    replayed `replays` times. Returns (us, algorithmic bytes per call): the K and V rows read (B * 8 * (pos + 1) * 256)
+    + q and out (2 * B * 32 * 128); the fp32 partials (B * 32 * S * 66 * 4 bytes, written then read once) stay in L2
+    and are not counted."""
     from lfm2opt.kernels import ext
 
     E = ext()
-    hbm = load_peaks().get("hbm_gbs")
     g = torch.Generator(device=dev).manual_seed(47)
+    cbytes = B * 8 * max_len * 64 * 2
+    copies = max(2, -(-400 * 10 ** 6 // (2 * cbytes)))
+    caches = [(torch.randn(B, 8, max_len, 64, generator=g, device=dev).to(torch.bfloat16),
+               torch.randn(B, 8, max_len, 64, generator=g, device=dev).to(torch.bfloat16)) for _ in range(copies)]
+    q = torch.randn(B, 32, 64, generator=g, device=dev).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    ws = torch.empty(B, 32, S, 66, device=dev)
+    p = torch.tensor([pos], device=dev)
+
+    def burst():
+        for i in range(per):
+            kc, vc = caches[i % copies]
+            E.decode_attention_split(q, kc, vc, p, o, ws, 0.125)
+
+    st = torch.cuda.Stream(dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(st):
+        burst()
+    torch.cuda.current_stream(dev).wait_stream(st)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        burst()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (replays * per), world)
+    del graph, caches
+    torch.cuda.empty_cache()
+    return us, B * 8 * (pos + 1) * 256 + 2 * B * 32 * 128
+
+
+def attention_sweep(dev, world):
+    """decode_attention_split at the decode shapes of ATTN_CASES (16 splits), GB/s = algorithmic bytes / time."""
+    hbm = load_peaks().get("hbm_gbs")
     out = {}
     for B, max_len, pos in ATTN_CASES:
-        cbytes = B * 8 * max_len * 64 * 2
-        copies = max(2, -(-400 * 10 ** 6 // (2 * cbytes)))
-        caches = [(torch.randn(B, 8, max_len, 64, generator=g, device=dev).to(torch.bfloat16),
-                   torch.randn(B, 8, max_len, 64, generator=g, device=dev).to(torch.bfloat16)) for _ in range(copies)]
-        q = torch.randn(B, 32, 64, generator=g, device=dev).to(torch.bfloat16)
-        o = torch.empty_like(q)
-        ws = torch.empty(B, 32, S, 66, device=dev)
-        p = torch.tensor([pos], device=dev)
-
-        def burst():
-            for i in range(per):
-                kc, vc = caches[i % copies]
-                E.decode_attention_split(q, kc, vc, p, o, ws, 0.125)
-
-        st = torch.cuda.Stream(dev)
-        st.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(st):
-            burst()
-        torch.cuda.current_stream(dev).wait_stream(st)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            burst()
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(replays):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (replays * per), world)
-        nbytes = B * 8 * (pos + 1) * 256 + 2 * B * 32 * 128
+        us, nbytes = time_attention(dev, world, B, max_len, pos)
         gbs = nbytes / (us * 1e-6) / 1e9
         out[f"B{B}_len{pos + 1}"] = {"us": round(us, 2), "gbs_per_gpu": round(gbs, 1),
                                      "frac_hbm": round(gbs / hbm, 4) if hbm else None}
-        del graph, caches
-        torch.cuda.empty_cache()
     return out
+
+
+def run_attn_case(a):
+    """One decode attention shape (--attn-case B,max_len,pos[,S]): the timing of attention_sweep, printed as JSON."""
+    B, max_len, pos, *rest = [int(v) for v in a.attn_case.split(",")]
+    S = rest[0] if rest else 16
+    dev = torch.device("cuda", 0)
+    us, nbytes = time_attention(dev, 1, B, max_len, pos, S, replays=max(1, a.steps))
+    hbm = load_peaks().get("hbm_gbs")
+    gbs = nbytes / (us * 1e-6) / 1e9
+    print(json.dumps({"attn_case": a.attn_case, "us": round(us, 2), "gbs": round(gbs, 1),
+                      "frac_hbm": round(gbs / hbm, 4) if hbm else None}), flush=True)
 
 
 # ----------------------------------------------------------------------------------------------- CPU baseline
@@ -1053,6 +1071,7 @@ def main():
                     help="M,K,N[,epi] — time one GEMM shape (epi: none|nobias|gelu|silu|group|groupq|w8|w8gelu); tuning "
                          "and ncu target")
     ap.add_argument("--tile", type=int, default=0, help="force the per-token GEMM tile width (128 or 256)")
+    ap.add_argument("--attn-case", default=None, help="B,max_len,pos[,S] — time one decode attention shape")
     ap.add_argument("--gemv-case", default=None, help="N,K,B[,rows] — time one decode GEMV shape (tuning, ncu target)")
     a = ap.parse_args()
     warmup = max(3, a.warmup)
@@ -1060,6 +1079,8 @@ def main():
         return run_case(a)
     if a.gemv_case:
         return run_gemv_case(a)
+    if a.attn_case:
+        return run_attn_case(a)
 
     if a.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

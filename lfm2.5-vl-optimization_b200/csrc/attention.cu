@@ -12,16 +12,20 @@
 // B200 design. Grid (B * NKV, S); a block covers one KV head's positions [s chunk, (s + 1) chunk) of one sequence
 // (chunk = ceil(max_len / S)): four consumer warps (the four query heads of the KV head) and one producer warp. The
 // producer streams the split's K and V rows (128 bytes per position) into shared memory with cp.async.bulk copies in
-// stages of 64 positions (8 KB of K and 8 KB of V), AT_STAGES deep, each stage completing on an mbarrier; the four
+// stages of 64 positions (8 KB of K and 8 KB of V), 3 or 6 deep, each stage completing on an mbarrier; the four
 // warps read every staged row from shared memory (one DRAM read per row, no L1 dependence) and release the stage on
 // a second mbarrier. Every wait is bounded (~1 s of SM clocks); a wait that gives up sets the device error word that
 // lfm2q_check_device reports and the block stops.
 // Per lane (position slot grp = lane / 8, dims 8 sub .. 8 sub + 7, sub = lane % 8) the arithmetic is the reference's
 // operation for operation: the lane's partial dot product over its 8 dims, an xor-shuffle sum over the 8 slices, the
 // online-softmax update per position in increasing order, the merge of the 4 slots by xor 8 then 16; the combine
-// merges the splits in order. So the values equal the reference kernel's.
+// merges the splits in order. So the values equal the reference kernel's. What differs is the instruction stream:
+// the 16 dot products of a stage are computed before its serial softmax updates, two positions (or two dims) per
+// packed fp32x2 instruction, and bf16 is widened by moving bits (integer pipe) instead of by conversions (which issue
+// at quarter rate and bounded the first version of this kernel).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 
@@ -38,10 +42,10 @@ constexpr int AT_D = 64;                 // head dim
 constexpr int AT_HEADS = 4;              // query heads per KV head (consumer warps)
 constexpr int AT_THREADS = 32 * (AT_HEADS + 1);
 constexpr int AT_ROWS = 64;              // positions per stage
-constexpr int AT_STAGES = 4;
+constexpr int AT_MAX_STAGES = 6;
 constexpr int AT_ROW_BYTES = AT_D * 2;   // one position of K (or V)
 constexpr int AT_STAGE_BYTES = AT_ROWS * AT_ROW_BYTES;
-constexpr int AT_SMEM = 2 * AT_STAGES * AT_STAGE_BYTES;  // 64 KB, dynamic
+constexpr int AT_MAX_SMEM = 2 * AT_MAX_STAGES * AT_STAGE_BYTES;  // 96 KB, dynamic
 constexpr long long AT_WAIT_LIMIT = 1ll << 31;
 
 __device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -86,18 +90,100 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
                : "memory");
 }
 
+// Two fp32 values in one 64-bit register, for the packed fp32 instructions of sm_100 (fma / mul / add .rn.f32x2):
+// each half of a packed op is the IEEE operation of its scalar form, so packing changes no value.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 up2(f32x2 v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// One staged block of up to AT_ROWS positions for one warp: lane (grp, sub) takes positions grp, grp + 4, ... of the
+// stage. The 16 dot products come first (independent: two positions per packed instruction, the loads and shuffles
+// of all 16 overlapping), then the online-softmax updates run in position order. Each value is the reference
+// kernel's (kernels/lfm2_decode.cu:329-365) with its operations spelled out as compiled: per pair of dims
+// t = fma(q0, k0, q1 * k1), dot = dot + t; acc = fma(p, v, acc * corr); l = fma(l, corr, p) (each checked bit for bit
+// against the reference kernel's output: the acc update fuses the second product). bf16 -> fp32 is exact
+// (the 16 bits moved up). Groups of four positions past `rows` are skipped by the whole warp, as the reference's loop
+// bound does; a lane's dot of a position past `rows` (within a pair still in range) is computed from stale shared
+// memory inside the stage buffer and never used.
+template <bool FULL>
+__device__ __forceinline__ void attend_stage(const uint4 *Ks, const uint4 *Vs, int rows, const f32x2 (&q0)[4],
+                                             const f32x2 (&q1)[4], int grp, int sub, float &m, float &l,
+                                             f32x2 (&acc)[4]) {
+  constexpr int IT = AT_ROWS / 4;
+  float dot[IT];
+#pragma unroll
+  for (int i = 0; i < IT; i += 2) {  // positions 4i + grp and 4(i + 1) + grp
+    if (!FULL && 4 * i >= rows) break;
+    const uint4 ka = Ks[(4 * i + grp) * (AT_D / 8) + sub], kb = Ks[(4 * i + 4 + grp) * (AT_D / 8) + sub];
+    const uint32_t wa[4] = {ka.x, ka.y, ka.z, ka.w}, wb[4] = {kb.x, kb.y, kb.z, kb.w};
+    f32x2 d = pk2(0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const f32x2 t = fma2(q0[j], pk2(bf_lo(wa[j]), bf_lo(wb[j])), mul2(q1[j], pk2(bf_hi(wa[j]), bf_hi(wb[j]))));
+      d = add2(d, t);
+    }
+    float2 dd = up2(d);
+    dd.x += __shfl_xor_sync(0xffffffffu, dd.x, 4);
+    dd.y += __shfl_xor_sync(0xffffffffu, dd.y, 4);
+    dd.x += __shfl_xor_sync(0xffffffffu, dd.x, 2);
+    dd.y += __shfl_xor_sync(0xffffffffu, dd.y, 2);
+    dd.x += __shfl_xor_sync(0xffffffffu, dd.x, 1);
+    dd.y += __shfl_xor_sync(0xffffffffu, dd.y, 1);
+    dot[i] = dd.x;
+    dot[i + 1] = dd.y;
+  }
+#pragma unroll
+  for (int i = 0; i < IT; ++i) {
+    const int t = 4 * i + grp;
+    if (FULL || t < rows) {
+      const uint4 vraw = Vs[t * (AT_D / 8) + sub];
+      const uint32_t wv[4] = {vraw.x, vraw.y, vraw.z, vraw.w};
+      const float mn = fmaxf(m, dot[i]), corr = __expf(m - mn), p = __expf(dot[i] - mn);
+      l = __fmaf_rn(l, corr, p);
+      const f32x2 c2 = pk2(corr, corr), p2 = pk2(p, p);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = fma2(p2, pk2(bf_lo(wv[j]), bf_hi(wv[j])), mul2(acc[j], c2));
+      m = mn;
+    }
+  }
+}
+
 // One block per (b * NKV + kv head, split): writes ws[((b * NQ + h) * S + s) * 66 + {0: m, 1: l, 2..65: acc}] for
-// the block's four query heads h.
+// the block's four query heads h (acc only where the split holds positions). `stages` (1..AT_MAX_STAGES) is the ring
+// depth; the dynamic shared memory holds 2 * stages * AT_STAGE_BYTES.
 __global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__restrict__ q, const bf16 *__restrict__ kc,
                                                                 const bf16 *__restrict__ vc,
                                                                 const int64_t *__restrict__ pos_p, float *__restrict__ ws,
                                                                 int NQ, int NKV, int max_len, int S, float scale,
-                                                                int pdl) {
-  extern __shared__ __align__(128) uint8_t at_smem[];  // [stage][K rows], [stage][V rows]
-  __shared__ __align__(8) uint64_t full[AT_STAGES], empty[AT_STAGES];
+                                                                int stages, int pdl) {
+  extern __shared__ __align__(128) uint8_t at_smem[];  // [stage][K rows], then [stage][V rows]
+  __shared__ __align__(8) uint64_t full[AT_MAX_STAGES], empty[AT_MAX_STAGES];
   __shared__ int stop;
   uint8_t(*stage_k)[AT_STAGE_BYTES] = reinterpret_cast<uint8_t(*)[AT_STAGE_BYTES]>(at_smem);
-  uint8_t(*stage_v)[AT_STAGE_BYTES] = reinterpret_cast<uint8_t(*)[AT_STAGE_BYTES]>(at_smem + AT_STAGES * AT_STAGE_BYTES);
+  uint8_t(*stage_v)[AT_STAGE_BYTES] = reinterpret_cast<uint8_t(*)[AT_STAGE_BYTES]>(at_smem + stages * AT_STAGE_BYTES);
   if (pdl) {
     pdl_trigger();
     pdl_wait();  // q, the newest cache row and pos come from the previous kernels
@@ -119,7 +205,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__re
   }
   const int nst = (t1 - t0 + AT_ROWS - 1) / AT_ROWS;  // stages of this split
   if (threadIdx.x == 0) {
-    for (int i = 0; i < AT_STAGES; ++i) {
+    for (int i = 0; i < stages; ++i) {
       bar_init(saddr(&full[i]), 1);
       bar_init(saddr(&empty[i]), AT_HEADS);
     }
@@ -133,8 +219,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__re
     // ---------------------------------------------------------------- producer: K and V rows of each stage
     if (lane == 0) {
       for (int i = 0; i < nst; ++i) {
-        const int slot = i % AT_STAGES;
-        if (i >= AT_STAGES && !bar_wait(saddr(&empty[slot]), (uint32_t)((i / AT_STAGES - 1) & 1), &stop)) break;
+        const int slot = i % stages;
+        if (i >= stages && !bar_wait(saddr(&empty[slot]), (uint32_t)((i / stages - 1) & 1), &stop)) break;
         const int r0 = t0 + i * AT_ROWS;
         const int rows = min(AT_ROWS, t1 - r0);
         const uint32_t bytes = (uint32_t)(rows * AT_ROW_BYTES);
@@ -149,23 +235,24 @@ __global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__re
   // ---------------------------------------------------------------- consumers: warp = query head of this KV head
   const int h = kvh * AT_HEADS + warp;
   const int grp = lane >> 3, sub = lane & 7;  // position slot in a group of four, 8-dim slice
-  float qv[8];
+  f32x2 q0[4], q1[4];  // (q * scale) of dims 8 sub + 2j and 8 sub + 2j + 1, each twice
   {
     const uint4 raw = ld_cg16(reinterpret_cast<const uint4 *>(q + ((size_t)b * NQ + h) * AT_D) + sub);
-    const __nv_bfloat162 *p2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(p2[j]);
-      qv[2 * j] = f.x * scale;
-      qv[2 * j + 1] = f.y * scale;
+      const float a = bf_lo(w[j]) * scale, c = bf_hi(w[j]) * scale;
+      q0[j] = pk2(a, a);
+      q1[j] = pk2(c, c);
     }
   }
-  float m = -INFINITY, l = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float m = -INFINITY, l = 0.f;
+  f32x2 accp[4] = {0ull, 0ull, 0ull, 0ull};  // (acc[2j], acc[2j + 1]); all-zero bits = (+0, +0)
   bool ok = true;
   for (int i = 0; i < nst && ok; ++i) {
-    const int slot = i % AT_STAGES;
+    const int slot = i % stages;
     // every lane observes the stage's completion itself (the bulk copies' bytes are then visible to it)
-    const bool fine = bar_wait(saddr(&full[slot]), (uint32_t)((i / AT_STAGES) & 1), &stop);
+    const bool fine = bar_wait(saddr(&full[slot]), (uint32_t)((i / stages) & 1), &stop);
     if (!__all_sync(0xffffffffu, fine)) {
       ok = false;
       break;
@@ -173,40 +260,19 @@ __global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__re
     const int rows = min(AT_ROWS, t1 - (t0 + i * AT_ROWS));
     const uint4 *Ks = reinterpret_cast<const uint4 *>(stage_k[slot]);
     const uint4 *Vs = reinterpret_cast<const uint4 *>(stage_v[slot]);
-#pragma unroll 4
-    for (int it = 0; it < rows; it += 4) {  // the same trip count for every lane (the shuffles take the full warp)
-      const int t = it + grp;
-      const bool valid = t < rows;
-      float dot = 0.f;
-      uint4 vraw = make_uint4(0u, 0u, 0u, 0u);
-      if (valid) {
-        const uint4 kraw = Ks[t * (AT_D / 8) + sub];
-        vraw = Vs[t * (AT_D / 8) + sub];
-        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&kraw);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(k2[j]);
-          dot += qv[2 * j] * f.x + qv[2 * j + 1] * f.y;
-        }
-      }
-      dot += __shfl_xor_sync(0xffffffffu, dot, 4);
-      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-      if (valid) {
-        const float mn = fmaxf(m, dot), corr = __expf(m - mn), p = __expf(dot - mn);
-        l = l * corr + p;
-        const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&vraw);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(v2[j]);
-          acc[2 * j] = acc[2 * j] * corr + p * f.x;
-          acc[2 * j + 1] = acc[2 * j + 1] * corr + p * f.y;
-        }
-        m = mn;
-      }
-    }
+    if (rows == AT_ROWS)
+      attend_stage<true>(Ks, Vs, AT_ROWS, q0, q1, grp, sub, m, l, accp);
+    else
+      attend_stage<false>(Ks, Vs, rows, q0, q1, grp, sub, m, l, accp);
     __syncwarp();
     if (lane == 0) bar_arrive(saddr(&empty[slot]));  // this warp is done with the stage
+  }
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 a = up2(accp[j]);
+    acc[2 * j] = a.x;
+    acc[2 * j + 1] = a.y;
   }
   // merge the four position slots (same sub = same dims): xor 8, then 16
 #pragma unroll
@@ -233,9 +299,15 @@ __global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__re
   }
 }
 
-// One block of 64 threads per (b, q head): the merge of the S partials, in split order.
+// One block of 64 threads per (b, q head): the merge of the S partials, in split order, as the reference's combine
+// (kernels/lfm2_decode.cu:389-416). M = max_s m_s is exact in any order (a max rounds nothing), so it is a block
+// reduction; the sums then run in split order from partials staged in shared memory AT_CMB_SPLITS at a time (all the
+// loads of a chunk in flight at once instead of one dependent L2 round trip per split).
+constexpr int AT_CMB_SPLITS = 64;
 __global__ void __launch_bounds__(AT_D) attn_combine_kernel(const float *__restrict__ ws, bf16 *__restrict__ out, int S,
                                                             int pdl) {
+  __shared__ float part[AT_CMB_SPLITS * (AT_D + 2)];
+  __shared__ float wmax[AT_D / 32];
   if (pdl) {
     pdl_trigger();
     pdl_wait();
@@ -243,14 +315,25 @@ __global__ void __launch_bounds__(AT_D) attn_combine_kernel(const float *__restr
   const int bh = blockIdx.x, d = threadIdx.x;
   const float *w = ws + (size_t)bh * S * (AT_D + 2);
   float M = -INFINITY;
-  for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(w + s * (AT_D + 2)));
+  for (int s = d; s < S; s += AT_D) M = fmaxf(M, __ldcg(w + (size_t)s * (AT_D + 2)));
+  M = warp_max(M);
+  if ((d & 31) == 0) wmax[d >> 5] = M;
+  __syncthreads();
+  M = fmaxf(wmax[0], wmax[1]);
   float L = 0.f, o = 0.f;
-  for (int s = 0; s < S; ++s) {
-    const float ls = __ldcg(w + s * (AT_D + 2) + 1);
-    if (ls == 0.f) continue;
-    const float c = __expf(__ldcg(w + s * (AT_D + 2)) - M);
-    L += ls * c;
-    o += __ldcg(w + s * (AT_D + 2) + 2 + d) * c;
+  for (int c0 = 0; c0 < S; c0 += AT_CMB_SPLITS) {
+    const int n = min(AT_CMB_SPLITS, S - c0);
+    const float *wc = w + (size_t)c0 * (AT_D + 2);
+    for (int i = d; i < n * (AT_D + 2); i += AT_D) part[i] = __ldcg(wc + i);
+    __syncthreads();
+    for (int s = 0; s < n; ++s) {
+      const float ls = part[s * (AT_D + 2) + 1];
+      if (ls == 0.f) continue;
+      const float c = __expf(part[s * (AT_D + 2)] - M);
+      L += ls * c;
+      o += part[s * (AT_D + 2) + 2 + d] * c;
+    }
+    __syncthreads();
   }
   out[(size_t)bh * AT_D + d] = f2bf(o / L);
 }
@@ -265,7 +348,8 @@ cudaError_t launch_decode_attention_split(const void *q, const void *kc, const v
   int dev = 0;
   if (const cudaError_t e = cudaGetDevice(&dev)) return e;
   if (dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
-    if (const cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM))
+    if (const cudaError_t e =
+            cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_MAX_SMEM))
       return e;
     attr_set[dev].store(1, std::memory_order_release);
   }
@@ -278,10 +362,15 @@ cudaError_t launch_decode_attention_split(const void *q, const void *kc, const v
   cfg.stream = st;
   cfg.gridDim = dim3(B * NKV, S);
   cfg.blockDim = dim3(AT_THREADS);
-  cfg.dynamicSmemBytes = AT_SMEM;
+  // Ring depth: 6 stages (96 KB, two blocks per SM) while the grid fits twice on the SMs, so that each SM keeps
+  // 192 KB of rows in flight; 3 (48 KB, four blocks per SM) for larger grids; never more than a split's stages.
+  const long long blocks = (long long)B * NKV * S;
+  const int chunk = (max_len + S - 1) / S;
+  const int stages = std::max(1, std::min(blocks <= 2LL * device_sm_count() ? 6 : 3, (chunk + AT_ROWS - 1) / AT_ROWS));
+  cfg.dynamicSmemBytes = 2 * stages * AT_STAGE_BYTES;
   const int p = pdl ? 1 : 0;
   if (const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_split_kernel, (const bf16 *)q, (const bf16 *)kc,
-                                               (const bf16 *)vc, pos, ws, NQ, NKV, max_len, S, scale, p))
+                                               (const bf16 *)vc, pos, ws, NQ, NKV, max_len, S, scale, stages, p))
     return e;
   cfg.gridDim = dim3(B * NQ);
   cfg.blockDim = dim3(AT_D);
