@@ -173,6 +173,23 @@ int lfm2q_decode_attention_split(const uint16_t *q, const uint16_t *kc, const ui
                                  uint16_t *out, float *ws, int B, int NQ, int NKV, int max_len, int S, float scale,
                                  void *stream);
 
+/* No counterpart in the reference. lfm2q_decode_attention_split without the ws argument, for callers that cannot
+ * allocate device memory: a C or FFI host that only receives device pointers for q, kc, vc, pos and out from another
+ * runtime and holds no allocator, or a decode loop where a cudaMalloc / cudaFree would synchronize the device and
+ * stall the other streams. The per-split partials go to a workspace inside the library itself: a static device array
+ * of LFM2Q_ATTN_NOALLOC_MAX_WS_FLOATS floats (8 MiB), which every GPU that loads the library holds until the process
+ * exits. Needs B * NQ * S * 66 <= LFM2Q_ATTN_NOALLOC_MAX_WS_FLOATS (else LFM2Q_EINVAL, nothing launched); otherwise
+ * the same arguments, checks and results as lfm2q_decode_attention_split. Nothing in the workspace needs to start at
+ * zero (every split writes its partials before the combine reads them), but all calls on one device share it: two
+ * calls whose kernels overlap on the GPU (other streams, other host threads) race and corrupt each other's results,
+ * so serialise them. The first call on each device finds the workspace's device address (cudaGetSymbolAddress, with
+ * that device current) and sets the kernel's shared-memory limit; make that first call before any stream capture.
+ * Allocates nothing. */
+#define LFM2Q_ATTN_NOALLOC_MAX_WS_FLOATS (1 << 21)
+int lfm2q_decode_attention_split_noalloc(const uint16_t *q, const uint16_t *kc, const uint16_t *vc,
+                                         const int64_t *pos, uint16_t *out, int B, int NQ, int NKV, int max_len, int S,
+                                         float scale, void *stream);
+
 /* Replace set_pdl / set_gemv_impl (kernels/lfm2_decode.cpp:165-166). set_pdl toggles Programmatic Dependent
  * Launch for the GEMV kernels (default on). set_gemv_impl is accepted for compatibility; this build has one
  * GEMV implementation. */

@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <mutex>
 
 #include "common.cuh"
 #include "launch.h"
@@ -376,6 +377,38 @@ cudaError_t launch_decode_attention_split(const void *q, const void *kc, const v
   cfg.blockDim = dim3(AT_D);
   cfg.dynamicSmemBytes = 0;
   return cudaLaunchKernelEx(&cfg, attn_combine_kernel, (const float *)ws, (bf16 *)out, S, p);
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+// The per-split partials of lfm2q_decode_attention_split_noalloc: a fixed 8 MiB array in the library's own device
+// image, present on every GPU that loads the library until the process exits. Host code may not pass the symbol
+// itself to a kernel (on the host it names a host-side shadow, not device memory): its device address is looked up
+// once per device, with that device current, and cached.
+static __device__ __align__(256) float g_attn_static_ws[ATTN_STATIC_WS_FLOATS];
+
+static cudaError_t attn_static_ws(float **ws) {
+  static std::mutex mu;
+  static float *addr[64] = {};
+  int dev = 0;
+  if (const cudaError_t e = cudaGetDevice(&dev)) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {  // first call on this device: an error is returned and not cached, so a later call retries
+    void *p = nullptr;
+    if (const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_ws)) return e;
+    addr[dev] = static_cast<float *>(p);
+  }
+  *ws = addr[dev];
+  return cudaSuccess;
+}
+
+cudaError_t launch_decode_attention_split_static(const void *q, const void *kc, const void *vc, const int64_t *pos,
+                                                 void *out, int B, int NQ, int NKV, int max_len, int S, float scale,
+                                                 bool pdl, cudaStream_t st) {
+  if ((long long)B * NQ * S * (AT_D + 2) > ATTN_STATIC_WS_FLOATS) return cudaErrorInvalidValue;
+  float *ws = nullptr;
+  if (const cudaError_t e = attn_static_ws(&ws)) return e;
+  return launch_decode_attention_split(q, kc, vc, pos, out, ws, B, NQ, NKV, max_len, S, scale, pdl, st);
 }
 
 int attn_device_error(bool clear) {

@@ -335,4 +335,26 @@ int lfm2q_decode_attention_split(const uint16_t *q, const uint16_t *kc, const ui
                   "decode_attention_split");
 }
 
+// Allocation-free variant: the partials live in the library's static device workspace (ATTN_STATIC_WS_FLOATS).
+int lfm2q_decode_attention_split_noalloc(const uint16_t *q, const uint16_t *kc, const uint16_t *vc,
+                                         const int64_t *pos, uint16_t *out, int B, int NQ, int NKV, int max_len, int S,
+                                         float scale, void *stream) {
+  static_assert(ATTN_STATIC_WS_FLOATS == LFM2Q_ATTN_NOALLOC_MAX_WS_FLOATS, "header and library disagree");
+  REQUIRE(B >= 0 && NKV > 0 && max_len > 0, "q [B, NQ, 64], kc / vc [B, NKV, max_len, 64]: need B >= 0, NKV > 0, "
+                                            "max_len > 0");
+  REQUIRE(NQ == 4 * NKV, "head_dim 64 and 4 query heads per KV head only");
+  REQUIRE(S >= 1 && S <= 65535, "need 1 <= S <= 65535");
+  REQUIRE((long long)B * NQ * S * 66 <= ATTN_STATIC_WS_FLOATS,
+          "B * NQ * S * 66 exceeds the static workspace of decode_attention_split_noalloc (" +
+              std::to_string(ATTN_STATIC_WS_FLOATS) + " floats, 8 MiB): use lfm2q_decode_attention_split with a "
+              "caller-allocated ws, or fewer splits");
+  if (B == 0) return LFM2Q_OK;
+  REQUIRE(q && kc && vc && pos && out, "q, kc, vc, pos and out must be non-null");
+  REQUIRE(aligned16(q) && aligned16(kc) && aligned16(vc), "q, kc and vc must be 16-byte aligned");
+  if (int e = device_gate()) return e;
+  return launched(launch_decode_attention_split_static(q, kc, vc, pos, out, B, NQ, NKV, max_len, S, scale,
+                                                       g_pdl.load(), (cudaStream_t)stream),
+                  "decode_attention_split_noalloc");
+}
+
 }  // extern "C"

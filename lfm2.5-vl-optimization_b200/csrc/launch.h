@@ -80,6 +80,11 @@ cudaError_t launch_decode_attention_split(const void *q, const void *kc, const v
                                           float *ws, int B, int NQ, int NKV, int max_len, int S, float scale, bool pdl,
                                           cudaStream_t st);
 int attn_device_error(bool clear);
+// the same with the per-split partials in the library's static device workspace (capacity in floats below)
+cudaError_t launch_decode_attention_split_static(const void *q, const void *kc, const void *vc, const int64_t *pos,
+                                                 void *out, int B, int NQ, int NKV, int max_len, int S, float scale,
+                                                 bool pdl, cudaStream_t st);
+constexpr long long ATTN_STATIC_WS_FLOATS = 1ll << 21;
 
 // device facts cached per device
 int device_sm_count();

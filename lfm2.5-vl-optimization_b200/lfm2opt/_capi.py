@@ -43,6 +43,7 @@ SIGNATURES = {
     "lfm2q_gemv_chain": [_p, _i, _i, _p],
     "lfm2q_gemv_w4": [_p, _p, _p, _p, _i, _i, _i, _i, _p],
     "lfm2q_decode_attention_split": [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p],
+    "lfm2q_decode_attention_split_noalloc": [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p],
 }
 _VOID = {"lfm2q_set_pdl", "lfm2q_set_gemv_impl", "lfm2q_set_gemm_tile", "lfm2q_set_gemv_trigger",
          "lfm2q_set_gemv_path"}

@@ -66,6 +66,10 @@ def test_validation_runs_before_the_device():
     assert b"ws [B, NQ, S, 66]" in _capi.lib().lfm2q_last_error()
     assert _st(att, fake + 8, fake, fake, fake, fake, fake, 2, 32, 8, 3072, 16, 0.125, None) == _capi.EINVAL
     assert b"aligned" in _capi.lib().lfm2q_last_error()
+    na = "lfm2q_decode_attention_split_noalloc"
+    assert _st(na, fake, fake, fake, fake, fake, 64, 32, 8, 3072, 16, 0.125, None) == _capi.EINVAL  # 8.65 M floats
+    assert b"static workspace" in _capi.lib().lfm2q_last_error()
+    assert _st(na, fake, fake, fake, fake, fake, 0, 32, 8, 3072, 16, 0.125, None) == _capi.OK
     assert _st("lfm2q_gemm_i8_silu", fake, fake, fake, fake, None, fake, 16, 12, 32, None) == _capi.EINVAL
     assert _st("lfm2q_silu_mul_q", fake, fake, fake, 4, 100, 0, None) == _capi.EINVAL
     assert _st("lfm2q_add_rmsnorm_q", fake, None, fake, fake, fake, 4, 20, ctypes.c_float(1e-5), 0, None) \
