@@ -161,6 +161,26 @@ int lfm2q_gemv_chain(const lfm2q_gemv_layer *layers, int n_layers, int B, void *
 int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int S,
                    int K, uint16_t *state, const uint16_t *cw, const uint16_t *cbias, void *stream);
 
+/* ------------------------------------------------------------------ decode step kernels
+ * Replace launch_add_rmsnorm / launch_shortconv_step / launch_qk_norm_rope_kv (kernels/lfm2_decode.cu:123-130,
+ * :157-161, :204-212) behind add_rmsnorm / shortconv_step / qk_norm_rope_kv (kernels/lfm2_decode.cpp:32-55). Outputs
+ * bit-identical to the reference kernels. All bf16 except inv_freq (fp32 [32]) and pos (int64 [1] on the device).
+ *
+ * add_rmsnorm: h [rows, H] (updated in place to bf16(h + y) when y is non-NULL), w [H], x [rows, H] =
+ * bf16(w * bf16(h * rsqrt(mean(h^2) + eps))). Needs H <= 8192. */
+int lfm2q_add_rmsnorm(uint16_t *h, const uint16_t *y, const uint16_t *w, uint16_t *x, int rows, int H, float eps,
+                      void *stream);
+/* shortconv_step: bcx [B, 3H] = (B | C | x), state [B, H, 3] (shifted in place), w [H, 3], bias [H] or NULL,
+ * y [B, H] = bf16(C * bf16(w . (s1, s2, bf16(B x)) + bias)). */
+int lfm2q_shortconv_step(const uint16_t *bcx, uint16_t *state, const uint16_t *w, const uint16_t *bias, uint16_t *y,
+                         int B, int H, void *stream);
+/* qk_norm_rope_kv: qkv [B, (NQ + 2 NKV) * 64] (q | k | v heads, head dim 64), qw / kw [64] per-head RMSNorm weights,
+ * rope cos / sin = bf16(cos / sin(pos * inv_freq[d % 32]) * scaling); q_out [B, NQ, 64]; k and v written to
+ * kc / vc [B, NKV, max_len, 64] at position pos (the caller keeps pos < max_len). */
+int lfm2q_qk_norm_rope_kv(const uint16_t *qkv, const uint16_t *qw, const uint16_t *kw, const float *inv_freq,
+                          float scaling, const int64_t *pos, uint16_t *q_out, uint16_t *kc, uint16_t *vc, int B,
+                          int NQ, int NKV, int max_len, float eps, void *stream);
+
 /* ------------------------------------------------------------------ decode attention
  * Replaces launch_decode_attention_split (kernels/lfm2_decode.cu:418-426) behind decode_attention_split
  * (kernels/lfm2_decode.cpp:64-71). One decode step of grouped-query attention over a bf16 KV cache, head dim 64, four

@@ -317,6 +317,41 @@ int lfm2q_gemv_epi(int epi, const void *W, int w_is_int8, const float *scale, co
                   "gemv_epi");
 }
 
+// ------------------------------------------------------------------ decode step kernels
+int lfm2q_add_rmsnorm(uint16_t *h, const uint16_t *y, const uint16_t *w, uint16_t *x, int rows, int H, float eps,
+                      void *stream) {
+  REQUIRE(rows >= 0 && H > 0 && H <= 8192, "h [rows, H]: need rows >= 0 and 0 < H <= 8192");
+  if (rows == 0) return LFM2Q_OK;
+  REQUIRE(h && w && x, "h, w and x must be non-null");
+  if (int e = device_gate()) return e;
+  return launched(launch_add_rmsnorm(h, y, w, x, rows, H, eps, g_pdl.load(), (cudaStream_t)stream), "add_rmsnorm");
+}
+
+int lfm2q_shortconv_step(const uint16_t *bcx, uint16_t *state, const uint16_t *w, const uint16_t *bias, uint16_t *y,
+                         int B, int H, void *stream) {
+  REQUIRE(B >= 0 && H > 0, "bcx [B, 3H], state [B, H, 3], w [H, 3], y [B, H]: need B >= 0, H > 0");
+  REQUIRE(B <= 65535, "B <= 65535");
+  if (B == 0) return LFM2Q_OK;
+  REQUIRE(bcx && state && w && y, "bcx, state, w and y must be non-null");
+  if (int e = device_gate()) return e;
+  return launched(launch_shortconv_step(bcx, state, w, bias, y, B, H, g_pdl.load(), (cudaStream_t)stream),
+                  "shortconv_step");
+}
+
+int lfm2q_qk_norm_rope_kv(const uint16_t *qkv, const uint16_t *qw, const uint16_t *kw, const float *inv_freq,
+                          float scaling, const int64_t *pos, uint16_t *q_out, uint16_t *kc, uint16_t *vc, int B,
+                          int NQ, int NKV, int max_len, float eps, void *stream) {
+  REQUIRE(B >= 0 && NQ > 0 && NKV > 0 && max_len > 0, "qkv [B, (NQ + 2 NKV) * 64]: need B >= 0, NQ, NKV, max_len > 0");
+  REQUIRE((long long)B * (NQ + 2 * NKV) <= 0x7fffffffLL, "B * (NQ + 2 NKV) too large");
+  if (B == 0) return LFM2Q_OK;
+  REQUIRE(qkv && qw && kw && inv_freq && pos && q_out && kc && vc, "every pointer must be non-null");
+  REQUIRE(aligned16(qkv) && aligned16(vc), "qkv and vc must be 16-byte aligned");
+  if (int e = device_gate()) return e;
+  return launched(launch_qk_norm_rope_kv(qkv, qw, kw, inv_freq, scaling, pos, q_out, kc, vc, B, NQ, NKV, max_len, eps,
+                                         g_pdl.load(), (cudaStream_t)stream),
+                  "qk_norm_rope_kv");
+}
+
 // ------------------------------------------------------------------ decode attention
 int lfm2q_decode_attention_split(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, const int64_t *pos,
                                  uint16_t *out, float *ws, int B, int NQ, int NKV, int max_len, int S, float scale,

@@ -86,6 +86,15 @@ cudaError_t launch_decode_attention_split_static(const void *q, const void *kc, 
                                                  bool pdl, cudaStream_t st);
 constexpr long long ATTN_STATIC_WS_FLOATS = 1ll << 21;
 
+// decode.cu: the decode step's small kernels
+cudaError_t launch_add_rmsnorm(void *h, const void *y, const void *w, void *x, int rows, int H, float eps, bool pdl,
+                               cudaStream_t st);
+cudaError_t launch_shortconv_step(const void *bcx, void *state, const void *w, const void *bias, void *y, int B, int H,
+                                  bool pdl, cudaStream_t st);
+cudaError_t launch_qk_norm_rope_kv(const void *qkv, const void *qw, const void *kw, const float *inv_freq,
+                                   float scaling, const int64_t *pos, void *q_out, void *kc, void *vc, int B, int NQ,
+                                   int NKV, int max_len, float eps, bool pdl, cudaStream_t st);
+
 // device facts cached per device
 int device_sm_count();
 bool device_is_sm100();

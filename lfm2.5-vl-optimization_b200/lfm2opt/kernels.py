@@ -316,6 +316,53 @@ class DecodeGemvExt:
             _capi.call("lfm2q_gemv_w4", Wp.data_ptr(), S.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, group, 1,
                        _stream(x))
 
+    def add_rmsnorm(self, h, y, w, x, eps):
+        """h += y (if y is not None); x = w * rmsnorm(h), bf16, rows of H (the reference's add_rmsnorm binding,
+        kernels/lfm2_decode.cpp:32-37)."""
+        for t, n in ((h, "h"), (w, "w"), (x, "x")):
+            if not (t.is_cuda and t.dtype == _BF and t.is_contiguous()):
+                raise RuntimeError(f"{n} must be contiguous CUDA bf16")
+        if y is not None and not (y.is_cuda and y.dtype == _BF and y.is_contiguous()):
+            raise RuntimeError("(*y) must be contiguous CUDA bf16")
+        H = h.size(-1)
+        rows = h.numel() // H
+        _req(w.numel() == H and x.numel() == h.numel() and (y is None or y.numel() == h.numel()), "shapes")
+        with _DeviceOf(h):
+            _capi.call("lfm2q_add_rmsnorm", h.data_ptr(), _ptr(y), w.data_ptr(), x.data_ptr(), rows, H, float(eps),
+                       _stream(h))
+
+    def shortconv_step(self, bcx, state, w, bias, y):
+        """One short-convolution decode step (the reference's shortconv_step binding,
+        kernels/lfm2_decode.cpp:39-45): bcx [B, 3H], state [B, H, 3] updated in place, w [H, 3], bias [H] or None,
+        y [B, H]."""
+        for t, n in ((bcx, "bcx"), (state, "state"), (w, "w"), (y, "y")):
+            if not (t.is_cuda and t.dtype == _BF and t.is_contiguous()):
+                raise RuntimeError(f"{n} must be contiguous CUDA bf16")
+        _req(state.size(-1) == 3, "conv state length must be 3")
+        B, H = bcx.size(0), bcx.size(-1) // 3
+        _req(state.numel() == B * H * 3 and w.numel() == H * 3 and y.numel() == B * H, "shapes")
+        if bias is not None:
+            _req(bias.is_cuda and bias.dtype == _BF and bias.is_contiguous() and bias.numel() == H, "bias [H] bf16")
+        with _DeviceOf(bcx):
+            _capi.call("lfm2q_shortconv_step", bcx.data_ptr(), state.data_ptr(), w.data_ptr(), _ptr(bias),
+                       y.data_ptr(), B, H, _stream(bcx))
+
+    def qk_norm_rope_kv(self, qkv, qw, kw, inv_freq, scaling, pos, q_out, kc, vc, eps):
+        """Per-head RMSNorm of q and k, RoPE, k and v into the cache at pos (the reference's qk_norm_rope_kv
+        binding, kernels/lfm2_decode.cpp:47-55): qkv [B, (NQ + 2 NKV) * 64], q_out [B, NQ, 64], kc / vc
+        [B, NKV, max_len, 64]."""
+        for t, n in ((qkv, "qkv"), (qw, "qw"), (kw, "kw"), (q_out, "q_out"), (kc, "kc"), (vc, "vc")):
+            if not (t.is_cuda and t.dtype == _BF and t.is_contiguous()):
+                raise RuntimeError(f"{n} must be contiguous CUDA bf16")
+        _req(inv_freq.dtype == _F32 and pos.dtype == torch.int64, "inv_freq fp32, pos int64")
+        _req(kc.size(3) == 64, "head_dim 64 only")
+        B, NQ, NKV, max_len = qkv.size(0), q_out.size(1), kc.size(1), kc.size(2)
+        _req(qkv.numel() == B * (NQ + 2 * NKV) * 64 and vc.shape == kc.shape and inv_freq.numel() >= 32, "shapes")
+        with _DeviceOf(qkv):
+            _capi.call("lfm2q_qk_norm_rope_kv", qkv.data_ptr(), qw.data_ptr(), kw.data_ptr(), inv_freq.data_ptr(),
+                       float(scaling), pos.data_ptr(), q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), B, NQ, NKV,
+                       max_len, float(eps), _stream(qkv))
+
     def decode_attention_split(self, q, kc, vc, pos, out, ws, scale):
         """One decode step of attention over the KV cache, split over positions (the reference's
         decode_attention_split binding, kernels/lfm2_decode.cpp:64-71): q bf16 [B, NQ, 64], kc / vc bf16

@@ -16,3 +16,4 @@ from .gemm import (gemm_i8_ref, gemm_i8_grouped_ref, gemm_i8_grouped_f64, gemm_i
                    gemm_w8_f64, int_mm_exact, bf16_ulps, silu_chain_close, gelu_close)
 from .gemv import gemv_ref, gemv_f64, gemv_epi_ref, gemv_w4_ref, gemv_w4_f64, dequantize_int4_ref  # noqa: F401
 from .attention import decode_attention_f64, decode_attention_sdpa, split_partials_f64  # noqa: F401
+from .decode import add_rmsnorm_ref, shortconv_step_ref, qk_norm_rope_kv_ref  # noqa: F401

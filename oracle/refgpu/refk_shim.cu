@@ -3,9 +3,9 @@
 // sm_100a from where they lie) into oracle/_ref/librefk.so by oracle/Makefile. The GPU parity tests call the
 // reference kernels through it on the same device buffers as lfm2q's, and time both.
 //
-// The prototypes below restate the reference launchers' signatures (kernels/int8_gemm.cu:741-742, :751-752, :765-766,
-// :782, :787-788, :798-799, :810, :822; kernels/lfm2_decode.cu:36, :418-419, :708, :818-819, :938, :965); they must match for
-// the link to resolve.
+// The prototypes below restate the reference launchers' signatures (kernels/int8_gemm.cu:741-742, :751-752,
+// :765-766, :782, :787-788, :798-799, :810, :822; kernels/lfm2_decode.cu:36, :123, :157, :204-206, :418-419, :708,
+// :818-819, :938, :965); they must match for the link to resolve.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -31,6 +31,12 @@ void launch_gemv(const void *W, bool int8, const float *scale, const void *x, vo
                  cudaStream_t st);
 void launch_decode_attention_split(const void *q, const void *kc, const void *vc, const int64_t *pos, void *out,
                                    float *ws, int B, int NQ, int NKV, int max_len, int S, float scale, cudaStream_t st);
+void launch_add_rmsnorm(void *h, const void *y, const void *w, void *x, int rows, int H, float eps, cudaStream_t st);
+void launch_shortconv_step(const void *bcx, void *state, const void *w, const void *bias, void *y, int B, int H,
+                           cudaStream_t st);
+void launch_qk_norm_rope_kv(const void *qkv, const void *qw, const void *kw, const float *inv_freq, float scaling,
+                            const int64_t *pos, void *q_out, void *kc, void *vc, int B, int NQ, int NKV, int max_len,
+                            float eps, cudaStream_t st);
 void set_pdl(bool on);
 
 // Each wrapper launches on `stream` and returns the launch status (cudaError_t as int; 0 = success).
@@ -93,6 +99,22 @@ int refk_gemv_w4(const void *Wp, const float *S, const void *x, void *y, int N, 
 int refk_decode_attention_split(const void *q, const void *kc, const void *vc, const int64_t *pos, void *out, float *ws,
                                 int B, int NQ, int NKV, int max_len, int S, float scale, void *stream) {
   launch_decode_attention_split(q, kc, vc, pos, out, ws, B, NQ, NKV, max_len, S, scale, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+int refk_add_rmsnorm(void *h, const void *y, const void *w, void *x, int rows, int H, float eps, void *stream) {
+  launch_add_rmsnorm(h, y, w, x, rows, H, eps, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+int refk_shortconv_step(const void *bcx, void *state, const void *w, const void *bias, void *y, int B, int H,
+                        void *stream) {
+  launch_shortconv_step(bcx, state, w, bias, y, B, H, (cudaStream_t)stream);
+  return (int)cudaGetLastError();
+}
+int refk_qk_norm_rope_kv(const void *qkv, const void *qw, const void *kw, const float *inv_freq, float scaling,
+                         const int64_t *pos, void *q_out, void *kc, void *vc, int B, int NQ, int NKV, int max_len,
+                         float eps, void *stream) {
+  launch_qk_norm_rope_kv(qkv, qw, kw, inv_freq, scaling, pos, q_out, kc, vc, B, NQ, NKV, max_len, eps,
+                         (cudaStream_t)stream);
   return (int)cudaGetLastError();
 }
 void refk_set_pdl(int on) { set_pdl(on != 0); }
