@@ -803,6 +803,55 @@ def attention_sweep(dev, world):
     return out
 
 
+def time_decode_step(dev, world, pos, replays=20, weights=None):
+    """One whole LFM2 decode step at batch 1 (lfm2opt.decode_step.DecodeStep: 65 int8 weight-only GEMVs, 6 split
+    attentions, 33 add_rmsnorm, 6 qk_norm_rope_kv, 10 conv steps fused into their in_proj GEMV, embedding and argmax)
+    replayed from one CUDA graph with `pos` cached positions. Returns (us per token, bytes per token): the int8
+    weights and their scales, the embedding row, the K/V rows read and written, the conv states."""
+    from lfm2opt.decode_step import DecodeStep, Lfm2Config, Lfm2Weights
+
+    cfg = Lfm2Config()
+    W = weights or Lfm2Weights(cfg, dev, seed=5)
+    max_len = -(-(pos + replays + 8) // 256) * 256
+    s = DecodeStep(W, max_len=max_len)
+    s.pos.fill_(pos - 1)
+    s.capture()
+    for _ in range(3):
+        s.replay()
+    torch.cuda.synchronize()
+    s.pos.fill_(pos)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        s.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / replays, world)
+    lin = [W.head] + [L[k] for L in W.layer for k in L if isinstance(L[k], tuple)]
+    wbytes = sum(q.numel() + 4 * sc.numel() for q, sc in lin)
+    kv = len(cfg.attn_layers) * 2 * cfg.n_kv * (pos + replays // 2 + 1) * cfg.head_dim * 2
+    conv = (cfg.layers - len(cfg.attn_layers)) * cfg.hidden * cfg.conv_len * 2 * 2
+    del s
+    torch.cuda.empty_cache()
+    return us, wbytes + cfg.hidden * 2 + kv + conv
+
+
+def decode_step_sweep(dev, world, positions=(1000, 4000)):
+    from lfm2opt.decode_step import Lfm2Config, Lfm2Weights
+
+    hbm = load_peaks().get("hbm_gbs")
+    W = Lfm2Weights(Lfm2Config(), dev, seed=5)
+    out = {}
+    for pos in positions:
+        us, nbytes = time_decode_step(dev, world, pos, weights=W)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[f"pos{pos}"] = {"us_per_token": round(us, 1), "tokens_per_s": round(1e6 / us, 1),
+                            "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4) if hbm else None}
+    del W
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_attn_case(a):
     """One decode attention shape (--attn-case B,max_len,pos[,S]): the timing of attention_sweep, printed as JSON."""
     B, max_len, pos, *rest = [int(v) for v in a.attn_case.split(",")]
@@ -1071,6 +1120,7 @@ def main():
                     help="M,K,N[,epi] — time one GEMM shape (epi: none|nobias|gelu|silu|group|groupq|w8|w8gelu); tuning "
                          "and ncu target")
     ap.add_argument("--tile", type=int, default=0, help="force the per-token GEMM tile width (128 or 256)")
+    ap.add_argument("--decode-step", type=int, default=None, help="POS — time one whole decode step (batch 1)")
     ap.add_argument("--attn-case", default=None, help="B,max_len,pos[,S] — time one decode attention shape")
     ap.add_argument("--gemv-case", default=None, help="N,K,B[,rows] — time one decode GEMV shape (tuning, ncu target)")
     a = ap.parse_args()
@@ -1081,6 +1131,14 @@ def main():
         return run_gemv_case(a)
     if a.attn_case:
         return run_attn_case(a)
+    if a.decode_step is not None:
+        dev = torch.device("cuda", 0)
+        us, nbytes = time_decode_step(dev, 1, a.decode_step, replays=max(1, a.steps))
+        hbm = load_peaks().get("hbm_gbs")
+        gbs = nbytes / (us * 1e-6) / 1e9
+        print(json.dumps({"decode_step_pos": a.decode_step, "us_per_token": round(us, 1), "gbs": round(gbs, 1),
+                          "frac_hbm": round(gbs / hbm, 4) if hbm else None}), flush=True)
+        return
 
     if a.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
@@ -1186,12 +1244,13 @@ def main():
     if dev_err:
         vdetail["device_error_word"] = "set: a bounded pipeline wait gave up"
 
-    gemv = gemv_shapes = gemv_shapes_w4 = attn = None
+    gemv = gemv_shapes = gemv_shapes_w4 = attn = dstep = None
     if not a.no_gemv:
         gemv = gemv_sweep(dev, world, rank)
         gemv_shapes = gemv_shape_sweep(dev, world)
         gemv_shapes_w4 = gemv_shape_sweep(dev, world, batches=(1, 2, 4), int4=True)
         attn = attention_sweep(dev, world)
+        dstep = decode_step_sweep(dev, world)
 
     peaks = load_peaks()
     hbm = peaks.get("hbm_gbs")
@@ -1240,6 +1299,10 @@ def main():
                                             "32 query / 8 KV heads, head dim 64, 16 splits, CUDA graph of 20 calls "
                                             "over >= 400 MB of cache copies)",
                                   "hbm_peak_gbs": hbm, "cases": attn} if attn else None),
+            "decode_step": ({"metric": "one whole LFM2 decode step, batch 1 (65 int8 weight-only GEMVs, 6 split "
+                                       "attentions, norms, RoPE, conv steps, embedding, argmax) replayed from one CUDA "
+                                       "graph; GB/s = int8 weights + scales + KV and conv state bytes per token",
+                             "hbm_peak_gbs": hbm, "cases": dstep} if dstep else None),
         }
         print(json.dumps(out), flush=True)
     if world > 1:

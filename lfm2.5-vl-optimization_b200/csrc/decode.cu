@@ -41,19 +41,32 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(bf16 *__restrict__ h, c
                                                          const bf16 *__restrict__ w, bf16 *__restrict__ x, int H,
                                                          float eps) {
   __shared__ float red[NT / 32];
-  pdl_trigger();
-  pdl_wait();
   const int t = threadIdx.x, lane = t & 31, wp = t >> 5;
   const size_t off = (size_t)blockIdx.x * H;
-  float hv[NORM_MAX_PER_THREAD];
+  float hv[NORM_MAX_PER_THREAD], yv[NORM_MAX_PER_THREAD], wv[NORM_MAX_PER_THREAD];
+  // the norm weights are immutable: read before the dependency wait, off the critical path
+#pragma unroll
+  for (int k = 0; k < NORM_MAX_PER_THREAD; ++k)
+    if (t + NT * k < H) wv[k] = ldg_bf(w + t + NT * k);
+  pdl_trigger();
+  pdl_wait();
+  // every load of the row first (all in flight together), then the arithmetic and the stores of h
+#pragma unroll
+  for (int k = 0; k < NORM_MAX_PER_THREAD; ++k) {
+    const int i = t + NT * k;
+    if (i < H) {
+      hv[k] = ldcg_bf(h + off + i);
+      if (ADD) yv[k] = ldcg_bf(y + off + i);
+    }
+  }
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < NORM_MAX_PER_THREAD; ++k) {
     const int i = t + NT * k;
     if (i < H) {
-      float v = ldcg_bf(h + off + i);
+      float v = hv[k];
       if (ADD) {
-        v = rbf(v + ldcg_bf(y + off + i));
+        v = rbf(v + yv[k]);
         h[off + i] = f2bf(v);
       }
       hv[k] = v;
@@ -69,7 +82,7 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(bf16 *__restrict__ h, c
 #pragma unroll
   for (int k = 0; k < NORM_MAX_PER_THREAD; ++k) {
     const int i = t + NT * k;
-    if (i < H) x[off + i] = f2bf(ldg_bf(w + i) * rbf(hv[k] * rs));
+    if (i < H) x[off + i] = f2bf(wv[k] * rbf(hv[k] * rs));
   }
 }
 
