@@ -52,10 +52,13 @@ constexpr int TM = 128;        // output rows per tile (UMMA M, one TMEM lane pe
 constexpr int TK = 128;        // K bytes per pipeline stage: one 128-byte swizzle row
 constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (2 per TMEM lane quarter)
 constexpr int EPI_WARPS = 8;
-// epilogue warps: W8 4 (warps 6-13 convert the weights), else 8
-__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_W8 ? 4 : EPI_WARPS; }
+// epilogue warps: W8 4 (warps 6-13 convert the weights); the grouped fold 16 (4 per TMEM lane quarter, 32 columns
+// each: its per-group read-out and fold is the kernel's bottleneck, and 16 warps keep more of it in flight); else 8
+__host__ __device__ constexpr int epi_warps(int epi) {
+  return epi == EPI_W8 ? 4 : (epi == EPI_GROUP ? 2 * EPI_WARPS : EPI_WARPS);
+}
 // threads per CTA: producer + MMA warps, the epilogue warps, W8 also 8 converter warps
-__host__ __device__ constexpr int cta_threads(int epi) { return epi == EPI_W8 ? NTHREADS + 128 : NTHREADS; }
+__host__ __device__ constexpr int cta_threads(int epi) { return 64 + 32 * epi_warps(epi) + (epi == EPI_W8 ? 256 : 0); }
 constexpr long long WAIT_LIMIT = 1ll << 31;
 constexpr uint32_t ACC_BIAS = 0x4B400000u;  // bit pattern of 1.5 * 2^23
 
@@ -299,7 +302,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int *ab
   return ok;
 }
 
-template <int BN, int STAGES, int W_BYTES_ = 0>
+template <int BN, int STAGES, int W_BYTES_ = 0, int NOUT = EPI_WARPS>
 struct Smem {
   static constexpr int A_BYTES = TM * TK;
   static constexpr int B_BYTES = BN * TK;
@@ -317,13 +320,14 @@ struct Smem {
   // epilogue: per-warp 32 x 32 bf16 output block (64-byte rows, 64-byte TMA swizzle), the source of its TMA store
   static constexpr int OUT_OFF = PAR_OFF + EPI_WARPS * PAR_FLOATS * 4;
   static constexpr int OUT_BLOCK = 32 * 64;
-  static constexpr int BYTES = OUT_OFF + EPI_WARPS * OUT_BLOCK;
+  static constexpr int BYTES = OUT_OFF + NOUT * OUT_BLOCK;  // one output block per epilogue warp
   static constexpr int ALLOC = BYTES + 1024;  // room to align the base to 1024
   static_assert(ALLOC <= 232448, "shared memory per block");
 };
 // the layout of one instantiation: per CTA, A 128 rows and B BN / CG rows per stage (W8: plus the int8 weight rows)
 template <int BN, int STAGES, int EPI, int CG>
-using SmemOf = Smem<BN / CG, STAGES, EPI == EPI_W8 ? (BN / CG) * 64 : 0>;
+using SmemOf = Smem<BN / CG, STAGES, EPI == EPI_W8 ? (BN / CG) * 64 : 0,
+                    (epi_warps(EPI) > EPI_WARPS ? epi_warps(EPI) : EPI_WARPS)>;
 
 // ------------------------------------------------------------------ the kernel
 // CG = 1: one CTA per 128 x BN tile. CG = 2: a cluster of two CTAs (a CTA pair) per 256 x BN tile; CTA r loads A
@@ -1499,7 +1503,7 @@ cudaError_t launch_gemm_i8(const int8_t *A, const float *sa, const int8_t *B, co
   if (grouped) {
     GemmArgs a = base_args(sa, sb, bias, M, N, K, N, 128);
     a.Y = (bf16 *)Y;
-    return gelu ? run_tc<128, 6, 4, EPI_GROUP, true, 1>(A, B, a, st) : run_tc<128, 6, 4, EPI_GROUP, false, 1>(A, B, a, st);
+    return gelu ? run_tc<128, 5, 4, EPI_GROUP, true, 1>(A, B, a, st) : run_tc<128, 5, 4, EPI_GROUP, false, 1>(A, B, a, st);
   }
   const int ov = g_tile_override.load() == 64 ? 0 : g_tile_override.load();  // 64: a W8A16-only choice
   if (!ov && a8_rows(M, N, K)) {
