@@ -13,15 +13,16 @@
 //   EPI_SILU    weight rows [0, I) = gate, [I, 2I) = up; g, u = bf16 of the per-token epilogue;
 //               y[m, n] = bf16( bf16(silu(g)) * u ),  silu(g) = g / (1 + __expf(-g)) (IEEE quotient),  y is [M, I]
 //
-// B200 structure (one persistent CTA per SM, 320 threads, warp-specialised):
+// B200 structure (one persistent CTA per SM, 320 threads (grouped fold 576), warp-specialised):
 //   warp 0      TMA producer: 128 x 128-byte A tile and BN x 128-byte B tile per stage, 128-byte swizzle,
 //               OOB rows / K columns zero-filled by the copy engine (M, N and K tails need no code)
 //   warp 1      allocates TMEM and issues tcgen05.mma.kind::i8 (K = 32 per instruction) from one thread;
 //               tcgen05.commit releases a smem stage when its MMAs retire and hands a finished accumulator over
-//   warps 2-9   epilogue, two warps per TMEM lane quarter (one per half of the tile's columns): tcgen05.ld
-//               (32 lanes x 32 columns per load) -> fp32 math -> 32 x 32 bf16 blocks written to a per-warp shared
-//               buffer and stored by TMA (QOUT: int8 rows stored directly); each thread owns one output row, so
-//               per-row scales and the QOUT row-group maxima stay in registers
+//   warps 2-9   epilogue, two warps per TMEM lane quarter (one per half of the tile's columns; the grouped fold:
+//               warps 2-17, four per quarter, a quarter of the columns each): tcgen05.ld (32 lanes x 32 columns
+//               per load) -> fp32 math -> 32 x 32 bf16 blocks written to a per-warp shared buffer and stored by TMA
+//               (QOUT: int8 rows stored directly); each thread owns one output row, so per-row scales and the QOUT
+//               row-group maxima stay in registers
 //   W8A16       (EPI_W8, tcgen05.mma.kind::f16, 448 threads): the int8 weight rows arrive by TMA into a staging
 //               area and eight converter warps write them as bf16 into the swizzled B stage; four epilogue warps
 //               take all of the tile's columns
