@@ -796,37 +796,80 @@ __global__ void __launch_bounds__(cta_threads(EPI), 1)
 #pragma unroll
         for (int j = 0; j < CW; ++j) f[j] = 0.f;
         bool ok = true;
-        for (int g = 0; g < G; ++g) {
-          const float s = sq0;
-          sq0 = sq1;
-          sq1 = sq2;
-          sq2 = scale_next();
-          if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) {
-            ok = false;
-            break;
+        // f = fmaf((float)acc, s, f) per element, two at a time: the partial sums (|acc| < 2^22) become exact floats
+        // through the 1.5 * 2^23 mantissa trick (integer add, packed subtract), then one packed fused multiply-add:
+        // 2 instructions per element instead of 3, the same roundings
+        const float2 big2 = make_float2(12582912.f, 12582912.f);
+        auto fold = [&](const uint32_t(&r)[32], float s, int l) {
+          const float2 s2 = make_float2(s, s);
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 2) {
+            const float2 a = fsub2(make_float2(__int_as_float((int)r[jj] + (int)ACC_BIAS),
+                                               __int_as_float((int)r[jj + 1] + (int)ACC_BIAS)), big2);
+            const float2 q = ffma2(a, s2, make_float2(f[32 * l + jj], f[32 * l + jj + 1]));
+            f[32 * l + jj] = q.x;
+            f[32 * l + jj + 1] = q.y;
           }
-          tc_fence_after();
-          const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
-          uint32_t r[NLD][32];
-#pragma unroll
-          for (int l = 0; l < NLD; ++l) tmem_ld32(tb + 32 * l, r[l]);
-#pragma unroll
-          for (int l = 0; l < NLD; ++l) tmem_wait_tie(r[l]);
-          release_acc();
-          // f = fmaf((float)acc, s, f) per element, two at a time: the partial sums (|acc| < 2^22) become exact
-          // floats through the 1.5 * 2^23 mantissa trick (integer add, packed subtract), then one packed fused
-          // multiply-add: 2 instructions per element instead of 3, the same roundings
-          const float2 big2 = make_float2(12582912.f, 12582912.f), s2 = make_float2(s, s);
-#pragma unroll
-          for (int l = 0; l < NLD; ++l) {
-#pragma unroll
-            for (int jj = 0; jj < 32; jj += 2) {
-              const float2 a = fsub2(make_float2(__int_as_float((int)r[l][jj] + (int)ACC_BIAS),
-                                                 __int_as_float((int)r[l][jj + 1] + (int)ACC_BIAS)), big2);
-              const float2 q = ffma2(a, s2, make_float2(f[32 * l + jj], f[32 * l + jj + 1]));
-              f[32 * l + jj] = q.x;
-              f[32 * l + jj + 1] = q.y;
+        };
+        if constexpr (NLD == 1) {
+          // 32 columns per warp: two K groups per handshake. Waiting for the later group's commit covers the earlier
+          // group's MMAs too (a commit tracks every MMA issued before it); both accumulators are read, released and
+          // folded in group order. The accumulator barriers of skipped waits are at most one phase ahead (the MMA
+          // refills an accumulator only after its release), so the parity bookkeeping holds.
+          for (int g = 0; g < G; g += 2) {
+            const bool two = g + 1 < G;
+            const float sa = sq0, sb = sq1;
+            if (two) {
+              sq0 = sq2;
+              sq1 = scale_next();
+              sq2 = scale_next();
+            } else {
+              sq0 = sq1;
+              sq1 = sq2;
+              sq2 = scale_next();
             }
+            const int acc_b = acc + 1 == NACC ? 0 : acc + 1;
+            const uint32_t ph_b = acc + 1 == NACC ? (aphase ^ 1u) : aphase;
+            if (!warp_wait(bar_tfull(two ? acc_b : acc), two ? ph_b : aphase, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            {
+              uint32_t r[32];  // one accumulator's columns at a time (registers)
+              tmem_ld32(tmem_base + lane_addr + acc * BN + half * CW, r);
+              tmem_wait_tie(r);
+              release_acc();
+              fold(r, sa, 0);
+            }
+            if (two) {
+              uint32_t r[32];
+              tmem_ld32(tmem_base + lane_addr + acc * BN + half * CW, r);  // release_acc advanced acc to acc_b
+              tmem_wait_tie(r);
+              release_acc();
+              fold(r, sb, 0);
+            }
+          }
+        } else {
+          for (int g = 0; g < G; ++g) {
+            const float s = sq0;
+            sq0 = sq1;
+            sq1 = sq2;
+            sq2 = scale_next();
+            if (!warp_wait(bar_tfull(acc), aphase, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t tb = tmem_base + lane_addr + acc * BN + half * CW;
+            uint32_t r[NLD][32];
+#pragma unroll
+            for (int l = 0; l < NLD; ++l) tmem_ld32(tb + 32 * l, r[l]);
+#pragma unroll
+            for (int l = 0; l < NLD; ++l) tmem_wait_tie(r[l]);
+            release_acc();
+#pragma unroll
+            for (int l = 0; l < NLD; ++l) fold(r[l], s, l);
           }
         }
         if (!ok) break;
