@@ -174,6 +174,16 @@ int lfm2q_add_rmsnorm(uint16_t *h, const uint16_t *y, const uint16_t *w, uint16_
  * y [B, H] = bf16(C * bf16(w . (s1, s2, bf16(B x)) + bias)). */
 int lfm2q_shortconv_step(const uint16_t *bcx, uint16_t *state, const uint16_t *w, const uint16_t *bias, uint16_t *y,
                          int B, int H, void *stream);
+/* No counterpart in the reference: the embedding lookup (F.embedding) and the first add_rmsnorm (no residual) of its
+ * decode step (src/lfm2opt/runtime.py:249-251) in one launch. h [rows, H] = embed[tok[r]] (bf16 [V, H], bits
+ * unchanged), x = rmsnorm(h) * w as lfm2q_add_rmsnorm with y NULL. tok: int64 [rows] on the device. H <= 8192. */
+int lfm2q_embed_rmsnorm(const int64_t *tok, const uint16_t *embed, const uint16_t *w, uint16_t *h, uint16_t *x,
+                        int rows, int H, float eps, void *stream);
+/* No counterpart in the reference: the end of its decode step (src/lfm2opt/runtime.py:286-294: torch.argmax over the
+ * logits, the token copied into the next input, the position advanced) in one launch. tok[b] = the first index of
+ * the largest value of logits row b (bf16 [B, V]; NaN counts as the largest, as torch.argmax), then pos[0] += 1 if pos
+ * is not NULL. logits 16-byte aligned; V a multiple of 8 when B > 1. */
+int lfm2q_argmax_next(const uint16_t *logits, int64_t *tok, int64_t *pos, int B, int V, void *stream);
 /* qk_norm_rope_kv: qkv [B, (NQ + 2 NKV) * 64] (q | k | v heads, head dim 64), qw / kw [64] per-head RMSNorm weights,
  * rope cos / sin = bf16(cos / sin(pos * inv_freq[d % 32]) * scaling); q_out [B, NQ, 64]; k and v written to
  * kc / vc [B, NKV, max_len, 64] at position pos (the caller keeps pos < max_len). */

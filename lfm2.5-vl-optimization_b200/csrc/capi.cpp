@@ -327,6 +327,26 @@ int lfm2q_add_rmsnorm(uint16_t *h, const uint16_t *y, const uint16_t *w, uint16_
   return launched(launch_add_rmsnorm(h, y, w, x, rows, H, eps, g_pdl.load(), (cudaStream_t)stream), "add_rmsnorm");
 }
 
+int lfm2q_embed_rmsnorm(const int64_t *tok, const uint16_t *embed, const uint16_t *w, uint16_t *h, uint16_t *x,
+                        int rows, int H, float eps, void *stream) {
+  REQUIRE(rows >= 0 && H > 0 && H <= 8192, "embed [V, H], h / x [rows, H]: need rows >= 0 and 0 < H <= 8192");
+  if (rows == 0) return LFM2Q_OK;
+  REQUIRE(tok && embed && w && h && x, "tok, embed, w, h and x must be non-null");
+  if (int e = device_gate()) return e;
+  return launched(launch_embed_rmsnorm(tok, embed, w, h, x, rows, H, eps, g_pdl.load(), (cudaStream_t)stream),
+                  "embed_rmsnorm");
+}
+
+int lfm2q_argmax_next(const uint16_t *logits, int64_t *tok, int64_t *pos, int B, int V, void *stream) {
+  REQUIRE(B >= 0 && B <= 65535 && V > 0, "logits [B, V]: need 0 <= B <= 65535 and V > 0");
+  if (B == 0) return LFM2Q_OK;
+  REQUIRE(logits && tok, "logits and tok must be non-null");
+  REQUIRE(aligned16(logits) && (V % 8 == 0 || B == 1),
+          "logits must be 16-byte aligned, and V a multiple of 8 when B > 1 (every row 16-byte aligned)");
+  if (int e = device_gate()) return e;
+  return launched(launch_argmax_next(logits, tok, pos, B, V, g_pdl.load(), (cudaStream_t)stream), "argmax_next");
+}
+
 int lfm2q_shortconv_step(const uint16_t *bcx, uint16_t *state, const uint16_t *w, const uint16_t *bias, uint16_t *y,
                          int B, int H, void *stream) {
   REQUIRE(B >= 0 && H > 0, "bcx [B, 3H], state [B, H, 3], w [H, 3], y [B, H]: need B >= 0, H > 0");

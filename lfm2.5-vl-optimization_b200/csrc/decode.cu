@@ -36,10 +36,13 @@ __device__ __forceinline__ float ldg_bf(const bf16 *p) {
 constexpr int NT = 256;
 constexpr int NORM_MAX_PER_THREAD = 32;
 
-template <bool ADD>
+// GATHER (embed_rmsnorm): the row is read from embed[tok[row]] instead of h and copied into h (bits unchanged), the
+// reference step's embedding lookup and first norm in one launch.
+template <bool ADD, bool GATHER = false>
 __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(bf16 *__restrict__ h, const bf16 *__restrict__ y,
                                                          const bf16 *__restrict__ w, bf16 *__restrict__ x, int H,
-                                                         float eps) {
+                                                         float eps, const bf16 *__restrict__ embed,
+                                                         const int64_t *__restrict__ tok) {
   __shared__ float red[NT / 32];
   const int t = threadIdx.x, lane = t & 31, wp = t >> 5;
   const size_t off = (size_t)blockIdx.x * H;
@@ -50,12 +53,14 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(bf16 *__restrict__ h, c
     if (t + NT * k < H) wv[k] = ldg_bf(w + t + NT * k);
   pdl_trigger();
   pdl_wait();
+  const bf16 *src = h + off;
+  if (GATHER) src = embed + (size_t)__ldcg(reinterpret_cast<const long long *>(tok) + blockIdx.x) * H;
   // every load of the row first (all in flight together), then the arithmetic and the stores of h
 #pragma unroll
   for (int k = 0; k < NORM_MAX_PER_THREAD; ++k) {
     const int i = t + NT * k;
     if (i < H) {
-      hv[k] = ldcg_bf(h + off + i);
+      hv[k] = GATHER ? ldg_bf(src + i) : ldcg_bf(src + i);
       if (ADD) yv[k] = ldcg_bf(y + off + i);
     }
   }
@@ -68,6 +73,8 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(bf16 *__restrict__ h, c
       if (ADD) {
         v = rbf(v + yv[k]);
         h[off + i] = f2bf(v);
+      } else if (GATHER) {
+        h[off + i] = f2bf(v);  // the embedding row, bits unchanged
       }
       hv[k] = v;
       ss += v * v;
@@ -153,6 +160,81 @@ __global__ void __launch_bounds__(32 * QK_WARPS) qk_norm_rope_kv_kernel(
   dst[lane + 32] = o1;
 }
 
+// ------------------------------------------------------------------ argmax_next
+// One block of AM = 1024 threads per sequence: tok[b] = the first index of the largest logit of row b (NaN counts as
+// the largest, as torch.argmax), then pos[0] += 1 by block 0 (the reference step's argmax, token copy and position
+// increment, src/lfm2opt/runtime.py:286-294, in one launch). Each thread scans 16-byte chunks c = tid, tid + 1024, ...
+// in order, keeping the first maximum it meets; (value, index) pairs then meet in a warp butterfly and across warps,
+// larger value first, smaller index on ties.
+constexpr int AM = 1024;
+__device__ __forceinline__ bool am_better(float a, int ia, float b, int ib) {
+  const bool na = a != a, nb = b != b;
+  if (na || nb) return na && (!nb || ia < ib);
+  return a > b || (a == b && ia < ib);
+}
+__global__ void __launch_bounds__(AM) argmax_next_kernel(const bf16 *__restrict__ logits, int V,
+                                                         int64_t *__restrict__ tok, int64_t *__restrict__ pos) {
+  __shared__ float sv[AM / 32];
+  __shared__ int si[AM / 32];
+  pdl_trigger();
+  pdl_wait();
+  const bf16 *row = logits + (size_t)blockIdx.x * V;
+  const int t = threadIdx.x, lane = t & 31, wp = t >> 5;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const int chunks = V / 8;
+  for (int c = t; c < chunks; c += AM) {
+    const uint4 u = ld_cg16(reinterpret_cast<const uint4 *>(row) + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = (e & 1) ? bf_hi(w[e >> 1]) : bf_lo(w[e >> 1]);
+      if (am_better(v, 8 * c + e, best, bi)) {
+        best = v;
+        bi = 8 * c + e;
+      }
+    }
+  }
+  for (int i = chunks * 8 + t; i < V; i += AM) {  // tail of a row whose length is not a multiple of 8
+    const float v = ldcg_bf(row + i);
+    if (am_better(v, i, best, bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (am_better(v2, i2, best, bi)) {
+      best = v2;
+      bi = i2;
+    }
+  }
+  if (lane == 0) {
+    sv[wp] = best;
+    si[wp] = bi;
+  }
+  __syncthreads();
+  if (wp == 0) {
+    best = sv[lane];
+    bi = si[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (am_better(v2, i2, best, bi)) {
+        best = v2;
+        bi = i2;
+      }
+    }
+    if (lane == 0) {
+      tok[blockIdx.x] = bi;
+      if (pos && blockIdx.x == 0) pos[0] = __ldcg(reinterpret_cast<const long long *>(pos)) + 1;
+    }
+  }
+}
+
 cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, bool pdl, cudaStream_t st, cudaLaunchAttribute *attr) {
   cudaLaunchConfig_t cfg = {};
   attr->id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -174,9 +256,26 @@ cudaError_t launch_add_rmsnorm(void *h, const void *y, const void *w, void *x, i
   const cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(NT), pdl, st, &attr);
   if (y)
     return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<true>, (bf16 *)h, (const bf16 *)y, (const bf16 *)w, (bf16 *)x,
-                              H, eps);
+                              H, eps, (const bf16 *)nullptr, (const int64_t *)nullptr);
   return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<false>, (bf16 *)h, (const bf16 *)nullptr, (const bf16 *)w,
-                            (bf16 *)x, H, eps);
+                            (bf16 *)x, H, eps, (const bf16 *)nullptr, (const int64_t *)nullptr);
+}
+
+cudaError_t launch_embed_rmsnorm(const int64_t *tok, const void *embed, const void *w, void *h, void *x, int rows,
+                                 int H, float eps, bool pdl, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  cudaLaunchAttribute attr;
+  const cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(NT), pdl, st, &attr);
+  return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<false, true>, (bf16 *)h, (const bf16 *)nullptr, (const bf16 *)w,
+                            (bf16 *)x, H, eps, (const bf16 *)embed, tok);
+}
+
+cudaError_t launch_argmax_next(const void *logits, int64_t *tok, int64_t *pos, int B, int V, bool pdl,
+                               cudaStream_t st) {
+  if (B <= 0) return cudaSuccess;
+  cudaLaunchAttribute attr;
+  const cudaLaunchConfig_t cfg = pdl_cfg(dim3(B), dim3(AM), pdl, st, &attr);
+  return cudaLaunchKernelEx(&cfg, argmax_next_kernel, (const bf16 *)logits, V, tok, pos);
 }
 
 cudaError_t launch_shortconv_step(const void *bcx, void *state, const void *w, const void *bias, void *y, int B, int H,

@@ -91,6 +91,10 @@ cudaError_t launch_add_rmsnorm(void *h, const void *y, const void *w, void *x, i
                                cudaStream_t st);
 cudaError_t launch_shortconv_step(const void *bcx, void *state, const void *w, const void *bias, void *y, int B, int H,
                                   bool pdl, cudaStream_t st);
+cudaError_t launch_embed_rmsnorm(const int64_t *tok, const void *embed, const void *w, void *h, void *x, int rows,
+                                 int H, float eps, bool pdl, cudaStream_t st);
+cudaError_t launch_argmax_next(const void *logits, int64_t *tok, int64_t *pos, int B, int V, bool pdl,
+                               cudaStream_t st);
 cudaError_t launch_qk_norm_rope_kv(const void *qkv, const void *qw, const void *kw, const float *inv_freq,
                                    float scaling, const int64_t *pos, void *q_out, void *kc, void *vc, int B, int NQ,
                                    int NKV, int max_len, float eps, bool pdl, cudaStream_t st);

@@ -44,6 +44,8 @@ SIGNATURES = {
     "lfm2q_gemv_w4": [_p, _p, _p, _p, _i, _i, _i, _i, _p],
     "lfm2q_add_rmsnorm": [_p, _p, _p, _p, _i, _i, _f, _p],
     "lfm2q_shortconv_step": [_p, _p, _p, _p, _p, _i, _i, _p],
+    "lfm2q_embed_rmsnorm": [_p, _p, _p, _p, _p, _i, _i, _f, _p],
+    "lfm2q_argmax_next": [_p, _p, _p, _i, _i, _p],
     "lfm2q_qk_norm_rope_kv": [_p, _p, _p, _p, _f, _p, _p, _p, _p, _i, _i, _i, _i, _f, _p],
     "lfm2q_decode_attention_split": [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p],
     "lfm2q_decode_attention_split_noalloc": [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p],

@@ -105,8 +105,12 @@ class DecodeStep:
     @torch.no_grad()
     def step(self):
         K, W, c = self.ops, self.w, self.cfg
-        self.h.copy_(F.embedding(self.tok, W.embed))
-        K.add_rmsnorm(self.h, None, W.norm[0], self.x, c.eps)
+        fused_ends = hasattr(K, "embed_rmsnorm") and hasattr(K, "argmax_next")  # lfm2q's backend
+        if fused_ends:  # embedding lookup + first norm in one launch
+            K.embed_rmsnorm(self.tok, W.embed, W.norm[0], self.h, self.x, c.eps)
+        else:
+            self.h.copy_(F.embedding(self.tok, W.embed))
+            K.add_rmsnorm(self.h, None, W.norm[0], self.x, c.eps)
         for i, L in enumerate(W.layer):
             if i in c.attn_layers:
                 K.gemv(L["qkv"][0], L["qkv"][1], self.x, self.qkv)
@@ -123,8 +127,11 @@ class DecodeStep:
             K.gemv(L["w2"][0], L["w2"][1], self.act, self.y)
             K.add_rmsnorm(self.h, self.y, W.norm[i + 1], self.x, c.eps)
         K.gemv(W.head[0], W.head[1], self.x, self.logits)
-        self.tok.copy_(torch.argmax(self.logits, dim=-1))
-        self.pos.add_(1)
+        if fused_ends:  # argmax, next token and position advance in one launch
+            K.argmax_next(self.logits, self.tok, self.pos)
+        else:
+            self.tok.copy_(torch.argmax(self.logits, dim=-1))
+            self.pos.add_(1)
 
     def capture(self):
         """Capture one step into a CUDA graph (after one eager warm-up step on a side stream, which advances the

@@ -331,6 +331,33 @@ class DecodeGemvExt:
             _capi.call("lfm2q_add_rmsnorm", h.data_ptr(), _ptr(y), w.data_ptr(), x.data_ptr(), rows, H, float(eps),
                        _stream(h))
 
+    def embed_rmsnorm(self, tok, embed, w, h, x, eps):
+        """h = embed[tok] (bits unchanged), x = w * rmsnorm(h): F.embedding + add_rmsnorm(h, None, w, x, eps) in one
+        launch (no counterpart in the reference). tok int64 [rows] on the device, embed bf16 [V, H]."""
+        for t, n in ((embed, "embed"), (w, "w"), (h, "h"), (x, "x")):
+            if not (t.is_cuda and t.dtype == _BF and t.is_contiguous()):
+                raise RuntimeError(f"{n} must be contiguous CUDA bf16")
+        _req(tok.is_cuda and tok.dtype == torch.int64 and tok.is_contiguous(), "tok: contiguous CUDA int64")
+        H = embed.size(1)
+        rows = tok.numel()
+        _req(h.numel() == rows * H and x.numel() == rows * H and w.numel() == H, "h, x [rows, H], w [H]")
+        with _DeviceOf(h):
+            _capi.call("lfm2q_embed_rmsnorm", tok.data_ptr(), embed.data_ptr(), w.data_ptr(), h.data_ptr(),
+                       x.data_ptr(), rows, H, float(eps), _stream(h))
+
+    def argmax_next(self, logits, tok, pos=None):
+        """tok[b] = argmax(logits[b]) (first index of the maximum, NaN largest, as torch.argmax), then pos += 1:
+        the end of a decode step in one launch (no counterpart in the reference)."""
+        if not (logits.is_cuda and logits.dtype == _BF and logits.is_contiguous()):
+            raise RuntimeError("logits must be contiguous CUDA bf16")
+        _req(tok.is_cuda and tok.dtype == torch.int64 and tok.is_contiguous(), "tok: contiguous CUDA int64")
+        _req(pos is None or (pos.is_cuda and pos.dtype == torch.int64), "pos: CUDA int64 [1]")
+        B = tok.numel()
+        V = logits.numel() // max(B, 1)
+        _req(logits.numel() == B * V, "logits [B, V]")
+        with _DeviceOf(logits):
+            _capi.call("lfm2q_argmax_next", logits.data_ptr(), tok.data_ptr(), _ptr(pos), B, V, _stream(logits))
+
     def shortconv_step(self, bcx, state, w, bias, y):
         """One short-convolution decode step (the reference's shortconv_step binding,
         kernels/lfm2_decode.cpp:39-45): bcx [B, 3H], state [B, H, 3] updated in place, w [H, 3], bias [H] or None,

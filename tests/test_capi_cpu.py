@@ -66,6 +66,9 @@ def test_validation_runs_before_the_device():
     assert b"ws [B, NQ, S, 66]" in _capi.lib().lfm2q_last_error()
     assert _st(att, fake + 8, fake, fake, fake, fake, fake, 2, 32, 8, 3072, 16, 0.125, None) == _capi.EINVAL
     assert b"aligned" in _capi.lib().lfm2q_last_error()
+    assert _st("lfm2q_argmax_next", fake, fake, None, 2, 1001, None) == _capi.EINVAL  # rows not 16-byte aligned
+    assert b"multiple of 8" in _capi.lib().lfm2q_last_error()
+    assert _st("lfm2q_embed_rmsnorm", fake, fake, fake, fake, fake, 1, 16384, 1e-5, None) == _capi.EINVAL
     na = "lfm2q_decode_attention_split_noalloc"
     assert _st(na, fake, fake, fake, fake, fake, 64, 32, 8, 3072, 16, 0.125, None) == _capi.EINVAL  # 8.65 M floats
     assert b"static workspace" in _capi.lib().lfm2q_last_error()

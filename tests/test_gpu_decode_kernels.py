@@ -125,3 +125,40 @@ def test_qk_norm_rope_kv(cuda_dev, B, NQ, NKV, max_len, pos, scaling):
                                   ptr(vr), B, NQ, NKV, max_len, EPS, st()) == 0
     torch.cuda.synchronize()
     assert torch.equal(qo, qr) and torch.equal(kc, kr) and torch.equal(vc, vr)
+
+
+@pytest.mark.parametrize("B,V", [(1, 65536), (3, 65536), (1, 1001), (2, 8), (4, 4096)])
+def test_argmax_next_equals_torch_argmax(cuda_dev, B, V):
+    g = gen(B * 7 + V)
+    logits = torch.randn(B, V, generator=g).to(BF)
+    logits[0, V // 3] = 50.0  # ties: the first index wins
+    logits[0, V // 2] = 50.0
+    if B > 1:
+        logits[1, V - 1] = float("nan")  # NaN counts as the largest, as in torch.argmax
+        logits[1, 0] = float("nan")
+    ld = logits.to(cuda_dev)
+    tok = torch.full((B,), -1, device=cuda_dev, dtype=torch.int64)
+    pos = torch.tensor([41], device=cuda_dev)
+    ext().argmax_next(ld, tok, pos)
+    torch.cuda.synchronize()
+    assert torch.equal(tok.cpu(), torch.argmax(logits.float(), dim=-1))
+    assert int(pos) == 42
+    ext().argmax_next(ld, tok)  # no position to advance
+    torch.cuda.synchronize()
+    assert int(pos) == 42
+
+
+@pytest.mark.parametrize("rows,H", [(1, 2048), (3, 2048), (2, 1000)])
+def test_embed_rmsnorm_equals_embedding_then_add_rmsnorm(cuda_dev, rows, H):
+    g = gen(rows + H)
+    embed = torch.randn(300, H, generator=g).to(BF).to(cuda_dev)
+    w = (torch.rand(H, generator=g) + 0.5).to(BF).to(cuda_dev)
+    tok = torch.tensor([5, 299, 0][:rows], device=cuda_dev)
+    h, x = torch.empty(rows, H, device=cuda_dev, dtype=BF), torch.empty(rows, H, device=cuda_dev, dtype=BF)
+    ext().embed_rmsnorm(tok, embed, w, h, x, EPS)
+    h_ref = embed[tok].clone()
+    x_ref = torch.empty_like(x)
+    L = refk()
+    assert L.refk_add_rmsnorm(ptr(h_ref), None, ptr(w), ptr(x_ref), rows, H, EPS, st()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(h, embed[tok]) and torch.equal(x, x_ref)
