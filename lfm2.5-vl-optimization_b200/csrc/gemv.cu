@@ -529,6 +529,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_xs_kernel(const int8_t *_
 
 constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
 constexpr int XS_RING = 6;  // ring depth of the x-sliced kernels (K steps of 1 KB per warp)
+constexpr int EPI_RING = 5;  // ... of the SwiGLU epilogue GEMV
 constexpr int GV_X_SMEM_MAX = 64 * 1024;  // fused-quantization A8 GEMV: B * (K + 64) bytes of int8 tokens
 std::atomic<bool> g_early_trigger{false};
 // 0 (default): deep-prefetch x-sliced kernel for 1-2 tokens, ring x-sliced kernel for 3-4 tokens from 8 M weights,
@@ -654,12 +655,13 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
   if (sizeof(WT) == 1 && g_gemv_impl != 1 && 3 * (size_t)(K + 64) <= (size_t)GV_X_SMEM_MAX && K % 256 == 0 &&
       K <= xs_max_k(1)) {
     const int8_t *Wi = reinterpret_cast<const int8_t *>(W);
-    const size_t dyn = (size_t)8 * XS_RING * 1024 + 3 * (size_t)(K + 64);
+    // SwiGLU (w1|w3): 5-deep rings, so four blocks fit per SM (smem) and the 512 blocks of an 8192-wide layer run
+    // in one wave (6-deep: three blocks per SM, two waves)
     if (epi == 0)
-      return launch_dyn(gemv_epi_xs_kernel<2, 0, XS_RING>, grid, GV_THREADS, pdl, st, dyn, Wi, scale, x, y, S, K, state,
-                        cw, cbias, p);
-    return launch_dyn(gemv_epi_xs_kernel<3, 1, XS_RING>, grid, GV_THREADS, pdl, st, dyn, Wi, scale, x, y, S, K, state,
-                      cw, cbias, p);
+      return launch_dyn(gemv_epi_xs_kernel<2, 0, EPI_RING>, grid, GV_THREADS, pdl, st,
+                        (size_t)8 * EPI_RING * 1024 + 3 * (size_t)(K + 64), Wi, scale, x, y, S, K, state, cw, cbias, p);
+    return launch_dyn(gemv_epi_xs_kernel<3, 1, XS_RING>, grid, GV_THREADS, pdl, st,
+                      (size_t)8 * XS_RING * 1024 + 3 * (size_t)(K + 64), Wi, scale, x, y, S, K, state, cw, cbias, p);
   }
   if (epi == 0)
     return launch_ex(gemv_epi_kernel<WT, 2, 0>, grid, GV_THREADS, pdl, st, 0, W, scale, x, y, S, K, state, cw, cbias, p);
