@@ -530,6 +530,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_epi_xs_kernel(const int8_t *_
 constexpr int GV_DYN_SMEM = 8 * GV_RING * 1024;
 constexpr int XS_RING = 6;  // ring depth of the x-sliced kernels (K steps of 1 KB per warp)
 constexpr int EPI_RING = 5;  // ... of the SwiGLU epilogue GEMV
+constexpr int CONV_RING = 10;  // ... of the short-conv epilogue GEMV
 constexpr int GV_X_SMEM_MAX = 64 * 1024;  // fused-quantization A8 GEMV: B * (K + 64) bytes of int8 tokens
 std::atomic<bool> g_early_trigger{false};
 // 0 (default): deep-prefetch x-sliced kernel for 1-2 tokens, ring x-sliced kernel for 3-4 tokens from 8 M weights,
@@ -660,6 +661,12 @@ cudaError_t gemv_epi_dispatch(int epi, const WT *W, const float *scale, const bf
     if (epi == 0)
       return launch_dyn(gemv_epi_xs_kernel<2, 0, EPI_RING>, grid, GV_THREADS, pdl, st,
                         (size_t)8 * EPI_RING * 1024 + 3 * (size_t)(K + 64), Wi, scale, x, y, S, K, state, cw, cbias, p);
+    // short conv (in_proj, 16 outputs x 3 parts per block): ~one block per SM at the model's 2048 channels, so a
+    // deeper ring keeps more of each block's weights in flight (where it fits the kernel's shared-memory limit)
+    const size_t dconv = (size_t)8 * CONV_RING * 1024 + 3 * (size_t)(K + 64);
+    if (dconv <= (size_t)(GV_DYN_SMEM + GV_X_SMEM_MAX))
+      return launch_dyn(gemv_epi_xs_kernel<3, 1, CONV_RING>, grid, GV_THREADS, pdl, st, dconv, Wi, scale, x, y, S, K,
+                        state, cw, cbias, p);
     return launch_dyn(gemv_epi_xs_kernel<3, 1, XS_RING>, grid, GV_THREADS, pdl, st,
                       (size_t)8 * XS_RING * 1024 + 3 * (size_t)(K + 64), Wi, scale, x, y, S, K, state, cw, cbias, p);
   }
