@@ -301,9 +301,10 @@ __global__ void __launch_bounds__(AT_THREADS) attn_split_kernel(const bf16 *__re
 }
 
 // One block of 64 threads per (b, q head): the merge of the S partials, in split order, as the reference's combine
-// (kernels/lfm2_decode.cu:389-416). M = max_s m_s is exact in any order (a max rounds nothing), so it is a block
-// reduction; the sums then run in split order from partials staged in shared memory AT_CMB_SPLITS at a time (all the
-// loads of a chunk in flight at once instead of one dependent L2 round trip per split).
+// (kernels/lfm2_decode.cu:389-416). M = max_s m_s is exact in any order (a max rounds nothing); the sums run in split
+// order from partials staged in shared memory (all the loads of a chunk in flight at once instead of one dependent L2
+// round trip per split). Up to AT_CMB_SPLITS splits everything is staged at once and M is read from shared memory:
+// one round trip in all; beyond, M is a block reduction over the m values first, then chunk by chunk.
 constexpr int AT_CMB_SPLITS = 64;
 __global__ void __launch_bounds__(AT_D) attn_combine_kernel(const float *__restrict__ ws, bf16 *__restrict__ out, int S,
                                                             int pdl) {
@@ -315,13 +316,27 @@ __global__ void __launch_bounds__(AT_D) attn_combine_kernel(const float *__restr
   }
   const int bh = blockIdx.x, d = threadIdx.x;
   const float *w = ws + (size_t)bh * S * (AT_D + 2);
-  float M = -INFINITY;
+  float M = -INFINITY, L = 0.f, o = 0.f;
+  if (S <= AT_CMB_SPLITS) {
+    // every partial in one round trip, M from shared memory (a max is exact in any order), then the sums
+    for (int i = d; i < S * (AT_D + 2); i += AT_D) part[i] = __ldcg(w + i);
+    __syncthreads();
+    for (int s = 0; s < S; ++s) M = fmaxf(M, part[s * (AT_D + 2)]);
+    for (int s = 0; s < S; ++s) {
+      const float ls = part[s * (AT_D + 2) + 1];
+      if (ls == 0.f) continue;
+      const float c = __expf(part[s * (AT_D + 2)] - M);
+      L += ls * c;
+      o += part[s * (AT_D + 2) + 2 + d] * c;
+    }
+    out[(size_t)bh * AT_D + d] = f2bf(o / L);
+    return;
+  }
   for (int s = d; s < S; s += AT_D) M = fmaxf(M, __ldcg(w + (size_t)s * (AT_D + 2)));
   M = warp_max(M);
   if ((d & 31) == 0) wmax[d >> 5] = M;
   __syncthreads();
   M = fmaxf(wmax[0], wmax[1]);
-  float L = 0.f, o = 0.f;
   for (int c0 = 0; c0 < S; c0 += AT_CMB_SPLITS) {
     const int n = min(AT_CMB_SPLITS, S - c0);
     const float *wc = w + (size_t)c0 * (AT_D + 2);

@@ -24,7 +24,8 @@ REF_LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "librefk.so"
 
 # (B, NKV, max_len, pos, S)
 CASES = [(2, 8, 3072, 2300, 16), (2, 8, 3072, 2300, 4), (2, 8, 3072, 0, 16), (1, 2, 300, 299, 3),
-         (3, 1, 129, 128, 2), (1, 8, 8192, 8191, 32), (4, 8, 1024, 63, 8), (1, 1, 64, 10, 64), (2, 4, 200, 130, 1)]
+         (3, 1, 129, 128, 2), (1, 8, 8192, 8191, 32), (4, 8, 1024, 63, 8), (1, 1, 64, 10, 64), (2, 4, 200, 130, 1),
+         (1, 2, 256, 200, 80)]  # the last: more splits than the combine stages at once
 
 
 def make(B, NKV, max_len, seed, dev):
