@@ -176,7 +176,8 @@ int lfm2q_shortconv_step(const uint16_t *bcx, uint16_t *state, const uint16_t *w
                          int B, int H, void *stream);
 /* No counterpart in the reference: the embedding lookup (F.embedding) and the first add_rmsnorm (no residual) of its
  * decode step (src/lfm2opt/runtime.py:249-251) in one launch. h [rows, H] = embed[tok[r]] (bf16 [V, H], bits
- * unchanged), x = rmsnorm(h) * w as lfm2q_add_rmsnorm with y NULL. tok: int64 [rows] on the device. H <= 8192. */
+ * unchanged), x = rmsnorm(h) * w as lfm2q_add_rmsnorm with y NULL. tok: int64 [rows] on the device, each in [0, V)
+ * (not checked: the values are on the device). H <= 8192. */
 int lfm2q_embed_rmsnorm(const int64_t *tok, const uint16_t *embed, const uint16_t *w, uint16_t *h, uint16_t *x,
                         int rows, int H, float eps, void *stream);
 /* No counterpart in the reference: the end of its decode step (src/lfm2opt/runtime.py:286-294: torch.argmax over the
