@@ -97,9 +97,10 @@ int lfm2q_silu_mul_q(const uint16_t *g, int8_t *q, float *s, int rows, int I, in
  * Replaces launch_gemv (kernels/lfm2_decode.cu:708-714) behind gemv (kernels/lfm2_decode.cpp:73-85).
  * y bf16 [B, N] = bf16((x . W^T) * scale[n]), fp32 accumulation. w_is_int8 != 0: W int8 [N, K] with scale fp32
  * [N] (required); else W bf16 [N, K] and scale optional (NULL = 1). x bf16 [B, K]. Needs K % 512 == 0 (int8) or
- * K % 256 == 0 (bf16). `rows` selects the kernel: 0 = automatic (int8 weights: the persistent kernel that streams
- * W with bulk copies); 1, 2, 4 or 8 = the register-streaming kernel with that many K-slices per 16-row group.
- * Results agree to fp32 summation order. */
+ * K % 256 == 0 (bf16). Int8 weights with 1-4 tokens run the x-sliced tensor-core path (the tokens as exact fixed-point
+ * bytes, exact int32 partial sums; see lfm2q_set_gemv_path), else bf16 MMAs on the exactly converted weights.
+ * `rows` (the reference's kernel-choice argument): 0 = automatic; 1, 2, 4 or 8 forces that many K-slices per 16-row
+ * group on the ring and bf16 paths (the deep-prefetch kernel sizes its own). Results agree to fp32 summation order. */
 int lfm2q_gemv(const void *W, int w_is_int8, const float *scale, const uint16_t *x, uint16_t *y, int N, int K,
                int rows, int B, void *stream);
 
