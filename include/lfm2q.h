@@ -39,8 +39,9 @@ const char *lfm2q_version(void);
 int lfm2q_device_supported(void);
 
 /* Reads (and with clear != 0 resets) the sticky device error words that the tcgen05 GEMMs and the decode attention
- * set when one of their bounded pipeline waits gives up (no other kernel of this library waits on anything). Returns LFM2Q_OK or
- * LFM2Q_ETIMEOUT. Synchronous (copies one int from the device). Poll it after a batch of work whose outputs matter. */
+ * set when one of their bounded pipeline waits gives up (no other kernel of this library waits on anything).
+ * Returns LFM2Q_OK or LFM2Q_ETIMEOUT. Synchronous (copies two ints from the device). Poll it after a batch of work
+ * whose outputs matter. */
 int lfm2q_check_device(int clear);
 
 /* ------------------------------------------------------------------ activation quantizers
