@@ -7,7 +7,9 @@ What is executed from the reference (jainilbavishi24/LFM2.5-VL-Optimization, che
   * tests/test_int8_gemm.py         ref_quant, ref_quant_groups, bf16_ulps, test_quant_rows, test_quant_groups,
                                     test_i8, test_i8_grouped (function definitions taken from the file's AST)
   * tests/test_kernels.py           test_gemv (function definition from the AST; its shape list is swapped for
-                                    small shapes so the CPU run stays quick)
+                                    small shapes so the CPU run stays quick); rms, test_add_rmsnorm, test_shortconv,
+                                    test_qk_rope_kv, test_attention and the module's model constants (H, NQ, NKV, D,
+                                    EPS), test_attention at a small cache (B = 1, 512 slots, position 300)
 The test functions are executed with dev = "cpu" and with stand-ins for the CUDA extension calls; a `check`
 stand-in captures the reference tensors the test computes (its locals), which become the golden outputs.
 
@@ -53,6 +55,18 @@ def load_functions(path: Path, names, replace_lists=None):
     if missing:
         raise RuntimeError(f"functions {missing} not found in {path}")
     return out
+
+
+def load_assign(path: Path, name):
+    """The top-level assignment statement of `path` that binds `name` (e.g. a tuple of model constants)."""
+    tree = ast.parse(path.read_text())
+    for node in tree.body:
+        if isinstance(node, ast.Assign):
+            for t in node.targets:
+                names = [e.id for e in t.elts] if isinstance(t, ast.Tuple) else [getattr(t, "id", None)]
+                if name in names:
+                    return ast.Module(body=[node], type_ignores=[])
+    raise RuntimeError(f"no assignment of {name} in {path}")
 
 
 def run_in(ns, mod):
@@ -204,6 +218,43 @@ def main():
         n += 1
     np.savez_compressed(HERE / "gemv.npz", **gv)
     np.savez_compressed(HERE / "gemv_w4.npz", **g4)
+
+    # ---------------------------------------------------------------- decode-step kernels and attention
+    kpath = ref / "tests/test_kernels.py"
+    tk3 = load_functions(kpath, ["rms", "test_add_rmsnorm", "test_shortconv", "test_qk_rope_kv", "test_attention"])
+    cap3 = Capture()
+    ns3 = {"torch": torch, "F": F, "dev": "cpu", "bf": torch.bfloat16, "K": Stub(), "report": cap3}
+    run_in(ns3, load_assign(kpath, "EPS"))  # H, I, NQ, NKV, D, EPS as the reference's test defines them
+    for name in ("rms", "test_add_rmsnorm", "test_shortconv", "test_qk_rope_kv", "test_attention"):
+        run_in(ns3, tk3[name])
+    dk = {}
+    torch.manual_seed(5)
+    ns3["test_add_rmsnorm"]()
+    c_res, c_norm, c_noadd = cap3.cases[-3:]
+    dk["norm_h"], dk["norm_y"], dk["norm_w"] = t2np(c_res["h"]), t2np(c_res["y"]), t2np(c_res["w"])
+    dk["norm_ref_h"], dk["norm_ref_x"] = t2np(c_res["ref_h"]), t2np(c_norm["ref_x"])
+    dk["norm_ref_x_noadd"] = t2np(c_noadd["_args"][2])
+    torch.manual_seed(6)
+    ns3["test_shortconv"]()
+    c_out, c_state = cap3.cases[-2:]
+    dk["conv_bcx"], dk["conv_state"], dk["conv_w"] = t2np(c_out["bcx"]), t2np(c_out["state"]), t2np(c_out["w"])
+    dk["conv_ref_y"], dk["conv_ref_state"] = t2np(c_out["ref"]), t2np(c_state["st"])
+    torch.manual_seed(7)
+    ns3["test_qk_rope_kv"]()
+    c_q, c_k, c_v = cap3.cases[-4:-1]
+    dk["qk_qkv"], dk["qk_qw"], dk["qk_kw"] = t2np(c_q["qkv"]), t2np(c_q["qw"]), t2np(c_q["kw"])
+    dk["qk_inv_freq"], dk["qk_meta"] = t2np(c_q["inv_freq"]), np.array([c_q["B"], c_q["max_len"], c_q["pos"]])
+    dk["qk_ref_q"], dk["qk_ref_k"], dk["qk_ref_v"] = (t2np(c_q["_args"][2]), t2np(c_k["_args"][2]),
+                                                      t2np(c_v["_args"][2]))
+    np.savez_compressed(HERE / "decode_kernels.npz", **dk)
+    at = {}
+    torch.manual_seed(8)
+    ns3["test_attention"](B=1, max_len=512, pos=300)
+    c_full, c_one = cap3.cases[-5], cap3.cases[-2]
+    at["q"], at["kc"], at["vc"] = t2np(c_full["q"]), t2np(c_full["kc"]), t2np(c_full["vc"])
+    at["scale"], at["meta"] = np.array(c_full["scale"], np.float64), np.array([1, 512, 300])
+    at["ref"], at["ref_len1"] = t2np(c_full["ref"]), t2np(c_one["_args"][2])
+    np.savez_compressed(HERE / "attention.npz", **at)
     print("golden vectors written to", HERE)
 
 
